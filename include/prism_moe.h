@@ -1,0 +1,228 @@
+/*
+ * prism_moe.h - C ABI of the B200 (sm_100a) implementation of Prism's bottleneck
+ * transformer / MoE stack.
+ *
+ * The reference dispatches GLSL compute shaders through Vulkan with three storage
+ * buffers and an int32 push-constant block per pass:
+ *   binding 0  read-only fp16 weight blob      (prism_moe_bench.cpp:105-112)
+ *   binding 1  read/write fp16 feature arena   (split2_qkv_attn_d256.comp.glsl:18-19)
+ *   binding 2  int32 aux arena (router output) (moe_router.comp.glsl:19-22)
+ * Every offset in a push-constant block is an ELEMENT offset (fp16 elements for
+ * bindings 0/1, int32 elements for binding 2), and every weight matrix is row-major
+ * [out][in].  This header keeps that contract: the per-pass entry points take the
+ * same push-constant structs (same field names and order) plus raw DEVICE pointers
+ * for the three bindings and a cudaStream_t passed as void*.  Nothing in this file
+ * depends on torch or on CUDA headers.
+ *
+ * Two groups of entry points:
+ *  - per-pass drop-ins (prism_attn_window, prism_router, prism_expert, prism_proj_up,
+ *    prism_proj_down, prism_dense_block): one call per reference vkCmdDispatch, same
+ *    arithmetic, operating on the caller's arenas in place;
+ *  - the fast path (prism_stack_*): the whole stack of a prism_stack_desc over a
+ *    batch of frames, with weights repacked once into an aligned device arena and
+ *    the per-expert dispatch loop replaced by route -> grouped expert GEMM.
+ *
+ * All calls are stream-ordered on the caller's stream and never synchronise the
+ * host, except prism_stack_create (weight upload/repack) and prism_stack_status.
+ * Status codes are returned; prism_last_error_string() describes the last failure
+ * on the calling thread.
+ */
+#ifndef PRISM_MOE_H
+#define PRISM_MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PRISM_ABI_VERSION 1
+
+/* Status codes.  The reference ignores most VkResults and reports a failed
+ * pipeline load as VK_NULL_HANDLE (prism_moe_bench.cpp:22,30); this ABI validates
+ * every offset and size on the host and returns one of these instead. */
+enum prism_status {
+    PRISM_OK = 0,
+    PRISM_E_ARG = 1,         /* null pointer, bad enum, inconsistent sizes        */
+    PRISM_E_ALIGN = 2,       /* pointer/offset alignment the path requires        */
+    PRISM_E_RANGE = 3,       /* offset or size outside the buffer / limit         */
+    PRISM_E_CUDA = 4,        /* a CUDA runtime/driver call failed                 */
+    PRISM_E_TIMEOUT = 5,     /* a bounded device-side wait gave up                */
+    PRISM_E_NOMEM = 6,       /* device allocation failed                          */
+    PRISM_E_UNSUPPORTED = 7  /* shape the kernels do not implement (e.g. dim 192) */
+};
+
+/* ---- push-constant blocks (field order = the GLSL declaration order) ---------- */
+
+/* split2_qkv_attn_d256.comp.glsl:11-16 */
+typedef struct prism_attn_params {
+    int32_t n_tokens, dim, n_heads, head_dim;
+    int32_t spatial_w, spatial_h, window_size;
+    int32_t qkv_w, qkv_b, out_w, out_b;
+    int32_t input_offset, output_offset;
+} prism_attn_params;
+
+/* moe_router.comp.glsl:11-17 */
+typedef struct prism_router_params {
+    int32_t n_tokens, dim, n_experts;
+    int32_t router_w, router_b;
+    int32_t input_offset;
+    int32_t assignment_offset;
+    int32_t count_offset;
+} prism_router_params;
+
+/* moe_expert_skip.comp.glsl:13-19 */
+typedef struct prism_expert_params {
+    int32_t n_tokens, dim;
+    int32_t expert_id;
+    int32_t w1_offset, b1_offset, w2_offset, b2_offset;
+    int32_t input_offset, output_offset;
+    int32_t assignment_offset;
+} prism_expert_params;
+
+/* pw_project_128to256.comp.glsl:11-15 and pw_project_256to128.comp.glsl:11-15 */
+typedef struct prism_proj_params {
+    int32_t n_tokens;
+    int32_t w_offset, b_offset;
+    int32_t input_offset, output_offset;
+} prism_proj_params;
+
+/* TransformerPush, prism_scaling_bench.cpp:60-68 (attention_windowed*.comp.glsl) */
+typedef struct prism_dense_params {
+    int32_t n_tokens, dim, n_heads, head_dim;
+    int32_t spatial_w, spatial_h, window_size;
+    int32_t qkv_w_offset, qkv_b_offset;
+    int32_t out_w_offset, out_b_offset;
+    int32_t ffn_w1_offset, ffn_b1_offset;
+    int32_t ffn_w2_offset, ffn_b2_offset;
+    int32_t input_offset, output_offset;
+} prism_dense_params;
+
+/* ---- context --------------------------------------------------------------- */
+
+typedef struct prism_ctx prism_ctx;
+
+/* Replaces the Vulkan instance/device setup of prism_moe_bench.cpp:55-88 and
+ * prism::PrismVulkan::Init (prism_vulkan.h:76).  One context per CUDA device;
+ * contexts are independent, one context must not be used from two host threads
+ * at the same time. */
+int prism_create(int device, prism_ctx** out);
+int prism_destroy(prism_ctx* ctx);
+
+/* Text of the last error on the calling host thread ("" if none). */
+const char* prism_last_error_string(void);
+int prism_abi_version(void);
+
+/* ---- per-pass drop-ins (one call = one reference vkCmdDispatch) -------------
+ * weights: device pointer to the fp16 blob (binding 0), weight_elems its length
+ * features: device pointer to the fp16 arena (binding 1), feature_elems its length
+ * aux: device pointer to the int32 arena (binding 2), aux_elems its length
+ * stream: cudaStream_t (NULL = legacy default stream)
+ * Offsets in the params are bounds-checked against these lengths. */
+
+/* Replaces vkCmdDispatch(split2_qkv_attn_d256, ceil(W/ws)*ceil(H/ws)) at
+ * prism_moe_bench.cpp:417-421: out = x + Wo*MHA_window(x) + bo.  dim 128 or 256,
+ * head_dim 32, window_size 8. */
+int prism_attn_window(prism_ctx* ctx, const prism_attn_params* p,
+                      const void* weights, size_t weight_elems,
+                      void* features, size_t feature_elems, void* stream);
+
+/* Replaces vkCmdDispatch(moe_router, ceil(T/256)) at prism_moe_bench.cpp:423-426:
+ * N-wide logits (256->N), first-max argmax, aux[assignment_offset+t] = e*,
+ * atomicAdd(aux[count_offset+e*], 1).  1 <= n_experts <= 256. */
+int prism_router(prism_ctx* ctx, const prism_router_params* p,
+                 const void* weights, size_t weight_elems,
+                 const void* features, size_t feature_elems,
+                 int32_t* aux, size_t aux_elems, void* stream);
+
+/* Replaces one vkCmdDispatch(moe_expert_skip) at prism_moe_bench.cpp:428-436:
+ * for tokens t with aux[assignment_offset+t] == expert_id,
+ * out[t] = x[t] + W2*gelu(W1*x[t] + b1) + b2. Other tokens are not written. */
+int prism_expert(prism_ctx* ctx, const prism_expert_params* p,
+                 const void* weights, size_t weight_elems,
+                 void* features, size_t feature_elems,
+                 const int32_t* aux, size_t aux_elems, void* stream);
+
+/* pw_project_128to256.comp.glsl: out = relu(Wu*x + bu) (prism_moe_bench.cpp:408-412) */
+int prism_proj_up(prism_ctx* ctx, const prism_proj_params* p,
+                  const void* weights, size_t weight_elems,
+                  void* features, size_t feature_elems, void* stream);
+
+/* pw_project_256to128.comp.glsl: out = Wd*x + bd (prism_moe_bench.cpp:441-444) */
+int prism_proj_down(prism_ctx* ctx, const prism_proj_params* p,
+                    const void* weights, size_t weight_elems,
+                    void* features, size_t feature_elems, void* stream);
+
+/* attention_windowed_d256.comp.glsl / attention_windowed.comp.glsl: attention as in
+ * prism_attn_window, then a dense FFN of width ffn_hidden.  The FFN output is
+ * accumulated in fp16 over ffn_hidden/ffn_chunk partial products, each of which
+ * includes b2 (attention_windowed_d256.comp.glsl:145-177): ffn_chunk = 256 gives the
+ * "Standard" d256 shader, ffn_chunk = ffn_hidden the unsplit d128 "Baseline"
+ * shader (attention_windowed.comp.glsl:151-170). */
+int prism_dense_block(prism_ctx* ctx, const prism_dense_params* p,
+                      int32_t ffn_hidden, int32_t ffn_chunk,
+                      const void* weights, size_t weight_elems,
+                      void* features, size_t feature_elems, void* stream);
+
+/* ---- fast path: a whole stack over a batch of frames ------------------------ */
+
+enum prism_block_kind { PRISM_BLOCK_MOE = 0, PRISM_BLOCK_DENSE = 1 };
+
+/* One transformer block: element offsets into the fp16 blob.  The MoE fields follow
+ * the bump layout of prism_moe_bench.cpp:164-172 (router [N][dim] + [N], expert e at
+ * expert_* + e*expert_stride); the dense fields follow TransformerPush. */
+typedef struct prism_block_desc {
+    int32_t kind;
+    int32_t qkv_w, qkv_b, out_w, out_b;
+    int32_t n_experts, router_w, router_b;
+    int32_t expert_w1, expert_b1, expert_w2, expert_b2, expert_stride;
+    int32_t ffn_hidden, ffn_chunk, ffn_w1, ffn_b1, ffn_w2, ffn_b2;
+} prism_block_desc;
+
+/* The stack: optional 128->256 ReLU adapter, n_blocks blocks, optional 256->128
+ * adapter (the sequence of prism_moe_bench.cpp:408-444).  Frames are
+ * spatial_h x spatial_w tokens, HWC fp16, consecutive in memory. */
+typedef struct prism_stack_desc {
+    int32_t dim, n_heads, head_dim;
+    int32_t spatial_w, spatial_h, window_size;
+    int32_t in_dim;          /* == dim, or 128 with the up adapter          */
+    int32_t up_w, up_b;      /* pw_project_128to256 weights, -1 if absent   */
+    int32_t out_dim;         /* == dim, or 128 with the down adapter        */
+    int32_t down_w, down_b;  /* pw_project_256to128 weights, -1 if absent   */
+    int32_t n_blocks;
+    const prism_block_desc* blocks;
+} prism_stack_desc;
+
+typedef struct prism_stack prism_stack;
+
+/* Validates desc against blob_elems, copies the blob (host or device pointer)
+ * into an aligned, repacked device arena and allocates the workspace for up to
+ * max_frames frames per forward.  Replaces the reference's weight upload
+ * (prism_vulkan.cpp:558-577, LoadWeights) for the transformer stack. */
+int prism_stack_create(prism_ctx* ctx, const prism_stack_desc* desc,
+                       const void* blob, size_t blob_elems, int blob_on_host,
+                       int max_frames, prism_stack** out);
+int prism_stack_destroy(prism_stack* st);
+
+/* in: device [frames][spatial_h*spatial_w][in_dim] fp16; out: device
+ * [frames][T][out_dim] fp16 (must not alias in).  assign (nullable): device int32
+ * [n_moe_blocks][frames*T] receives each MoE block's routing.  Stream-ordered,
+ * no host synchronisation, no allocation: CUDA-graph capturable. */
+int prism_stack_forward(prism_stack* st, const void* in, void* out, int frames,
+                        int32_t* assign, void* stream);
+
+/* Host-synchronising check of the device error word the kernels set when a
+ * bounded wait gives up (PRISM_E_TIMEOUT) or an invariant fails; clears it. */
+int prism_stack_status(prism_stack* st, void* stream);
+
+/* Number of kernel launches one prism_stack_forward issues for `frames`. */
+int prism_stack_launch_count(const prism_stack* st, int frames);
+
+/* Per-token element count of the stack's frames (spatial_h*spatial_w). */
+int prism_stack_tokens_per_frame(const prism_stack* st);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* PRISM_MOE_H */
