@@ -216,6 +216,20 @@ int prism_stack_forward(prism_stack* st, const void* in, void* out, int frames,
  * bounded wait gives up (PRISM_E_TIMEOUT) or an invariant fails; clears it. */
 int prism_stack_status(prism_stack* st, void* stream);
 
+/* Per-kernel timing (no counterpart in the reference, whose benches time a whole
+ * command buffer with timestamp queries, prism_moe_bench.cpp:183-209).  While
+ * enabled, prism_stack_forward brackets every launch with CUDA events on the
+ * caller's stream.  prism_stack_profile_read synchronises, adds up the elapsed
+ * milliseconds and launch counts per kernel kind (enum prism_kernel_kind, n_kinds
+ * entries) since the last read, and clears them. */
+enum prism_kernel_kind {
+    PRISM_K_PROJ_UP = 0, PRISM_K_ATTN = 1, PRISM_K_ROUTER = 2, PRISM_K_ROUTE = 3,
+    PRISM_K_EXPERT = 4, PRISM_K_DENSE_FFN = 5, PRISM_K_PROJ_DOWN = 6, PRISM_K_COPY = 7,
+    PRISM_K_COUNT = 8
+};
+int prism_stack_profile(prism_stack* st, int enable);
+int prism_stack_profile_read(prism_stack* st, double* ms, int64_t* launches, int n_kinds);
+
 /* Number of kernel launches one prism_stack_forward issues for `frames`. */
 int prism_stack_launch_count(const prism_stack* st, int frames);
 

@@ -1,0 +1,140 @@
+"""prism_inference_b200 - B200 (sm_100a) implementation of Prism's bottleneck
+transformer / MoE stack behind the C ABI of include/prism_moe.h.
+
+The Python layer is a thin host mirror over libprism_moe.so (ctypes): PyTorch is
+used only to own device memory and streams.  Two interfaces:
+
+* the per-pass drop-ins, one call per reference vkCmdDispatch, taking the same
+  push-constant blocks (AttnParams, RouterParams, ExpertParams, ProjParams,
+  DenseParams) and the three arenas (fp16 weight blob, fp16 feature arena, int32 aux
+  arena) - the dispatch contract of prism_moe_bench.cpp:213-505;
+* Stack: the whole stack of a StackLayout over a batch of frames (the fast path).
+
+No entry point falls back to the CPU: a missing libprism_moe.so raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+from . import abi, configs, layout, synth
+from .abi import (AttnParams, DenseParams, ExpertParams, PrismError, ProjParams, RouterParams,
+                  check)
+from .layout import StackLayout, build_stack
+
+__all__ = ["Prism", "Stack", "AttnParams", "RouterParams", "ExpertParams", "ProjParams",
+           "DenseParams", "PrismError", "StackLayout", "build_stack", "configs", "layout", "synth"]
+
+
+def _ptr(t) -> int:
+    return t.data_ptr()
+
+
+def _stream(stream) -> int | None:
+    if stream is None:
+        import torch
+        return torch.cuda.current_stream().cuda_stream
+    return getattr(stream, "cuda_stream", stream)
+
+
+class Prism:
+    """One context per CUDA device (prism_create)."""
+
+    def __init__(self, device: int = 0):
+        self.lib = abi.load()
+        self.device = device
+        h = C.c_void_p()
+        check(self.lib, self.lib.prism_create(device, C.byref(h)))
+        self.h = h
+
+    def close(self):
+        if self.h:
+            self.lib.prism_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # ---- per-pass drop-ins (tensors are flat CUDA arenas) ------------------------
+    def attn_window(self, p: AttnParams, weights, features, stream=None):
+        check(self.lib, self.lib.prism_attn_window(self.h, C.byref(p), _ptr(weights), weights.numel(),
+                                                   _ptr(features), features.numel(), _stream(stream)))
+
+    def router(self, p: RouterParams, weights, features, aux, stream=None):
+        check(self.lib, self.lib.prism_router(self.h, C.byref(p), _ptr(weights), weights.numel(),
+                                              _ptr(features), features.numel(), _ptr(aux), aux.numel(),
+                                              _stream(stream)))
+
+    def expert(self, p: ExpertParams, weights, features, aux, stream=None):
+        check(self.lib, self.lib.prism_expert(self.h, C.byref(p), _ptr(weights), weights.numel(),
+                                              _ptr(features), features.numel(), _ptr(aux), aux.numel(),
+                                              _stream(stream)))
+
+    def proj_up(self, p: ProjParams, weights, features, stream=None):
+        check(self.lib, self.lib.prism_proj_up(self.h, C.byref(p), _ptr(weights), weights.numel(),
+                                               _ptr(features), features.numel(), _stream(stream)))
+
+    def proj_down(self, p: ProjParams, weights, features, stream=None):
+        check(self.lib, self.lib.prism_proj_down(self.h, C.byref(p), _ptr(weights), weights.numel(),
+                                                 _ptr(features), features.numel(), _stream(stream)))
+
+    def dense_block(self, p: DenseParams, ffn_hidden: int, ffn_chunk: int, weights, features, stream=None):
+        check(self.lib, self.lib.prism_dense_block(self.h, C.byref(p), ffn_hidden, ffn_chunk, _ptr(weights),
+                                                   weights.numel(), _ptr(features), features.numel(),
+                                                   _stream(stream)))
+
+
+class Stack:
+    """The whole stack of a StackLayout (prism_stack_create / prism_stack_forward).
+
+    blob: numpy fp16/uint16 array (host) or a CUDA fp16 tensor (device)."""
+
+    def __init__(self, ctx: Prism, L: StackLayout, blob, max_frames: int):
+        self.ctx, self.lib, self.layout, self.max_frames = ctx, ctx.lib, L, max_frames
+        self._desc, self._keep = abi.stack_desc(L)
+        h = C.c_void_p()
+        if hasattr(blob, "data_ptr"):
+            ptr, n, on_host = blob.data_ptr(), blob.numel(), 0
+        else:
+            ptr, n, on_host = blob.ctypes.data, blob.size, 1
+        check(self.lib, self.lib.prism_stack_create(ctx.h, C.byref(self._desc), ptr, n, on_host, max_frames,
+                                                    C.byref(h)))
+        self.h = h
+
+    def forward(self, x, out, assign=None, stream=None):
+        """x: CUDA fp16 [F, T, in_dim]; out: CUDA fp16 [F, T, out_dim];
+        assign: optional CUDA int32 [n_moe_blocks, F*T]."""
+        F = x.shape[0]
+        check(self.lib, self.lib.prism_stack_forward(self.h, _ptr(x), _ptr(out), F,
+                                                     _ptr(assign) if assign is not None else None,
+                                                     _stream(stream)))
+        return out
+
+    def status(self, stream=None):
+        check(self.lib, self.lib.prism_stack_status(self.h, _stream(stream)))
+
+    def profile(self, enable: bool = True):
+        check(self.lib, self.lib.prism_stack_profile(self.h, int(enable)))
+
+    def profile_read(self):
+        """{kernel kind: (total ms, launches)} since the last read (synchronises)."""
+        n = len(abi.KERNEL_KINDS)
+        ms, cnt = (C.c_double * n)(), (C.c_int64 * n)()
+        check(self.lib, self.lib.prism_stack_profile_read(self.h, ms, cnt, n))
+        return {k: (ms[i], cnt[i]) for i, k in enumerate(abi.KERNEL_KINDS) if cnt[i]}
+
+    def launch_count(self, frames: int) -> int:
+        return self.lib.prism_stack_launch_count(self.h, frames)
+
+    def close(self):
+        if self.h:
+            self.lib.prism_stack_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -85,7 +85,8 @@ EXPORTS = ("prism_create", "prism_destroy", "prism_last_error_string", "prism_ab
            "prism_attn_window", "prism_router", "prism_expert", "prism_proj_up",
            "prism_proj_down", "prism_dense_block", "prism_stack_create", "prism_stack_destroy",
            "prism_stack_forward", "prism_stack_status", "prism_stack_launch_count",
-           "prism_stack_tokens_per_frame")
+           "prism_stack_tokens_per_frame", "prism_stack_profile", "prism_stack_profile_read")
+KERNEL_KINDS = ("proj_up", "attn", "router", "route", "expert", "dense_ffn", "proj_down", "copy")
 
 _lib = None
 
@@ -119,6 +120,8 @@ def load(path: os.PathLike | None = None) -> C.CDLL:
         "prism_stack_status": (i32, [vp, vp]),
         "prism_stack_launch_count": (i32, [vp, i32]),
         "prism_stack_tokens_per_frame": (i32, [vp]),
+        "prism_stack_profile": (i32, [vp, i32]),
+        "prism_stack_profile_read": (i32, [vp, C.POINTER(C.c_double), C.POINTER(C.c_int64), i32]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

@@ -1,0 +1,243 @@
+// common.cuh - sm_100a building blocks shared by the kernels of libprism_moe.so:
+// fp16 helpers, mbarriers with bounded waits, TMA (cp.async.bulk.tensor, no
+// multicast), tcgen05 MMA / TMEM, and the shared-memory matrix descriptors.
+#pragma once
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/prism_moe.h"
+
+#define PRISM_DEV __device__ __forceinline__
+
+namespace prism {
+
+// ---- error word ---------------------------------------------------------------
+// Kernels never trap.  A bounded wait that gives up ORs one of these bits into the
+// stack's device error word and the kernel winds down; prism_stack_status() turns
+// the word into PRISM_E_TIMEOUT / PRISM_E_RANGE on the host.
+enum : uint32_t { ERR_TIMEOUT = 1u, ERR_ROUTE = 2u };
+
+// Upper bound of any spin on an mbarrier: 2 s of %globaltimer.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+PRISM_DEV uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+PRISM_DEV uint64_t globaltimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+
+// ---- fp16 -----------------------------------------------------------------------
+PRISM_DEV float h2f(__half h) { return __half2float(h); }
+PRISM_DEV __half f2h(float f) { return __float2half_rn(f); }
+PRISM_DEV float rh(float f) { return __half2float(__float2half_rn(f)); }
+// two fp32 -> packed f16x2 (lo = a), round to nearest even
+PRISM_DEV uint32_t pack_h2(float a, float b) {
+    uint32_t r;
+    asm("cvt.rn.f16x2.f32 %0, %2, %1;" : "=r"(r) : "f"(a), "f"(b));
+    return r;
+}
+PRISM_DEV float lo_h2f(uint32_t v) { return __half2float(__ushort_as_half((unsigned short)(v & 0xffff))); }
+PRISM_DEV float hi_h2f(uint32_t v) { return __half2float(__ushort_as_half((unsigned short)(v >> 16))); }
+
+// GELU(tanh) of moe_expert_skip.comp.glsl:41-44 in fp32, left-to-right as the GLSL
+// writes it; tanh from the hardware tanh.approx.f32 (the result is rounded to fp16).
+PRISM_DEV float tanh_approx(float x) {
+    float y;
+    asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+// Same expression with the accurate tanhf (used by the per-pass drop-in kernels).
+PRISM_DEV float gelu_exact(float x) {
+    float c = __fmul_rn(0.044715f, x);
+    c = __fmul_rn(c, x);
+    c = __fmul_rn(c, x);
+    float inner = __fmul_rn(0.7978846f, __fadd_rn(x, c));
+    float t = tanhf(inner);
+    return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, t));
+}
+PRISM_DEV float gelu_f32(float x) {
+    float c = __fmul_rn(0.044715f, x);
+    c = __fmul_rn(c, x);
+    c = __fmul_rn(c, x);
+    float inner = __fmul_rn(0.7978846f, __fadd_rn(x, c));
+    float t = tanh_approx(inner);
+    return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, t));
+}
+
+// ---- mbarrier -------------------------------------------------------------------
+PRISM_DEV void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+PRISM_DEV void fence_barrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+PRISM_DEV void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+PRISM_DEV void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+PRISM_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait.  Returns false (and raises *abort) if the phase did not complete
+// within kWaitLimitNs or another role already aborted.
+PRISM_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+    if (mbar_try_wait(bar, parity)) return true;
+    uint64_t t0 = globaltimer();
+    for (uint32_t it = 1;; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 255u) == 0) {
+            if (*abort) return false;
+            if (globaltimer() - t0 > kWaitLimitNs) {
+                *abort = 1;
+                return false;
+            }
+        }
+    }
+}
+// cp.async (non-bulk) completion tracked by an mbarrier: one arrival per thread.
+PRISM_DEV void cp_async_mbar_arrive(uint64_t* bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// 16-byte global -> shared copy; src_bytes = 0 zero-fills the destination.
+PRISM_DEV void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes)
+                 : "memory");
+}
+
+// generic-proxy shared-memory writes -> visible to the async proxy (TMA, tcgen05)
+PRISM_DEV void fence_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// ---- TMA (no multicast anywhere in this library) ---------------------------------
+PRISM_DEV void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+        "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+        : "memory");
+}
+PRISM_DEV void tma_load_4d(uint32_t dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2,
+                           int c3) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
+        "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+        : "memory");
+}
+// Store of a box; elements outside the tensor are not written (masked store).
+PRISM_DEV void tma_store_4d(const CUtensorMap* map, uint32_t src, int c0, int c1, int c2, int c3) {
+    asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+                     map),
+                 "r"(src), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+                 : "memory");
+}
+PRISM_DEV void tma_store_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+PRISM_DEV void tma_store_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+PRISM_DEV void tma_store_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+PRISM_DEV void prefetch_tmap(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+
+// ---- tcgen05 / TMEM ------------------------------------------------------------
+PRISM_DEV void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {  // whole warp
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+                 "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+PRISM_DEV void tmem_dealloc(uint32_t taddr, uint32_t ncols) {  // whole warp
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+PRISM_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+PRISM_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// D(tmem) (+)= A(smem desc) x B(smem desc)^T, kind::f16 (fp16 inputs, fp32 accumulate)
+PRISM_DEV void mma_f16_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// mbarrier arrives once every tcgen05 op this thread issued before has completed
+PRISM_DEV void mma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     smem_u32(bar))
+                 : "memory");
+}
+
+// Instruction descriptor, kind::f16: A = B = fp16, D = fp32, both K-major.
+//  [4,6) D format (1 = f32), [7,10) A format (0 = f16), [10,13) B format (0 = f16),
+//  [15] A major, [16] B major (0 = K), [17,23) N >> 3, [24,29) M >> 4.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
+    return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// Shared-memory matrix descriptor for a K-major operand stored in the canonical
+// swizzled layout: rows of `row_bytes` (128 or 64) bytes, 8-row atoms of
+// 8*row_bytes bytes stacked along M/N (SBO = 8*row_bytes), the 16-byte chunk index
+// within a row XOR-ed with address bits [7,10) (128B) or [7,9) (64B).
+//  [0,14) start >> 4, [16,30) LBO >> 4 (ignored for swizzled K-major, 1),
+//  [32,46) SBO >> 4, [46,48) version = 1, [49,52) base offset = 0,
+//  [61,64) layout: 2 = SWIZZLE_128B, 4 = SWIZZLE_64B.
+enum : int { SW128 = 2, SW64 = 4 };
+PRISM_DEV uint64_t sdesc(uint32_t saddr, int layout) {
+    const uint32_t sbo = layout == SW128 ? 1024u : 512u;
+    return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(sbo >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)layout << 61);
+}
+
+// Byte offset of the 16-byte chunk `chunk` of row `row` inside a swizzled K-major
+// block whose base is aligned to the swizzle repeat (1024 B / 512 B).
+PRISM_DEV uint32_t sw128_off(uint32_t row, uint32_t chunk) {
+    return row * 128u + ((chunk ^ (row & 7u)) << 4);
+}
+PRISM_DEV uint32_t sw64_off(uint32_t row, uint32_t chunk) {
+    return row * 64u + ((chunk ^ ((row >> 1) & 3u)) << 4);
+}
+
+// tcgen05.ld 32 lanes x 32 bit, 16 consecutive columns -> 16 registers per thread
+PRISM_DEV void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+          "=r"(r[15])
+        : "r"(taddr));
+}
+PRISM_DEV void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+PRISM_DEV uint32_t elect_one() {  // 1 on exactly one active lane of the warp
+    uint32_t pred = 0;
+    asm volatile(
+        "{\n\t.reg .pred P;\n\t.reg .b32 rx;\n\t"
+        "elect.sync rx|P, %1;\n\t"
+        "selp.u32 %0, 1, 0, P;\n\t}"
+        : "=r"(pred)
+        : "r"(0xffffffffu));
+    return pred;
+}
+
+PRISM_DEV void named_bar_sync(int id, int nthreads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+}  // namespace prism

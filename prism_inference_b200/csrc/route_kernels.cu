@@ -1,0 +1,87 @@
+// route_kernels.cu - token routing for the grouped expert GEMM.
+//
+// The reference routes with an atomic per-expert count (moe_router.comp.glsl:50) and
+// then dispatches every expert over every token, letting unrouted tokens return
+// early (moe_expert_skip.comp.glsl:30; prism_moe_bench.cpp:428-436).  Its unused
+// packed variant scatters tokens into per-expert buffers with atomics
+// (moe_pack.comp.glsl:23-40).  Here the router's counts feed:
+//   route_plan     one CTA: exclusive scan of the counts -> segment offsets, the list
+//                  of 128-row tiles (expert, first sorted row, rows) and the tile
+//                  count, then resets the counters for the next block;
+//   route_scatter  every token takes a slot in its expert's segment (warp-aggregated
+//                  atomics), giving perm[sorted row] = token.
+// The order of tokens inside a segment is not fixed, but each output row of the
+// grouped GEMM depends only on its own input row, so results do not depend on it.
+#include "common.cuh"
+#include "route_kernels.cuh"
+#include "tc_ffn.cuh"
+
+namespace prism {
+
+__global__ void __launch_bounds__(256) route_plan_kernel(RoutePlanArgs a) {
+    __shared__ int s_off[256], s_toff[256];
+    const int e = threadIdx.x;
+    const int n = a.n_experts;
+    const int c = e < n ? a.counts[e] : 0;
+    s_off[e] = c;
+    s_toff[e] = (c + 127) / 128;
+    __syncthreads();
+    // inclusive Hillis-Steele scans of counts and tile counts
+    for (int d = 1; d < 256; d <<= 1) {
+        const int v0 = e >= d ? s_off[e - d] : 0;
+        const int v1 = e >= d ? s_toff[e - d] : 0;
+        __syncthreads();
+        s_off[e] += v0;
+        s_toff[e] += v1;
+        __syncthreads();
+    }
+    const int off = s_off[e] - c;                 // exclusive
+    const int nt = (c + 127) / 128;
+    const int toff = s_toff[e] - nt;
+    if (e < n) {
+        a.offsets[e] = off;
+        a.cursor[e] = 0;
+        if (a.counts_out) a.counts_out[e] = c;
+        a.counts[e] = 0;  // ready for the next block's router
+        for (int j = 0; j < nt; ++j) {
+            ExpertTile t;
+            t.expert = e;
+            t.start = off + j * 128;
+            t.rows = min(128, c - j * 128);
+            t.pad = 0;
+            a.tiles[toff + j] = t;
+        }
+    }
+    if (e == 255) {
+        *a.n_tiles = s_toff[255];
+        if (s_off[255] != a.n_tokens) atomicOr(a.err, ERR_ROUTE);  // every token routed exactly once
+    }
+}
+
+__global__ void __launch_bounds__(256) route_scatter_kernel(RouteScatterArgs a) {
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    const bool active = t < a.n_tokens;
+    int e = active ? a.assign[t] : -1;
+    if (active && (e < 0 || e >= a.n_experts)) {
+        atomicOr(a.err, ERR_ROUTE);
+        e = -1;
+    }
+    const unsigned lanes = __activemask();
+    const unsigned peers = __match_any_sync(lanes, e);
+    const int leader = __ffs(peers) - 1;
+    const int rank = __popc(peers & ((1u << (threadIdx.x & 31)) - 1));
+    int base = 0;
+    if (e >= 0 && (int)(threadIdx.x & 31) == leader) base = atomicAdd(&a.cursor[e], __popc(peers));
+    base = __shfl_sync(lanes, base, leader);
+    if (e >= 0) a.perm[a.offsets[e] + base + rank] = t;
+}
+
+cudaError_t launch_route(const RoutePlanArgs& p, const RouteScatterArgs& s, cudaStream_t st) {
+    route_plan_kernel<<<1, 256, 0, st>>>(p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    if (s.n_tokens > 0) route_scatter_kernel<<<(s.n_tokens + 255) / 256, 256, 0, st>>>(s);
+    return cudaGetLastError();
+}
+
+}  // namespace prism

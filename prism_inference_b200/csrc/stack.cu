@@ -1,0 +1,810 @@
+// stack.cu - host side of libprism_moe.so: the C ABI of include/prism_moe.h.
+//
+// Replaces the reference's host dispatch (prism_moe_bench.cpp): instead of recording
+// push constants + vkCmdDispatch + barrier per pass into a Vulkan command buffer, the
+// entry points validate their arguments and launch stream-ordered CUDA kernels.
+//  * per-pass drop-ins: one launch per reference dispatch (pass_kernels.cu)
+//  * prism_stack_*: the whole stack over a batch of frames, with the weights repacked
+//    once into aligned device arrays for TMA and the per-expert dispatch loop
+//    replaced by route (route_kernels.cu) + one grouped tcgen05 GEMM (tc_ffn.cu).
+#include <cudaTypedefs.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "pass_kernels.cuh"
+#include "route_kernels.cuh"
+#include "tc_ffn.cuh"
+
+using namespace prism;
+
+struct prism_ctx {
+    int device;
+    int sm_count;
+};
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    return code;
+}
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int d) {
+        if (cudaGetDevice(&prev) == cudaSuccess && prev != d) cudaSetDevice(d);
+    }
+    ~DeviceGuard() {
+        int cur;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+#define CUDA_TRY(x)                                                                          \
+    do {                                                                                     \
+        cudaError_t e_ = (x);                                                                \
+        if (e_ != cudaSuccess) return fail(PRISM_E_CUDA, "%s: %s", #x, cudaGetErrorString(e_)); \
+    } while (0)
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// [off, off + n) inside [0, limit)?
+inline bool in_range(int64_t off, int64_t n, size_t limit) {
+    return off >= 0 && n >= 0 && (uint64_t)(off + n) <= (uint64_t)limit;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+// 2-D fp16 row-major [rows][cols] tensor, box [box_rows][64] with 128-byte swizzle.
+int make_map_2d(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+    auto fn = encode_fn();
+    if (!fn) return fail(PRISM_E_CUDA, "cuTensorMapEncodeTiled is not available");
+    if (((uintptr_t)base & 15) || (cols * 2) % 16) return fail(PRISM_E_ALIGN, "tensor map base/stride not 16-byte aligned");
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {cols * 2};
+    cuuint32_t box[2] = {64, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(PRISM_E_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return PRISM_OK;
+}
+
+float half_bits_to_float(uint16_t h) {
+    __half_raw r;
+    r.x = h;
+    return __half2float(__half(r));
+}
+
+}  // namespace
+
+// ============================== context =========================================
+
+extern "C" int prism_abi_version(void) { return PRISM_ABI_VERSION; }
+extern "C" const char* prism_last_error_string(void) { return g_err.c_str(); }
+
+extern "C" int prism_create(int device, prism_ctx** out) {
+    if (!out) return fail(PRISM_E_ARG, "prism_create: out is NULL");
+    *out = nullptr;
+    int n = 0;
+    CUDA_TRY(cudaGetDeviceCount(&n));
+    if (device < 0 || device >= n) return fail(PRISM_E_ARG, "prism_create: device %d of %d", device, n);
+    cudaDeviceProp prop;
+    CUDA_TRY(cudaGetDeviceProperties(&prop, device));
+    if (prop.major != 10)
+        return fail(PRISM_E_UNSUPPORTED, "prism_create: device %d is sm_%d%d; this library is built for sm_100a",
+                    device, prop.major, prop.minor);
+    auto* c = new prism_ctx;
+    c->device = device;
+    c->sm_count = prop.multiProcessorCount;
+    *out = c;
+    return PRISM_OK;
+}
+
+extern "C" int prism_destroy(prism_ctx* ctx) {
+    delete ctx;
+    return PRISM_OK;
+}
+
+// ============================== per-pass drop-ins ===============================
+
+static int check_attn_shape(int dim, int n_heads, int head_dim, int ws, int W, int H, int n_tokens) {
+    if (dim != 128 && dim != 256) return fail(PRISM_E_UNSUPPORTED, "dim %d (128 or 256)", dim);
+    if (head_dim != 32 || n_heads * head_dim != dim)
+        return fail(PRISM_E_UNSUPPORTED, "heads %d x %d for dim %d (head_dim 32)", n_heads, head_dim, dim);
+    if (ws != 8) return fail(PRISM_E_UNSUPPORTED, "window_size %d (8)", ws);
+    if (W <= 0 || H <= 0 || n_tokens <= 0) return fail(PRISM_E_ARG, "spatial %dx%d, n_tokens %d", W, H, n_tokens);
+    return PRISM_OK;
+}
+
+extern "C" int prism_attn_window(prism_ctx* ctx, const prism_attn_params* p, const void* weights,
+                                 size_t weight_elems, void* features, size_t feature_elems, void* stream) {
+    if (!ctx || !p || !weights || !features) return fail(PRISM_E_ARG, "prism_attn_window: NULL argument");
+    int rc = check_attn_shape(p->dim, p->n_heads, p->head_dim, p->window_size, p->spatial_w, p->spatial_h,
+                              p->n_tokens);
+    if (rc) return rc;
+    const int64_t D = p->dim, T = (int64_t)p->spatial_w * p->spatial_h;
+    if (!in_range(p->input_offset, T * D, feature_elems) || !in_range(p->output_offset, T * D, feature_elems))
+        return fail(PRISM_E_RANGE, "prism_attn_window: feature offsets outside the arena");
+    if (!in_range(p->qkv_w, 3 * D * D, weight_elems) || !in_range(p->qkv_b, 3 * D, weight_elems) ||
+        !in_range(p->out_w, D * D, weight_elems) || !in_range(p->out_b, D, weight_elems))
+        return fail(PRISM_E_RANGE, "prism_attn_window: weight offsets outside the blob");
+    DeviceGuard g(ctx->device);
+    AttnArgs a;
+    a.weights = static_cast<const __half*>(weights);
+    a.x = static_cast<const __half*>(features) + p->input_offset;
+    a.y = static_cast<__half*>(features) + p->output_offset;
+    a.frame_stride = T * D;
+    a.qkv_w = p->qkv_w;
+    a.qkv_b = p->qkv_b;
+    a.out_w = p->out_w;
+    a.out_b = p->out_b;
+    a.W = p->spatial_w;
+    a.H = p->spatial_h;
+    a.n_tokens = p->n_tokens;
+    a.scale = 0.1767766953f;  // 1/sqrt(32), split2_qkv_attn_d256.comp.glsl:62
+    CUDA_TRY(launch_attn_window(a, p->dim, 1, as_stream(stream)));
+    return PRISM_OK;
+}
+
+extern "C" int prism_router(prism_ctx* ctx, const prism_router_params* p, const void* weights,
+                            size_t weight_elems, const void* features, size_t feature_elems, int32_t* aux,
+                            size_t aux_elems, void* stream) {
+    if (!ctx || !p || !weights || !features || !aux) return fail(PRISM_E_ARG, "prism_router: NULL argument");
+    if (p->dim != 128 && p->dim != 256) return fail(PRISM_E_UNSUPPORTED, "prism_router: dim %d", p->dim);
+    if (p->n_experts < 1 || p->n_experts > 256)
+        return fail(PRISM_E_UNSUPPORTED, "prism_router: n_experts %d (1..256)", p->n_experts);
+    if (p->n_tokens < 0) return fail(PRISM_E_ARG, "prism_router: n_tokens %d", p->n_tokens);
+    const int64_t D = p->dim, T = p->n_tokens, N = p->n_experts;
+    if (!in_range(p->input_offset, T * D, feature_elems))
+        return fail(PRISM_E_RANGE, "prism_router: input outside the arena");
+    if (!in_range(p->assignment_offset, T, aux_elems) || !in_range(p->count_offset, N, aux_elems))
+        return fail(PRISM_E_RANGE, "prism_router: aux offsets outside the aux arena");
+    if (!in_range(p->router_w, N * D, weight_elems) || !in_range(p->router_b, N, weight_elems))
+        return fail(PRISM_E_RANGE, "prism_router: weight offsets outside the blob");
+    DeviceGuard g(ctx->device);
+    RouterArgs a;
+    a.weights = static_cast<const __half*>(weights);
+    a.x = static_cast<const __half*>(features) + p->input_offset;
+    a.assign = aux + p->assignment_offset;
+    a.counts = aux + p->count_offset;
+    a.router_w = p->router_w;
+    a.router_b = p->router_b;
+    a.n_experts = p->n_experts;
+    a.n_tokens = p->n_tokens;
+    CUDA_TRY(launch_router(a, p->dim, as_stream(stream)));
+    return PRISM_OK;
+}
+
+extern "C" int prism_expert(prism_ctx* ctx, const prism_expert_params* p, const void* weights,
+                            size_t weight_elems, void* features, size_t feature_elems, const int32_t* aux,
+                            size_t aux_elems, void* stream) {
+    if (!ctx || !p || !weights || !features || !aux) return fail(PRISM_E_ARG, "prism_expert: NULL argument");
+    if (p->dim != 128 && p->dim != 256) return fail(PRISM_E_UNSUPPORTED, "prism_expert: dim %d", p->dim);
+    if (p->n_tokens < 0) return fail(PRISM_E_ARG, "prism_expert: n_tokens %d", p->n_tokens);
+    const int64_t D = p->dim, T = p->n_tokens;
+    if (!in_range(p->input_offset, T * D, feature_elems) || !in_range(p->output_offset, T * D, feature_elems))
+        return fail(PRISM_E_RANGE, "prism_expert: feature offsets outside the arena");
+    if (!in_range(p->assignment_offset, T, aux_elems))
+        return fail(PRISM_E_RANGE, "prism_expert: assignment outside the aux arena");
+    if (!in_range(p->w1_offset, D * D, weight_elems) || !in_range(p->b1_offset, D, weight_elems) ||
+        !in_range(p->w2_offset, D * D, weight_elems) || !in_range(p->b2_offset, D, weight_elems))
+        return fail(PRISM_E_RANGE, "prism_expert: weight offsets outside the blob");
+    DeviceGuard g(ctx->device);
+    ExpertArgs a;
+    a.weights = static_cast<const __half*>(weights);
+    a.x = static_cast<const __half*>(features) + p->input_offset;
+    a.y = static_cast<__half*>(features) + p->output_offset;
+    a.assign = aux + p->assignment_offset;
+    a.w1 = p->w1_offset;
+    a.b1 = p->b1_offset;
+    a.w2 = p->w2_offset;
+    a.b2 = p->b2_offset;
+    a.expert_id = p->expert_id;
+    a.n_tokens = p->n_tokens;
+    CUDA_TRY(launch_expert(a, p->dim, as_stream(stream)));
+    return PRISM_OK;
+}
+
+static int proj_common(prism_ctx* ctx, const prism_proj_params* p, const void* weights, size_t weight_elems,
+                       void* features, size_t feature_elems, void* stream, bool up) {
+    const char* name = up ? "prism_proj_up" : "prism_proj_down";
+    if (!ctx || !p || !weights || !features) return fail(PRISM_E_ARG, "%s: NULL argument", name);
+    if (p->n_tokens < 0) return fail(PRISM_E_ARG, "%s: n_tokens %d", name, p->n_tokens);
+    const int64_t T = p->n_tokens, K = up ? 128 : 256, N = up ? 256 : 128;
+    if (!in_range(p->input_offset, T * K, feature_elems) || !in_range(p->output_offset, T * N, feature_elems))
+        return fail(PRISM_E_RANGE, "%s: feature offsets outside the arena", name);
+    if (!in_range(p->w_offset, N * K, weight_elems) || !in_range(p->b_offset, N, weight_elems))
+        return fail(PRISM_E_RANGE, "%s: weight offsets outside the blob", name);
+    DeviceGuard g(ctx->device);
+    ProjArgs a;
+    a.weights = static_cast<const __half*>(weights);
+    a.x = static_cast<const __half*>(features) + p->input_offset;
+    a.y = static_cast<__half*>(features) + p->output_offset;
+    a.w = p->w_offset;
+    a.b = p->b_offset;
+    a.n_tokens = p->n_tokens;
+    CUDA_TRY(launch_proj(a, up, as_stream(stream)));
+    return PRISM_OK;
+}
+
+extern "C" int prism_proj_up(prism_ctx* ctx, const prism_proj_params* p, const void* weights, size_t weight_elems,
+                             void* features, size_t feature_elems, void* stream) {
+    return proj_common(ctx, p, weights, weight_elems, features, feature_elems, stream, true);
+}
+extern "C" int prism_proj_down(prism_ctx* ctx, const prism_proj_params* p, const void* weights,
+                               size_t weight_elems, void* features, size_t feature_elems, void* stream) {
+    return proj_common(ctx, p, weights, weight_elems, features, feature_elems, stream, false);
+}
+
+extern "C" int prism_dense_block(prism_ctx* ctx, const prism_dense_params* p, int32_t ffn_hidden,
+                                 int32_t ffn_chunk, const void* weights, size_t weight_elems, void* features,
+                                 size_t feature_elems, void* stream) {
+    if (!ctx || !p || !weights || !features) return fail(PRISM_E_ARG, "prism_dense_block: NULL argument");
+    int rc = check_attn_shape(p->dim, p->n_heads, p->head_dim, p->window_size, p->spatial_w, p->spatial_h,
+                              p->n_tokens);
+    if (rc) return rc;
+    if (ffn_hidden <= 0 || ffn_chunk <= 0 || ffn_hidden % ffn_chunk || ffn_chunk > 512 || ffn_chunk % 32)
+        return fail(PRISM_E_UNSUPPORTED, "prism_dense_block: ffn_hidden %d / ffn_chunk %d", ffn_hidden, ffn_chunk);
+    const int64_t D = p->dim, T = (int64_t)p->spatial_w * p->spatial_h, Hd = ffn_hidden;
+    if (!in_range(p->input_offset, T * D, feature_elems) || !in_range(p->output_offset, T * D, feature_elems))
+        return fail(PRISM_E_RANGE, "prism_dense_block: feature offsets outside the arena");
+    if (!in_range(p->qkv_w_offset, 3 * D * D, weight_elems) || !in_range(p->qkv_b_offset, 3 * D, weight_elems) ||
+        !in_range(p->out_w_offset, D * D, weight_elems) || !in_range(p->out_b_offset, D, weight_elems) ||
+        !in_range(p->ffn_w1_offset, Hd * D, weight_elems) || !in_range(p->ffn_b1_offset, Hd, weight_elems) ||
+        !in_range(p->ffn_w2_offset, D * Hd, weight_elems) || !in_range(p->ffn_b2_offset, D, weight_elems))
+        return fail(PRISM_E_RANGE, "prism_dense_block: weight offsets outside the blob");
+    DeviceGuard g(ctx->device);
+    AttnArgs a;
+    a.weights = static_cast<const __half*>(weights);
+    a.x = static_cast<const __half*>(features) + p->input_offset;
+    a.y = static_cast<__half*>(features) + p->output_offset;
+    a.frame_stride = T * D;
+    a.qkv_w = p->qkv_w_offset;
+    a.qkv_b = p->qkv_b_offset;
+    a.out_w = p->out_w_offset;
+    a.out_b = p->out_b_offset;
+    a.W = p->spatial_w;
+    a.H = p->spatial_h;
+    a.n_tokens = p->n_tokens;
+    a.scale = 0.1767766953f;
+    CUDA_TRY(launch_attn_window(a, p->dim, 1, as_stream(stream)));
+    DenseFfnArgs f;
+    f.weights = a.weights;
+    f.io = a.y;
+    f.w1 = p->ffn_w1_offset;
+    f.b1 = p->ffn_b1_offset;
+    f.w2 = p->ffn_w2_offset;
+    f.b2 = p->ffn_b2_offset;
+    f.hidden = ffn_hidden;
+    f.chunk = ffn_chunk;
+    f.n_tokens = (int)T;
+    CUDA_TRY(launch_dense_ffn(f, p->dim, as_stream(stream)));
+    return PRISM_OK;
+}
+
+// ============================== fast path ======================================
+
+namespace {
+
+struct FastBlock {
+    prism_block_desc d;
+    __half* w1 = nullptr;  // experts: [E][256][256]; dense: [hidden][256]
+    __half* w2 = nullptr;  // experts: [E][256][256]; dense: [256][hidden]
+    float* b1 = nullptr;   // [E][256] / [hidden]
+    float* b2 = nullptr;   // [E][256] / [256]
+    CUtensorMap tm_w1, tm_w2;
+    int moe_index = -1;
+};
+
+}  // namespace
+
+struct prism_stack {
+    prism_ctx* ctx = nullptr;
+    prism_stack_desc desc;
+    std::vector<prism_block_desc> bdesc;
+    int T = 0, max_frames = 0, n_moe = 0;
+    bool tc = false;  // dim 256: tensor-core expert / dense FFN / adapters
+    __half* blob = nullptr;
+    size_t blob_elems = 0;
+    __half *up_w = nullptr, *dn_w = nullptr;
+    float *up_b = nullptr, *dn_b = nullptr;
+    CUtensorMap tm_up, tm_dn, tm_act_a, tm_act_b, tm_act_y;
+    std::vector<FastBlock> blocks;
+    __half *act_a = nullptr, *act_b = nullptr, *act_y = nullptr;
+    int32_t *assign_ws = nullptr, *counts = nullptr, *offsets = nullptr, *cursor = nullptr, *perm = nullptr,
+            *n_tiles = nullptr;
+    ExpertTile* tiles = nullptr;
+    uint32_t* err = nullptr;
+    std::vector<void*> allocs;
+    // per-kernel profiling (prism_stack_profile)
+    bool profiling = false;
+    std::vector<cudaEvent_t> ev_pool;
+    size_t ev_used = 0;
+    std::vector<int> ev_kind;  // kind of each recorded (start, end) pair
+};
+
+namespace {
+
+template <typename T>
+int dev_alloc(prism_stack* st, T** p, size_t count) {
+    void* q = nullptr;
+    if (cudaMalloc(&q, count * sizeof(T) + 16) != cudaSuccess)
+        return fail(PRISM_E_NOMEM, "cudaMalloc of %zu bytes failed", count * sizeof(T));
+    st->allocs.push_back(q);
+    *p = static_cast<T*>(q);
+    return PRISM_OK;
+}
+
+void free_stack(prism_stack* st) {
+    for (void* p : st->allocs) cudaFree(p);
+    st->allocs.clear();
+    for (cudaEvent_t e : st->ev_pool) cudaEventDestroy(e);
+    st->ev_pool.clear();
+}
+
+// Brackets one launch with events when profiling is on.
+struct KernelTimer {
+    prism_stack* st;
+    cudaStream_t s;
+    int kind;
+    cudaEvent_t end = nullptr;
+    KernelTimer(prism_stack* st_, cudaStream_t s_, int kind_) : st(st_), s(s_), kind(kind_) {
+        if (!st->profiling) return;
+        while (st->ev_pool.size() < st->ev_used + 2) {
+            cudaEvent_t e;
+            if (cudaEventCreate(&e) != cudaSuccess) return;
+            st->ev_pool.push_back(e);
+        }
+        cudaEventRecord(st->ev_pool[st->ev_used], s);
+        end = st->ev_pool[st->ev_used + 1];
+        st->ev_used += 2;
+        st->ev_kind.push_back(kind);
+    }
+    ~KernelTimer() {
+        if (end) cudaEventRecord(end, s);
+    }
+};
+
+int validate_desc(const prism_stack_desc* d, size_t elems) {
+    int rc = check_attn_shape(d->dim, d->n_heads, d->head_dim, d->window_size, d->spatial_w, d->spatial_h, 1);
+    if (rc) return rc;
+    const int64_t D = d->dim;
+    if (d->n_blocks < 0 || (d->n_blocks > 0 && !d->blocks)) return fail(PRISM_E_ARG, "n_blocks %d", d->n_blocks);
+    if (d->up_w >= 0) {
+        if (D != 256 || d->in_dim != 128) return fail(PRISM_E_UNSUPPORTED, "up adapter needs dim 256, in_dim 128");
+        if (!in_range(d->up_w, 256 * 128, elems) || !in_range(d->up_b, 256, elems))
+            return fail(PRISM_E_RANGE, "up adapter outside the blob");
+    } else if (d->in_dim != D) {
+        return fail(PRISM_E_ARG, "in_dim %d without adapter", d->in_dim);
+    }
+    if (d->down_w >= 0) {
+        if (D != 256 || d->out_dim != 128) return fail(PRISM_E_UNSUPPORTED, "down adapter needs dim 256, out_dim 128");
+        if (!in_range(d->down_w, 128 * 256, elems) || !in_range(d->down_b, 128, elems))
+            return fail(PRISM_E_RANGE, "down adapter outside the blob");
+    } else if (d->out_dim != D) {
+        return fail(PRISM_E_ARG, "out_dim %d without adapter", d->out_dim);
+    }
+    for (int i = 0; i < d->n_blocks; ++i) {
+        const prism_block_desc& b = d->blocks[i];
+        if (!in_range(b.qkv_w, 3 * D * D, elems) || !in_range(b.qkv_b, 3 * D, elems) ||
+            !in_range(b.out_w, D * D, elems) || !in_range(b.out_b, D, elems))
+            return fail(PRISM_E_RANGE, "block %d: attention weights outside the blob", i);
+        if (b.kind == PRISM_BLOCK_MOE) {
+            if (D != 256) return fail(PRISM_E_UNSUPPORTED, "block %d: MoE blocks need dim 256", i);
+            if (b.n_experts < 1 || b.n_experts > 256) return fail(PRISM_E_UNSUPPORTED, "block %d: n_experts %d", i, b.n_experts);
+            if (!in_range(b.router_w, b.n_experts * D, elems) || !in_range(b.router_b, b.n_experts, elems))
+                return fail(PRISM_E_RANGE, "block %d: router outside the blob", i);
+            const int64_t last = (int64_t)(b.n_experts - 1) * b.expert_stride;
+            if (b.expert_stride < 0 || !in_range(b.expert_w1, last + D * D, elems) ||
+                !in_range(b.expert_b1, last + D, elems) || !in_range(b.expert_w2, last + D * D, elems) ||
+                !in_range(b.expert_b2, last + D, elems))
+                return fail(PRISM_E_RANGE, "block %d: experts outside the blob", i);
+        } else if (b.kind == PRISM_BLOCK_DENSE) {
+            const int64_t Hd = b.ffn_hidden;
+            if (Hd <= 0 || b.ffn_chunk <= 0 || Hd % b.ffn_chunk || b.ffn_chunk > 512 || b.ffn_chunk % 32)
+                return fail(PRISM_E_UNSUPPORTED, "block %d: ffn_hidden %d / ffn_chunk %d", i, b.ffn_hidden, b.ffn_chunk);
+            if (D == 256 && b.ffn_chunk != 256)
+                return fail(PRISM_E_UNSUPPORTED, "block %d: dim-256 dense FFN needs ffn_chunk 256", i);
+            if (!in_range(b.ffn_w1, Hd * D, elems) || !in_range(b.ffn_b1, Hd, elems) ||
+                !in_range(b.ffn_w2, D * Hd, elems) || !in_range(b.ffn_b2, D, elems))
+                return fail(PRISM_E_RANGE, "block %d: FFN weights outside the blob", i);
+        } else {
+            return fail(PRISM_E_ARG, "block %d: kind %d", i, b.kind);
+        }
+    }
+    return PRISM_OK;
+}
+
+template <typename T>
+int upload(prism_stack* st, T** dst, const std::vector<T>& src) {
+    int rc = dev_alloc(st, dst, src.size());
+    if (rc) return rc;
+    CUDA_TRY(cudaMemcpy(*dst, src.data(), src.size() * sizeof(T), cudaMemcpyHostToDevice));
+    return PRISM_OK;
+}
+
+}  // namespace
+
+extern "C" int prism_stack_create(prism_ctx* ctx, const prism_stack_desc* desc, const void* blob, size_t blob_elems,
+                                  int blob_on_host, int max_frames, prism_stack** out) {
+    if (!ctx || !desc || !blob || !out) return fail(PRISM_E_ARG, "prism_stack_create: NULL argument");
+    *out = nullptr;
+    if (max_frames < 1) return fail(PRISM_E_ARG, "prism_stack_create: max_frames %d", max_frames);
+    int rc = validate_desc(desc, blob_elems);
+    if (rc) return rc;
+    DeviceGuard g(ctx->device);
+    if (!blob_on_host) {
+        cudaPointerAttributes attr;
+        if (cudaPointerGetAttributes(&attr, blob) != cudaSuccess || attr.type != cudaMemoryTypeDevice ||
+            attr.device != ctx->device)
+            return fail(PRISM_E_ARG, "prism_stack_create: blob is not device memory of device %d", ctx->device);
+    }
+    const int64_t T = (int64_t)desc->spatial_w * desc->spatial_h;
+    const int64_t rows = T * max_frames;
+    if (rows > (int64_t)1 << 30) return fail(PRISM_E_RANGE, "prism_stack_create: %lld tokens", (long long)rows);
+
+    auto* st = new prism_stack;
+    st->ctx = ctx;
+    st->desc = *desc;
+    st->bdesc.assign(desc->blocks, desc->blocks + desc->n_blocks);
+    st->desc.blocks = st->bdesc.data();
+    st->T = (int)T;
+    st->max_frames = max_frames;
+    st->tc = desc->dim == 256;
+
+    // host copy of the blob (repacking is done on the host once)
+    std::vector<uint16_t> hb;
+    const uint16_t* hblob = static_cast<const uint16_t*>(blob);
+    if (!blob_on_host) {
+        hb.resize(blob_elems);
+        if (cudaMemcpy(hb.data(), blob, blob_elems * 2, cudaMemcpyDeviceToHost) != cudaSuccess) {
+            delete st;
+            return fail(PRISM_E_CUDA, "prism_stack_create: blob download failed");
+        }
+        hblob = hb.data();
+    }
+    auto fail_cleanup = [&](int code) {
+        free_stack(st);
+        delete st;
+        return code;
+    };
+    // raw blob on the device (the attention / router kernels address it by element offset)
+    if ((rc = dev_alloc(st, &st->blob, blob_elems))) return fail_cleanup(rc);
+    st->blob_elems = blob_elems;
+    if (cudaMemcpy(st->blob, hblob, blob_elems * 2, cudaMemcpyHostToDevice) != cudaSuccess)
+        return fail_cleanup(fail(PRISM_E_CUDA, "blob upload failed"));
+
+    auto copy_mat = [&](std::vector<uint16_t>& dst, size_t dst_off, int64_t src_off, int64_t rows_, int64_t cols,
+                        int64_t src_ld) {
+        for (int64_t r = 0; r < rows_; ++r)
+            memcpy(&dst[dst_off + r * cols], hblob + src_off + r * src_ld, cols * 2);
+    };
+    auto copy_bias = [&](std::vector<float>& dst, size_t dst_off, int64_t src_off, int64_t n) {
+        for (int64_t i = 0; i < n; ++i) dst[dst_off + i] = half_bits_to_float(hblob[src_off + i]);
+    };
+    if (desc->up_w >= 0) {
+        std::vector<uint16_t> w(256 * 128);
+        std::vector<float> b(256);
+        copy_mat(w, 0, desc->up_w, 256, 128, 128);
+        copy_bias(b, 0, desc->up_b, 256);
+        if ((rc = upload(st, (uint16_t**)&st->up_w, w)) || (rc = upload(st, &st->up_b, b))) return fail_cleanup(rc);
+        if ((rc = make_map_2d(&st->tm_up, st->up_w, 256, 128, 256))) return fail_cleanup(rc);
+    }
+    if (desc->down_w >= 0) {
+        std::vector<uint16_t> w(128 * 256);
+        std::vector<float> b(128);
+        copy_mat(w, 0, desc->down_w, 128, 256, 256);
+        copy_bias(b, 0, desc->down_b, 128);
+        if ((rc = upload(st, (uint16_t**)&st->dn_w, w)) || (rc = upload(st, &st->dn_b, b))) return fail_cleanup(rc);
+        if ((rc = make_map_2d(&st->tm_dn, st->dn_w, 128, 256, 128))) return fail_cleanup(rc);
+    }
+    const int64_t D = desc->dim;
+    int max_experts = 1;
+    for (int i = 0; i < desc->n_blocks; ++i) {
+        FastBlock fb;
+        fb.d = desc->blocks[i];
+        if (fb.d.kind == PRISM_BLOCK_MOE) {
+            fb.moe_index = st->n_moe++;
+            const int E = fb.d.n_experts;
+            max_experts = std::max(max_experts, E);
+            std::vector<uint16_t> w1((size_t)E * D * D), w2((size_t)E * D * D);
+            std::vector<float> b1((size_t)E * D), b2((size_t)E * D);
+            for (int e = 0; e < E; ++e) {
+                const int64_t eo = (int64_t)e * fb.d.expert_stride;
+                copy_mat(w1, (size_t)e * D * D, fb.d.expert_w1 + eo, D, D, D);
+                copy_mat(w2, (size_t)e * D * D, fb.d.expert_w2 + eo, D, D, D);
+                copy_bias(b1, (size_t)e * D, fb.d.expert_b1 + eo, D);
+                copy_bias(b2, (size_t)e * D, fb.d.expert_b2 + eo, D);
+            }
+            if ((rc = upload(st, (uint16_t**)&fb.w1, w1)) || (rc = upload(st, (uint16_t**)&fb.w2, w2)) ||
+                (rc = upload(st, &fb.b1, b1)) || (rc = upload(st, &fb.b2, b2)))
+                return fail_cleanup(rc);
+            if ((rc = make_map_2d(&fb.tm_w1, fb.w1, (uint64_t)E * D, D, 256)) ||
+                (rc = make_map_2d(&fb.tm_w2, fb.w2, (uint64_t)E * D, D, 256)))
+                return fail_cleanup(rc);
+        } else if (st->tc) {
+            const int64_t Hd = fb.d.ffn_hidden;
+            std::vector<uint16_t> w1((size_t)Hd * D), w2((size_t)D * Hd);
+            std::vector<float> b1(Hd), b2(D);
+            copy_mat(w1, 0, fb.d.ffn_w1, Hd, D, D);
+            copy_mat(w2, 0, fb.d.ffn_w2, D, Hd, Hd);
+            copy_bias(b1, 0, fb.d.ffn_b1, Hd);
+            copy_bias(b2, 0, fb.d.ffn_b2, D);
+            if ((rc = upload(st, (uint16_t**)&fb.w1, w1)) || (rc = upload(st, (uint16_t**)&fb.w2, w2)) ||
+                (rc = upload(st, &fb.b1, b1)) || (rc = upload(st, &fb.b2, b2)))
+                return fail_cleanup(rc);
+            if ((rc = make_map_2d(&fb.tm_w1, fb.w1, Hd, D, 256)) || (rc = make_map_2d(&fb.tm_w2, fb.w2, D, Hd, 256)))
+                return fail_cleanup(rc);
+        }
+        st->blocks.push_back(fb);
+    }
+    // workspace
+    if ((rc = dev_alloc(st, &st->act_a, rows * D)) || (rc = dev_alloc(st, &st->act_b, rows * D)) ||
+        (rc = dev_alloc(st, &st->act_y, rows * D)) || (rc = dev_alloc(st, &st->assign_ws, rows)) ||
+        (rc = dev_alloc(st, &st->counts, 256)) || (rc = dev_alloc(st, &st->offsets, 256)) ||
+        (rc = dev_alloc(st, &st->cursor, 256)) || (rc = dev_alloc(st, &st->perm, rows)) ||
+        (rc = dev_alloc(st, &st->n_tiles, 1)) || (rc = dev_alloc(st, &st->tiles, rows / 128 + 256 + 1)) ||
+        (rc = dev_alloc(st, &st->err, 1)))
+        return fail_cleanup(rc);
+    if (cudaMemset(st->counts, 0, 256 * 4) != cudaSuccess || cudaMemset(st->err, 0, 4) != cudaSuccess)
+        return fail_cleanup(fail(PRISM_E_CUDA, "workspace memset failed"));
+    if (st->tc) {
+        if ((rc = make_map_2d(&st->tm_act_a, st->act_a, rows, D, 128)) ||
+            (rc = make_map_2d(&st->tm_act_b, st->act_b, rows, D, 128)) ||
+            (rc = make_map_2d(&st->tm_act_y, st->act_y, rows, D, 128)))
+            return fail_cleanup(rc);
+    }
+    if (cudaDeviceSynchronize() != cudaSuccess) return fail_cleanup(fail(PRISM_E_CUDA, "stack upload failed"));
+    *out = st;
+    return PRISM_OK;
+}
+
+extern "C" int prism_stack_destroy(prism_stack* st) {
+    if (!st) return PRISM_OK;
+    DeviceGuard g(st->ctx->device);
+    cudaDeviceSynchronize();
+    free_stack(st);
+    delete st;
+    return PRISM_OK;
+}
+
+extern "C" int prism_stack_tokens_per_frame(const prism_stack* st) { return st ? st->T : 0; }
+
+extern "C" int prism_stack_launch_count(const prism_stack* st, int frames) {
+    if (!st || frames <= 0) return 0;
+    int n = (st->desc.up_w >= 0 ? 1 : 0) + (st->desc.down_w >= 0 ? 1 : 0);
+    for (const auto& b : st->blocks) n += b.d.kind == PRISM_BLOCK_MOE ? 5 : 2;
+    if (st->desc.down_w < 0 && st->blocks.empty()) n += 1;  // plain copy
+    return n;
+}
+
+extern "C" int prism_stack_status(prism_stack* st, void* stream) {
+    if (!st) return fail(PRISM_E_ARG, "prism_stack_status: NULL");
+    DeviceGuard g(st->ctx->device);
+    uint32_t e = 0;
+    CUDA_TRY(cudaMemcpyAsync(&e, st->err, 4, cudaMemcpyDeviceToHost, as_stream(stream)));
+    CUDA_TRY(cudaStreamSynchronize(as_stream(stream)));
+    CUDA_TRY(cudaMemsetAsync(st->err, 0, 4, as_stream(stream)));
+    CUDA_TRY(cudaStreamSynchronize(as_stream(stream)));
+    if (e & ERR_TIMEOUT) return fail(PRISM_E_TIMEOUT, "a device-side wait timed out (error word 0x%x)", e);
+    if (e & ERR_ROUTE) return fail(PRISM_E_RANGE, "routing invariant failed (error word 0x%x)", e);
+    return PRISM_OK;
+}
+
+extern "C" int prism_stack_forward(prism_stack* st, const void* in, void* out, int frames, int32_t* assign,
+                                   void* stream) {
+    if (!st || !in || !out) return fail(PRISM_E_ARG, "prism_stack_forward: NULL argument");
+    if (frames < 0 || frames > st->max_frames)
+        return fail(PRISM_E_RANGE, "prism_stack_forward: frames %d (max %d)", frames, st->max_frames);
+    if (frames == 0) return PRISM_OK;
+    if (in == out) return fail(PRISM_E_ARG, "prism_stack_forward: out aliases in");
+    DeviceGuard g(st->ctx->device);
+    cudaStream_t s = as_stream(stream);
+    const prism_stack_desc& d = st->desc;
+    const int D = d.dim, T = st->T;
+    const int rows = T * frames;
+    const int grid = st->ctx->sm_count;
+    int rc;
+
+    const __half* cur = static_cast<const __half*>(in);
+    const CUtensorMap* cur_map = nullptr;
+    CUtensorMap tm_in;
+    if (d.up_w >= 0) {
+        if ((rc = make_map_2d(&tm_in, in, rows, 128, 128))) return rc;
+        FfnArgs a{};
+        a.x = static_cast<const __half*>(in);
+        a.y = st->act_a;
+        a.n_rows = rows;
+        a.b1 = st->up_b;
+        a.err = st->err;
+        KernelTimer kt(st, s, PRISM_K_PROJ_UP);
+        CUDA_TRY(launch_ffn_proj_up(a, tm_in, st->tm_up, std::min(grid, (rows + 127) / 128), s));
+        cur = st->act_a;
+        cur_map = &st->tm_act_a;
+    }
+    const int nb = (int)st->blocks.size();
+    for (int bi = 0; bi < nb; ++bi) {
+        const FastBlock& b = st->blocks[bi];
+        const bool last = bi == nb - 1;
+        // output of this block: the caller's buffer if nothing follows, else a ping-pong buffer
+        __half* nxt;
+        const CUtensorMap* nxt_map;
+        if (last && d.down_w < 0) {
+            nxt = static_cast<__half*>(out);
+            nxt_map = nullptr;
+        } else if (cur == st->act_a) {
+            nxt = st->act_b;
+            nxt_map = &st->tm_act_b;
+        } else {
+            nxt = st->act_a;
+            nxt_map = &st->tm_act_a;
+        }
+        // attention: x (cur) -> y (act_y)
+        AttnArgs at;
+        at.weights = st->blob;
+        at.x = cur;
+        // dim 128 runs the CUDA-core dense FFN in place on the block output
+        at.y = (b.d.kind == PRISM_BLOCK_DENSE && !st->tc) ? nxt : st->act_y;
+        at.frame_stride = (int64_t)T * D;
+        at.qkv_w = b.d.qkv_w;
+        at.qkv_b = b.d.qkv_b;
+        at.out_w = b.d.out_w;
+        at.out_b = b.d.out_b;
+        at.W = d.spatial_w;
+        at.H = d.spatial_h;
+        at.n_tokens = T;
+        at.scale = 0.1767766953f;
+        {
+            KernelTimer kt(st, s, PRISM_K_ATTN);
+            CUDA_TRY(launch_attn_window(at, D, frames, s));
+        }
+        if (b.d.kind == PRISM_BLOCK_MOE) {
+            int32_t* asg = assign ? assign + (size_t)b.moe_index * rows : st->assign_ws;
+            RouterArgs ra;
+            ra.weights = st->blob;
+            ra.x = st->act_y;
+            ra.assign = asg;
+            ra.counts = st->counts;
+            ra.router_w = b.d.router_w;
+            ra.router_b = b.d.router_b;
+            ra.n_experts = b.d.n_experts;
+            ra.n_tokens = rows;
+            {
+                KernelTimer kt(st, s, PRISM_K_ROUTER);
+                CUDA_TRY(launch_router(ra, D, s));
+            }
+            RoutePlanArgs rp;
+            rp.counts = st->counts;
+            rp.counts_out = nullptr;
+            rp.offsets = st->offsets;
+            rp.cursor = st->cursor;
+            rp.tiles = st->tiles;
+            rp.n_tiles = st->n_tiles;
+            rp.n_experts = b.d.n_experts;
+            rp.n_tokens = rows;
+            rp.err = st->err;
+            RouteScatterArgs rs;
+            rs.assign = asg;
+            rs.offsets = st->offsets;
+            rs.cursor = st->cursor;
+            rs.perm = st->perm;
+            rs.n_experts = b.d.n_experts;
+            rs.n_tokens = rows;
+            rs.err = st->err;
+            {
+                KernelTimer kt(st, s, PRISM_K_ROUTE);
+                CUDA_TRY(launch_route(rp, rs, s));
+            }
+            FfnArgs fa{};
+            fa.x = st->act_y;
+            fa.y = nxt;
+            fa.perm = st->perm;
+            fa.tiles = st->tiles;
+            fa.n_tiles = st->n_tiles;
+            fa.b1 = b.b1;
+            fa.b2 = b.b2;
+            fa.err = st->err;
+            KernelTimer kt(st, s, PRISM_K_EXPERT);
+            CUDA_TRY(launch_ffn_expert256(fa, b.tm_w1, b.tm_w2, std::min(grid, rows / 128 + b.d.n_experts), s));
+        } else if (st->tc) {
+            FfnArgs fa{};
+            fa.x = st->act_y;
+            fa.y = nxt;
+            fa.n_rows = rows;
+            fa.b1 = b.b1;
+            fa.b2 = b.b2;
+            fa.err = st->err;
+            KernelTimer kt(st, s, PRISM_K_DENSE_FFN);
+            CUDA_TRY(launch_ffn_dense256(fa, st->tm_act_y, b.tm_w1, b.tm_w2, b.d.ffn_hidden / 256,
+                                         std::min(grid, (rows + 127) / 128), s));
+        } else {
+            DenseFfnArgs f;
+            f.weights = st->blob;
+            f.io = nxt;
+            f.w1 = b.d.ffn_w1;
+            f.b1 = b.d.ffn_b1;
+            f.w2 = b.d.ffn_w2;
+            f.b2 = b.d.ffn_b2;
+            f.hidden = b.d.ffn_hidden;
+            f.chunk = b.d.ffn_chunk;
+            f.n_tokens = rows;
+            KernelTimer kt(st, s, PRISM_K_DENSE_FFN);
+            CUDA_TRY(launch_dense_ffn(f, D, s));
+        }
+        cur = nxt;
+        cur_map = nxt_map;
+    }
+    if (d.down_w >= 0) {
+        const CUtensorMap* xm = cur_map;
+        CUtensorMap tm_cur;
+        if (!xm) {  // no blocks and no up adapter: x is the caller's input
+            if ((rc = make_map_2d(&tm_cur, cur, rows, 256, 128))) return rc;
+            xm = &tm_cur;
+        }
+        FfnArgs a{};
+        a.x = cur;
+        a.y = static_cast<__half*>(out);
+        a.n_rows = rows;
+        a.b1 = st->dn_b;
+        a.err = st->err;
+        KernelTimer kt(st, s, PRISM_K_PROJ_DOWN);
+        CUDA_TRY(launch_ffn_proj_down(a, *xm, st->tm_dn, std::min(grid, (rows + 127) / 128), s));
+    } else if (nb == 0) {
+        KernelTimer kt(st, s, PRISM_K_COPY);
+        CUDA_TRY(cudaMemcpyAsync(out, cur, (size_t)rows * D * 2, cudaMemcpyDeviceToDevice, s));
+    }
+    return PRISM_OK;
+}
+
+extern "C" int prism_stack_profile(prism_stack* st, int enable) {
+    if (!st) return fail(PRISM_E_ARG, "prism_stack_profile: NULL");
+    st->profiling = enable != 0;
+    return PRISM_OK;
+}
+
+extern "C" int prism_stack_profile_read(prism_stack* st, double* ms, int64_t* launches, int n_kinds) {
+    if (!st || !ms || !launches || n_kinds < 0) return fail(PRISM_E_ARG, "prism_stack_profile_read: NULL");
+    DeviceGuard g(st->ctx->device);
+    for (int k = 0; k < n_kinds; ++k) {
+        ms[k] = 0.0;
+        launches[k] = 0;
+    }
+    if (st->ev_used) CUDA_TRY(cudaEventSynchronize(st->ev_pool[st->ev_used - 1]));
+    for (size_t i = 0; i < st->ev_kind.size(); ++i) {
+        float t = 0.0f;
+        CUDA_TRY(cudaEventElapsedTime(&t, st->ev_pool[2 * i], st->ev_pool[2 * i + 1]));
+        const int k = st->ev_kind[i];
+        if (k < n_kinds) {
+            ms[k] += t;
+            launches[k] += 1;
+        }
+    }
+    st->ev_used = 0;
+    st->ev_kind.clear();
+    return PRISM_OK;
+}

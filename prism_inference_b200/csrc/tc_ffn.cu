@@ -1,0 +1,417 @@
+// tc_ffn.cu - tcgen05 row-tile GEMM chain for sm_100a.
+//
+// One persistent CTA per SM walks 128-row tiles.  Per tile:
+//   GEMM1  acc1[128 x HID] = A[128 x KIN] . W1^T         (TMEM, fp32)
+//   epi1   h = act(fp16(acc1 + b1))  -> fp16 tile H in shared memory (K-major SW128)
+//   GEMM2  acc2[128 x NOUT] = H . W2^T                     (TMEM, fp32)   [two-GEMM modes]
+//   epi2   out = fp16(fp16(acc2 + b2) + x)  (expert)  or the chunked dense rule
+// The rounding points are those of the reference shaders: every coopVecMatMulAddNV
+// result is rounded to fp16 once (acc + bias), GELU is evaluated in fp32 on that
+// fp16 value and rounded again, the residual add is an fp16 add.
+//
+// Warp roles (320 threads):
+//   warp 0     producer: A rows (cp.async gather for experts, TMA otherwise) and the
+//              W1/W2 K-chunks (TMA, 128B swizzle) through a STAGES-deep ring
+//   warp 1     TMEM allocation + single-thread tcgen05.mma issue
+//   warps 2-9  epilogue: warp w reads TMEM lanes 32*(w%4).. (its rows) and one half
+//              of the columns
+// Expert mode replaces the reference's per-expert early-return dispatch loop
+// (moe_expert_skip.comp.glsl:25-54 dispatched N times by prism_moe_bench.cpp:428-436):
+// the tiles of all experts run in one launch, each tile holding up to 128 tokens of
+// one expert (the permutation built by route_kernels.cu), and the epilogue scatters
+// the rows back to their token positions with the residual add fused.
+#include "common.cuh"
+#include "tc_ffn.cuh"
+
+namespace prism {
+
+namespace {
+
+constexpr int kThreads = 320;
+constexpr int kEpiWarps = 8;
+
+template <int MODE, int KIN, int HID, int NOUT>
+struct FfnCfg {
+    static constexpr bool kTwoGemm = (MODE == FFN_EXPERT || MODE == FFN_DENSE);
+    static constexpr int kA = KIN * 128 * 2;                    // A tile bytes
+    static constexpr int kH = kTwoGemm ? HID * 128 * 2 : 0;     // H tile bytes
+    static constexpr int kWRows = HID > NOUT ? HID : NOUT;      // rows of one W K-chunk
+    static constexpr int kStage = kWRows * 128;                 // bytes of one ring stage
+    static constexpr int kStages = kTwoGemm ? 3 : 4;
+    static constexpr int kTmemCols = kTwoGemm ? 512 : 256;
+    static constexpr int kAcc2 = 256;                           // TMEM column of acc2
+    static constexpr int kBarBytes = 256;
+    static constexpr int kSmem = kA + kH + kStages * kStage + kBarBytes + 1024;  // + alignment slack
+};
+
+struct Bars {
+    uint64_t full[4], empty[4];
+    uint64_t a_full, a_empty, acc1_full, acc1_empty, h_full, acc2_full, acc2_empty, drain;
+    uint32_t tmem_base;
+    int abort;
+};
+
+template <int MODE, int KIN, int HID, int NOUT>
+__global__ void __launch_bounds__(kThreads, 1)
+    ffn_tc_kernel(const FfnArgs a, const __grid_constant__ CUtensorMap tm_x,
+                  const __grid_constant__ CUtensorMap tm_w1, const __grid_constant__ CUtensorMap tm_w2,
+                  int n_chunks) {
+    using Cfg = FfnCfg<MODE, KIN, HID, NOUT>;
+    extern __shared__ unsigned char smem_raw[];
+    // 1024-byte alignment for the swizzled operand tiles
+    unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    unsigned char* sA = smem;
+    unsigned char* sH = sA + Cfg::kA;
+    unsigned char* sW = sH + Cfg::kH;
+    Bars* bars = reinterpret_cast<Bars*>(sW + Cfg::kStages * Cfg::kStage);
+    volatile int* abort = &bars->abort;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n_tiles = MODE == FFN_EXPERT ? *a.n_tiles : (a.n_rows + 127) / 128;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < Cfg::kStages; ++s) {
+            mbar_init(&bars->full[s], 1);
+            mbar_init(&bars->empty[s], 1);
+        }
+        mbar_init(&bars->a_full, MODE == FFN_EXPERT ? 32 : 1);
+        mbar_init(&bars->a_empty, Cfg::kTwoGemm ? kEpiWarps : 1);
+        mbar_init(&bars->acc1_full, 1);
+        mbar_init(&bars->acc1_empty, kEpiWarps);
+        mbar_init(&bars->h_full, kEpiWarps);
+        mbar_init(&bars->acc2_full, 1);
+        mbar_init(&bars->acc2_empty, kEpiWarps);
+        mbar_init(&bars->drain, 1);
+        bars->abort = 0;
+        fence_barrier_init();
+        fence_async_shared();
+    }
+    if (warp == 1) tmem_alloc(&bars->tmem_base, Cfg::kTmemCols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = bars->tmem_base;
+
+    if (warp == 0) {
+        // ===================== producer =====================
+        if (lane == 0) {
+            prefetch_tmap(&tm_w1);
+            if (Cfg::kTwoGemm) prefetch_tmap(&tm_w2);
+            if (MODE != FFN_EXPERT) prefetch_tmap(&tm_x);
+        }
+        int stage = 0;
+        uint32_t phase = 0;
+        uint32_t it = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, ++it) {
+            int e = 0, start = 0, rows = 128;
+            if (MODE == FFN_EXPERT) {
+                const ExpertTile t = a.tiles[tile];
+                e = t.expert;
+                start = t.start;
+                rows = t.rows;
+            } else {
+                start = tile * 128;
+            }
+            // --- A rows (wait until the previous tile released the A buffer)
+            if (!mbar_wait(&bars->a_empty, (it & 1) ^ 1, abort)) { ok = false; break; }
+            if (MODE == FFN_EXPERT) {
+                const uint32_t a_base = smem_u32(sA);
+                for (int r = lane; r < 128; r += 32) {
+                    const bool valid = r < rows;
+                    const int tok = valid ? a.perm[start + r] : 0;
+                    const __half* src = a.x + (size_t)tok * KIN;
+#pragma unroll
+                    for (int kb = 0; kb < KIN / 64; ++kb)
+#pragma unroll
+                        for (int c = 0; c < 8; ++c)
+                            cp_async16(a_base + kb * 16384 + sw128_off(r, c), src + kb * 64 + c * 8, valid ? 16u : 0u);
+                }
+                cp_async_mbar_arrive(&bars->a_full);
+            } else if (lane == 0) {
+                mbar_expect_tx(&bars->a_full, Cfg::kA);
+#pragma unroll
+                for (int kb = 0; kb < KIN / 64; ++kb)
+                    tma_load_2d(smem_u32(sA + kb * 16384), &tm_x, &bars->a_full, kb * 64, start);
+            }
+            // --- weight K-chunks, in the order the MMA warp consumes them
+            for (int c = 0; c < n_chunks && ok; ++c) {
+                for (int kc = 0; kc < KIN / 64; ++kc) {  // GEMM1: W1 rows of this chunk
+                    if (!mbar_wait(&bars->empty[stage], phase ^ 1, abort)) { ok = false; break; }
+                    if (lane == 0) {
+                        mbar_expect_tx(&bars->full[stage], HID * 128);
+                        const int row = MODE == FFN_EXPERT ? e * HID : c * HID;
+                        tma_load_2d(smem_u32(sW + stage * Cfg::kStage), &tm_w1, &bars->full[stage], kc * 64, row);
+                    }
+                    if (++stage == Cfg::kStages) { stage = 0; phase ^= 1; }
+                }
+                if (!Cfg::kTwoGemm) continue;
+                for (int kc = 0; kc < HID / 64 && ok; ++kc) {  // GEMM2: W2 columns of this chunk
+                    if (!mbar_wait(&bars->empty[stage], phase ^ 1, abort)) { ok = false; break; }
+                    if (lane == 0) {
+                        mbar_expect_tx(&bars->full[stage], NOUT * 128);
+                        const int col = (MODE == FFN_EXPERT ? 0 : c * HID) + kc * 64;
+                        const int row = MODE == FFN_EXPERT ? e * NOUT : 0;
+                        tma_load_2d(smem_u32(sW + stage * Cfg::kStage), &tm_w2, &bars->full[stage], col, row);
+                    }
+                    if (++stage == Cfg::kStages) { stage = 0; phase ^= 1; }
+                }
+            }
+            __syncwarp();
+        }
+        asm volatile("cp.async.wait_all;" ::: "memory");
+    } else if (warp == 1) {
+        // ===================== MMA issuer =====================
+        constexpr uint32_t idesc1 = idesc_f16(128, HID);
+        constexpr uint32_t idesc2 = idesc_f16(128, NOUT);
+        int stage = 0;
+        uint32_t phase = 0;
+        uint32_t it = 0;
+        uint32_t chunk_it = 0;  // counts (tile, chunk) pairs for the acc barriers
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, ++it) {
+            if (!mbar_wait(&bars->a_full, it & 1, abort)) { ok = false; break; }
+            fence_async_shared();
+            tc_fence_after();
+            for (int c = 0; c < n_chunks && ok; ++c, ++chunk_it) {
+                // GEMM1 -> acc1 (columns [0, HID))
+                if (!mbar_wait(&bars->acc1_empty, (chunk_it & 1) ^ 1, abort)) { ok = false; break; }
+                tc_fence_after();
+                for (int kc = 0; kc < KIN / 64; ++kc) {
+                    if (!mbar_wait(&bars->full[stage], phase, abort)) { ok = false; break; }
+                    tc_fence_after();
+                    if (lane == 0) {
+                        const uint32_t a0 = smem_u32(sA + kc * 16384);
+                        const uint32_t b0 = smem_u32(sW + stage * Cfg::kStage);
+#pragma unroll
+                        for (int k = 0; k < 4; ++k)
+                            mma_f16_ss(tmem, sdesc(a0 + k * 32, SW128), sdesc(b0 + k * 32, SW128), idesc1,
+                                       (kc | k) != 0);
+                        mma_commit(&bars->empty[stage]);
+                    }
+                    __syncwarp();
+                    if (++stage == Cfg::kStages) { stage = 0; phase ^= 1; }
+                }
+                if (!ok) break;
+                if (lane == 0) {
+                    mma_commit(&bars->acc1_full);
+                    if (!Cfg::kTwoGemm) mma_commit(&bars->a_empty);
+                }
+                __syncwarp();
+                if (!Cfg::kTwoGemm) continue;
+                // GEMM2 -> acc2 (columns [256, 256 + NOUT)), A = H from the epilogue
+                if (!mbar_wait(&bars->h_full, chunk_it & 1, abort)) { ok = false; break; }
+                if (!mbar_wait(&bars->acc2_empty, (chunk_it & 1) ^ 1, abort)) { ok = false; break; }
+                fence_async_shared();
+                tc_fence_after();
+                for (int kc = 0; kc < HID / 64; ++kc) {
+                    if (!mbar_wait(&bars->full[stage], phase, abort)) { ok = false; break; }
+                    tc_fence_after();
+                    if (lane == 0) {
+                        const uint32_t a0 = smem_u32(sH + kc * 16384);
+                        const uint32_t b0 = smem_u32(sW + stage * Cfg::kStage);
+#pragma unroll
+                        for (int k = 0; k < 4; ++k)
+                            mma_f16_ss(tmem + Cfg::kAcc2, sdesc(a0 + k * 32, SW128), sdesc(b0 + k * 32, SW128),
+                                       idesc2, (kc | k) != 0);
+                        mma_commit(&bars->empty[stage]);
+                    }
+                    __syncwarp();
+                    if (++stage == Cfg::kStages) { stage = 0; phase ^= 1; }
+                }
+                if (!ok) break;
+                if (lane == 0) mma_commit(&bars->acc2_full);
+                __syncwarp();
+            }
+        }
+        // every issued MMA has completed before TMEM is released
+        if (lane == 0) mma_commit(&bars->drain);
+        __syncwarp();
+        mbar_wait(&bars->drain, 0, abort);
+    } else {
+        // ===================== epilogue =====================
+        const int quad = warp & 3;               // TMEM lanes 32*quad .. +31
+        const int half = (warp - 2) >> 2;        // column half
+        const int row = quad * 32 + lane;        // tile row of this thread
+        const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
+        uint32_t it = 0, chunk_it = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, ++it) {
+            int e = 0, start = 0, rows = 128;
+            if (MODE == FFN_EXPERT) {
+                const ExpertTile t = a.tiles[tile];
+                e = t.expert;
+                start = t.start;
+                rows = t.rows;
+            } else {
+                start = tile * 128;
+                rows = min(128, a.n_rows - start);
+            }
+            const bool row_valid = row < rows;
+            const int out_row = MODE == FFN_EXPERT ? (row_valid ? a.perm[start + row] : 0) : start + row;
+            // fp16 running sum of the dense FFN chunk outputs (attention_windowed_d256.comp.glsl:167-168)
+            uint32_t accum[MODE == FFN_DENSE ? NOUT / 4 : 1];
+            if (MODE == FFN_DENSE) {
+#pragma unroll
+                for (int i = 0; i < NOUT / 4; ++i) accum[i] = 0u;
+            }
+            for (int c = 0; c < n_chunks && ok; ++c, ++chunk_it) {
+                // ---- epi1: acc1 -> bias -> fp16 -> activation -> fp16
+                if (!mbar_wait(&bars->acc1_full, chunk_it & 1, abort)) { ok = false; break; }
+                tc_fence_after();
+                const float* b1 = a.b1 + (size_t)e * HID * n_chunks + c * HID;
+                constexpr int kCols1 = HID / 2;
+#pragma unroll 1
+                for (int g = 0; g < kCols1 / 16; ++g) {
+                    const int col0 = half * kCols1 + g * 16;
+                    uint32_t r[16];
+                    tmem_ld16(tmem + lane_addr + col0, r);
+                    tmem_ld_wait();
+                    uint32_t packed[8];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        float v0 = rh(__fadd_rn(__uint_as_float(r[2 * j]), b1[col0 + 2 * j]));
+                        float v1 = rh(__fadd_rn(__uint_as_float(r[2 * j + 1]), b1[col0 + 2 * j + 1]));
+                        if (MODE == FFN_EXPERT || MODE == FFN_DENSE) {
+                            v0 = gelu_f32(v0);
+                            v1 = gelu_f32(v1);
+                        } else if (MODE == FFN_PROJ_UP) {
+                            v0 = v0 < 0.0f ? 0.0f : v0;
+                            v1 = v1 < 0.0f ? 0.0f : v1;
+                        }
+                        packed[j] = pack_h2(v0, v1);
+                    }
+                    if (Cfg::kTwoGemm) {
+                        // H tile, K-major SW128: column col0 -> K-block col0/64, chunk (col0%64)/8
+                        unsigned char* blk = sH + (col0 >> 6) * 16384;
+                        const int ch = (col0 & 63) >> 3;
+                        *reinterpret_cast<uint4*>(blk + sw128_off(row, ch)) =
+                            make_uint4(packed[0], packed[1], packed[2], packed[3]);
+                        *reinterpret_cast<uint4*>(blk + sw128_off(row, ch + 1)) =
+                            make_uint4(packed[4], packed[5], packed[6], packed[7]);
+                    } else if (row_valid) {
+                        uint4* dst = reinterpret_cast<uint4*>(a.y + (size_t)out_row * NOUT + col0);
+                        dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+                        dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bars->acc1_empty);
+                if (!Cfg::kTwoGemm) continue;
+                fence_async_shared();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bars->h_full);
+
+                // ---- epi2: acc2 -> bias -> fp16 -> (+ residual) -> store
+                if (!mbar_wait(&bars->acc2_full, chunk_it & 1, abort)) { ok = false; break; }
+                tc_fence_after();
+                const float* b2 = a.b2 + (size_t)e * NOUT;
+                const bool last = (c == n_chunks - 1);
+                constexpr int kCols2 = NOUT / 2;
+#pragma unroll
+                for (int g = 0; g < kCols2 / 16; ++g) {
+                    const int col0 = half * kCols2 + g * 16;
+                    uint32_t r[16];
+                    tmem_ld16(tmem + Cfg::kAcc2 + lane_addr + col0, r);
+                    tmem_ld_wait();
+                    float part[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) part[j] = rh(__fadd_rn(__uint_as_float(r[j]), b2[col0 + j]));
+                    if (MODE == FFN_DENSE) {
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            const uint32_t prev = accum[g * 8 + j];
+                            accum[g * 8 + j] = pack_h2(__fadd_rn(lo_h2f(prev), part[2 * j]),
+                                                       __fadd_rn(hi_h2f(prev), part[2 * j + 1]));
+                        }
+                    }
+                    if (!last) continue;
+                    // residual x from the A tile (same row, column col0 of K-block col0/64)
+                    const unsigned char* ablk = sA + (col0 >> 6) * 16384;
+                    const int ch = (col0 & 63) >> 3;
+                    const uint4 x0 = *reinterpret_cast<const uint4*>(ablk + sw128_off(row, ch));
+                    const uint4 x1 = *reinterpret_cast<const uint4*>(ablk + sw128_off(row, ch + 1));
+                    const uint32_t xs[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+                    uint32_t packed[8];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        float z0, z1;
+                        if (MODE == FFN_DENSE) {
+                            // out = h(acc - (n_chunks-1)*b2 + y)   (attention_windowed_d256.comp.glsl:171-177)
+                            const float corr = (float)(n_chunks - 1);
+                            const uint32_t acc = accum[g * 8 + j];
+                            z0 = __fadd_rn(__fsub_rn(lo_h2f(acc), __fmul_rn(corr, b2[col0 + 2 * j])), lo_h2f(xs[j]));
+                            z1 = __fadd_rn(__fsub_rn(hi_h2f(acc), __fmul_rn(corr, b2[col0 + 2 * j + 1])),
+                                           hi_h2f(xs[j]));
+                        } else {
+                            // z = h(r + y)   (moe_expert_skip.comp.glsl:52)
+                            z0 = __fadd_rn(part[2 * j], lo_h2f(xs[j]));
+                            z1 = __fadd_rn(part[2 * j + 1], hi_h2f(xs[j]));
+                        }
+                        packed[j] = pack_h2(z0, z1);
+                    }
+                    if (row_valid) {
+                        uint4* dst = reinterpret_cast<uint4*>(a.y + (size_t)out_row * NOUT + col0);
+                        dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+                        dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bars->acc2_empty);
+            }
+            if (Cfg::kTwoGemm && ok) {
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bars->a_empty);  // residual read done
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (bars->abort) {
+        if (threadIdx.x == 0) atomicOr(a.err, ERR_TIMEOUT);
+        // let any bulk copy still in flight land before the CTA exits
+        const uint64_t t0 = globaltimer();
+        while (globaltimer() - t0 < 1000000ull) {
+        }
+    }
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, Cfg::kTmemCols);
+    }
+}
+
+template <int MODE, int KIN, int HID, int NOUT>
+cudaError_t launch_ffn(const FfnArgs& a, const CUtensorMap& tx, const CUtensorMap& t1, const CUtensorMap& t2,
+                       int n_chunks, int grid, cudaStream_t s) {
+    using Cfg = FfnCfg<MODE, KIN, HID, NOUT>;
+    auto k = ffn_tc_kernel<MODE, KIN, HID, NOUT>;
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
+    if (e != cudaSuccess) return e;
+    if (grid <= 0) return cudaSuccess;
+    k<<<grid, kThreads, Cfg::kSmem, s>>>(a, tx, t1, t2, n_chunks);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_ffn_expert256(const FfnArgs& a, const CUtensorMap& w1, const CUtensorMap& w2, int grid,
+                                 cudaStream_t s) {
+    return launch_ffn<FFN_EXPERT, 256, 256, 256>(a, w1, w1, w2, 1, grid, s);
+}
+cudaError_t launch_ffn_dense256(const FfnArgs& a, const CUtensorMap& x, const CUtensorMap& w1, const CUtensorMap& w2,
+                                int n_chunks, int grid, cudaStream_t s) {
+    return launch_ffn<FFN_DENSE, 256, 256, 256>(a, x, w1, w2, n_chunks, grid, s);
+}
+cudaError_t launch_ffn_proj_up(const FfnArgs& a, const CUtensorMap& x, const CUtensorMap& w, int grid,
+                               cudaStream_t s) {
+    return launch_ffn<FFN_PROJ_UP, 128, 256, 256>(a, x, w, w, 1, grid, s);
+}
+cudaError_t launch_ffn_proj_down(const FfnArgs& a, const CUtensorMap& x, const CUtensorMap& w, int grid,
+                                 cudaStream_t s) {
+    return launch_ffn<FFN_PROJ_DOWN, 256, 128, 128>(a, x, w, w, 1, grid, s);
+}
+
+}  // namespace prism

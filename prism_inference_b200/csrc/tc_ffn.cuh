@@ -1,0 +1,44 @@
+// tc_ffn.cuh - argument block of the tcgen05 row-tile GEMM-chain kernel.
+#pragma once
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace prism {
+
+// Modes of the row-tile GEMM chain.
+enum FfnMode : int {
+    FFN_EXPERT = 0,     // gathered rows of one expert: x + W2 gelu(W1 x + b1) + b2, scattered back
+    FFN_PROJ_UP = 1,    // relu(W x + b), 128 -> 256
+    FFN_PROJ_DOWN = 2,  // W x + b, 256 -> 128
+    FFN_DENSE = 3       // dense FFN of width NCH*HID, fp16 accumulation of NCH chunk outputs
+};
+
+// One tile of the grouped expert GEMM: rows perm[start .. start+rows) of expert e.
+struct ExpertTile {
+    int expert, start, rows, pad;
+};
+
+struct FfnArgs {
+    const __half* x;           // input rows [n_rows][KIN] fp16
+    __half* y;                 // output rows [n_rows][NOUT] fp16 (may alias x only row-wise in place)
+    const int32_t* perm;       // FFN_EXPERT: sorted row -> token
+    const ExpertTile* tiles;   // FFN_EXPERT: tile list
+    const int32_t* n_tiles;    // FFN_EXPERT: device tile count
+    int n_rows;                // other modes: number of rows
+    const float* b1;           // fp32 biases [experts][HID*NCH]
+    const float* b2;           // fp32 biases [experts][NOUT]
+    uint32_t* err;             // device error word
+};
+
+cudaError_t launch_ffn_expert256(const FfnArgs& a, const CUtensorMap& w1, const CUtensorMap& w2, int grid,
+                                 cudaStream_t s);
+cudaError_t launch_ffn_dense256(const FfnArgs& a, const CUtensorMap& x, const CUtensorMap& w1, const CUtensorMap& w2,
+                                int n_chunks, int grid, cudaStream_t s);
+cudaError_t launch_ffn_proj_up(const FfnArgs& a, const CUtensorMap& x, const CUtensorMap& w, int grid,
+                               cudaStream_t s);
+cudaError_t launch_ffn_proj_down(const FfnArgs& a, const CUtensorMap& x, const CUtensorMap& w, int grid,
+                                 cudaStream_t s);
+
+}  // namespace prism

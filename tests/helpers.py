@@ -1,0 +1,32 @@
+"""Shared helpers of the parity tests: tolerances of BASELINE.json's north star and
+the comparison / routing-agreement statistics."""
+from __future__ import annotations
+
+import numpy as np
+
+MAX_ABS = 2e-2       # max |gpu - oracle| over fp16 outputs
+REL_L2 = 1e-3        # ||gpu - oracle||_2 / ||oracle||_2
+TIE_MARGIN = 1e-3    # routing may differ only where the oracle's top-2 logit margin is below this
+
+
+def err_stats(got, ref):
+    g = np.asarray(got, dtype=np.float32).ravel()
+    r = np.asarray(ref, dtype=np.float32).ravel()
+    d = np.abs(g - r)
+    rel = float(np.linalg.norm(g - r) / max(np.linalg.norm(r), 1e-30))
+    return float(d.max()) if d.size else 0.0, rel, int((g != r).sum())
+
+
+def assert_close(got, ref, what="", max_abs=MAX_ABS, rel_l2=REL_L2):
+    m, rel, nd = err_stats(got, ref)
+    assert np.isfinite(np.asarray(got, dtype=np.float32)).all(), f"{what}: non-finite values"
+    assert m <= max_abs and rel <= rel_l2, f"{what}: max_abs {m:.3g} rel_l2 {rel:.3g} ({nd} differ)"
+    return m, rel, nd
+
+
+def routing_agreement(gpu_assign, ref_assign, margin):
+    """(hard mismatches, tie mismatches): a mismatch is a tie when the oracle's top-2
+    margin is below TIE_MARGIN."""
+    diff = np.asarray(gpu_assign) != np.asarray(ref_assign)
+    ties = np.asarray(margin) < TIE_MARGIN
+    return int((diff & ~ties).sum()), int((diff & ties).sum())

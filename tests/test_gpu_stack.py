@@ -1,0 +1,121 @@
+"""The fast path (prism_stack_forward: tcgen05 adapters, route + grouped expert
+GEMM) against the oracle stack.
+
+Routing: the oracle follows the GPU's choice only where its own top-2 margin is
+below 1e-3 (a tie); any other difference is a hard mismatch and fails the test.
+Ties are reported."""
+import numpy as np
+import pytest
+
+from helpers import TIE_MARGIN, assert_close
+from prism_inference_b200 import Prism, Stack, configs, layout, synth
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(ctx, L, blob, x, max_frames=None):
+    import torch
+    F = x.shape[0]
+    st = Stack(ctx, L, blob, max_frames or F)
+    xd = torch.from_numpy(x.view(np.int16)).cuda().view(torch.float16)
+    out = torch.empty((F, L.tokens, L.out_dim), dtype=torch.float16, device="cuda")
+    asg = torch.full((max(1, L.n_moe_blocks), F * L.tokens), -1, dtype=torch.int32, device="cuda")
+    st.forward(xd, out, asg)
+    torch.cuda.synchronize()
+    st.status()
+    o = out.view(torch.int16).cpu().numpy().view(np.float16)
+    a = asg.cpu().numpy()
+    st.close()
+    return o, a
+
+
+def _check(ctx, oracle, L, blob, x, what):
+    o, a = _run(ctx, L, blob, x)
+    ref, ra, stats = oracle.stack(L, blob, x, forced=a if L.n_moe_blocks else None, tie_thr=TIE_MARGIN)
+    assert stats[2] == 0, f"{what}: {stats[2]} hard routing mismatches"
+    m = assert_close(o, ref, what)
+    print(f"{what}: max_abs {m[0]:.3g} rel_l2 {m[1]:.3g}; routed {stats[0]}, followed at ties {stats[1]}, "
+          f"near-ties {stats[3]}")
+    return o, a
+
+
+def test_stack_adapters_only(prism_ctx, oracle):
+    """The two tcgen05 adapter GEMMs alone (no blocks): 128->256 ReLU, 256->128."""
+    L = layout.build_stack(256, 0, up_adapter=True, down_adapter=True)
+    blob = synth.make_blob(L)
+    x = synth.make_frames(L, 2)
+    o, _ = _run(prism_ctx, L, blob, x)
+    ref, _, _ = oracle.stack(L, blob, x)
+    assert_close(o, ref, "adapters")
+
+
+@pytest.mark.parametrize("key,n_blocks,frames", [("moe16x1", 1, 1), ("moe64x16", 2, 2), ("moe32x22skew", 2, 1),
+                                                 ("dense256x12", 2, 1), ("dense128x4", 2, 2)])
+def test_stack_matches_oracle(prism_ctx, oracle, key, n_blocks, frames):
+    cfg = configs.get(key, n_blocks=n_blocks)
+    blob = synth.make_blob(cfg.layout, router_skew=cfg.router_skew, skew_bias=cfg.skew_bias)
+    x = synth.make_frames(cfg.layout, frames)
+    _check(prism_ctx, oracle, cfg.layout, blob, x, key)
+
+
+@pytest.mark.parametrize("key", ["dense256x12", "dense128x4"])
+def test_stack_reference_ffn_widths(prism_ctx, oracle, key):
+    """The shader widths: FFN 1024 in four fp16-accumulated chunks (d256) and 512
+    unsplit (d128)."""
+    cfg = configs.get(key, reference_widths=True, n_blocks=2)
+    blob = synth.make_blob(cfg.layout)
+    x = synth.make_frames(cfg.layout, 1)
+    _check(prism_ctx, oracle, cfg.layout, blob, x, key + "-ref-widths")
+
+
+def test_headline_stack_full_depth(prism_ctx, oracle):
+    """Config 4 as benchmarked: 64 experts x 16 blocks + adapters, one frame."""
+    cfg = configs.get("moe64x16")
+    blob = synth.make_blob(cfg.layout)
+    x = synth.make_frames(cfg.layout, 1)
+    _check(prism_ctx, oracle, cfg.layout, blob, x, "moe64x16-full")
+
+
+def test_frames_are_independent_and_deterministic(prism_ctx):
+    """Frame f gives the same bits alone and inside a batch (tiles mix frames), and
+    two runs give the same bits."""
+    cfg = configs.get("moe64x16", n_blocks=3)
+    blob = synth.make_blob(cfg.layout)
+    x = synth.make_frames(cfg.layout, 4)
+    o4, a4 = _run(prism_ctx, cfg.layout, blob, x)
+    o4b, _ = _run(prism_ctx, cfg.layout, blob, x)
+    o1, a1 = _run(prism_ctx, cfg.layout, blob, x[2:3], max_frames=4)
+    assert (o4.view(np.uint16) == o4b.view(np.uint16)).all()
+    assert (o4[2].view(np.uint16) == o1[0].view(np.uint16)).all()
+    T = cfg.layout.tokens
+    assert (a4[:, 2 * T:3 * T] == a1).all()
+
+
+def test_routing_histogram_and_skew(prism_ctx):
+    cfg = configs.get("moe32x22skew", n_blocks=2)
+    blob = synth.make_blob(cfg.layout, router_skew=cfg.router_skew, skew_bias=cfg.skew_bias)
+    x = synth.make_frames(cfg.layout, 2)
+    _, a = _run(prism_ctx, cfg.layout, blob, x)
+    for blk in a:
+        h = np.bincount(blk, minlength=32)
+        assert h.sum() == blk.size and blk.min() >= 0 and blk.max() < 32
+        frac = h[:4].sum() / blk.size
+        assert 0.3 < frac < 0.7, f"skewed experts take {frac:.2f} of the tokens"
+
+
+def test_stack_argument_errors(prism_ctx):
+    import torch
+    from prism_inference_b200.abi import PrismError
+    cfg = configs.get("moe16x1")
+    blob = synth.make_blob(cfg.layout)
+    st = Stack(prism_ctx, cfg.layout, blob, 1)
+    x = torch.zeros((2, cfg.layout.tokens, 256), dtype=torch.float16, device="cuda")
+    out = torch.zeros_like(x)
+    with pytest.raises(PrismError, match="RANGE"):
+        st.forward(x, out)  # 2 frames > max_frames 1
+    with pytest.raises(PrismError, match="ARG"):
+        st.forward(x[:1], x[:1])  # out aliases in
+    L = layout.build_stack(256, 1, n_experts=16)
+    with pytest.raises(PrismError, match="RANGE"):
+        Stack(prism_ctx, L, blob[:1000], 1)
+    st.close()
