@@ -19,10 +19,10 @@ WEIGHT_SEED = 0x5EED0000
 
 
 def make_blob(layout: StackLayout, seed: int = WEIGHT_SEED, std: float = 0.02,
-              router_skew: int = 0, skew_bias: float = 0.0) -> np.ndarray:
+              router_skew: int = 0, skew_bias=0.0) -> np.ndarray:
     """Flat fp16 blob (as np.float16) for `layout`.  router_skew > 0 adds skew_bias
-    to the router bias of experts 0..router_skew-1 in every MoE block (the
-    load-imbalance stress configuration)."""
+    (a number, or one number per MoE block) to the router bias of experts
+    0..router_skew-1 in every MoE block (the load-imbalance stress configuration)."""
     rng = np.random.Generator(np.random.PCG64(seed))
     blob = np.empty(layout.total, dtype=np.float16)
     chunk = 1 << 24
@@ -30,11 +30,12 @@ def make_blob(layout: StackLayout, seed: int = WEIGHT_SEED, std: float = 0.02,
         n = min(chunk, layout.total - s)
         blob[s:s + n] = (rng.standard_normal(n, dtype=np.float32) * np.float32(std)).astype(np.float16)
     if router_skew > 0:
-        for b in layout.blocks:
-            if b.kind == "moe":
-                rb = b.router_b
-                blob[rb:rb + router_skew] = (blob[rb:rb + router_skew].astype(np.float32)
-                                             + np.float32(skew_bias)).astype(np.float16)
+        moe = [b for b in layout.blocks if b.kind == "moe"]
+        for i, b in enumerate(moe):
+            sb = skew_bias[i % len(skew_bias)] if isinstance(skew_bias, (tuple, list)) else skew_bias
+            rb = b.router_b
+            blob[rb:rb + router_skew] = (blob[rb:rb + router_skew].astype(np.float32)
+                                         + np.float32(sb)).astype(np.float16)
     return blob
 
 
