@@ -1,0 +1,533 @@
+// attn_tc.cu - fused windowed-attention block on the sm_100a tensor cores.
+//
+// Computes, for every 8x8 window of every frame, the first pass of a Prism MoE block
+// (split2_qkv_attn_d256.comp.glsl:24-79) and the router that follows it
+// (moe_router.comp.glsl:24-52 with N-wide logits, moe_ffn_16exp.comp.glsl:27-34):
+//     y = x + Wo . MHA_window(x) + bo            (fp16, masked store of valid tokens)
+//     assign[t] = argmax_e (Wr . y + br)[e]      (first maximum), counts[e] += 1
+//
+// One persistent CTA per SM walks tiles of two windows (128 rows; row = window slot
+// li = 8*ty + tx, slots outside the frame are the reference's phantom zero tokens:
+// the 4-D TMA load zero-fills them and they take part as keys, :31-37, :60).
+// Per tile and head h (8 heads x 32):
+//   QKV_h   TMEM[96]  = X[128x256] . Wqkv_h^T        (tcgen05, K = 256)
+//   drain   Q_h, K_h (fp16, K-major SW64) and V_h^T (fp16, K-major SW128) to smem
+//   S_h     TMEM[128] = Q_h . K_h^T                   (both windows; rows use their own)
+//   softmax fp32 per row over its window's 64 keys (scale, max, exp, sum as :60-66),
+//           P = fp16(exp(s - max)) to smem, the other window's keys stay zero
+//   PV_h    TMEM[32]  = P[128x128] . V_h               (block-diagonal P)
+//   O_h     = fp16(PV * 1/max(sum, 1e-6))  -> attention-output tile (head pair)
+//   PO     += O_pair[128x64] . Wo[:, pair]^T          (TMEM[256], K split by head pair)
+// then y = fp16(fp16(PO + bo) + x) overwrites X in smem, is stored with a 4-D TMA
+// store (rows outside the frame are clipped = the masked store :78), and the router
+// GEMM TMEM = y . Wr^T gives the logits for the argmax.
+//
+// Warp roles: warp 0 = TMA producer (X tile, weight ring), warp 1 = TMEM owner +
+// tcgen05.mma issuer, warps 2..5 = epilogue/softmax (thread = tile row = TMEM lane).
+// Every wait is bounded (common.cuh); on timeout the CTA sets the error word and
+// winds down.  No TMA multicast.
+#include "attn_tc.cuh"
+#include "common.cuh"
+
+namespace prism {
+namespace {
+
+constexpr int kThreads = 192;  // 6 warps
+constexpr int kEpiThreads = 128;
+constexpr int kStage = 16384;  // weight ring stage: [<=128 rows][64] fp16
+constexpr int kStages = 4;
+
+// shared-memory map (offsets from the 1024-aligned base)
+constexpr int kOffX = 0;                          // 4 K-blocks x [128][128 B] = 64 KB
+constexpr int kOffQ = kOffX + 65536;              // [128][64 B]  SW64   8 KB
+constexpr int kOffK = kOffQ + 8192;               // [128][64 B]  SW64   8 KB
+constexpr int kOffVt = kOffK + 8192;              // 2 x [32][128 B] SW128 8 KB
+constexpr int kOffP = kOffVt + 8192;              // 2 x [128][128 B] SW128 32 KB
+constexpr int kOffAO = kOffP + 32768;             // [128][128 B] SW128 16 KB
+constexpr int kOffW = kOffAO + 16384;             // ring 4 x 16 KB
+constexpr int kOffBar = kOffW + kStages * kStage;
+constexpr int kSmem = kOffBar + 1024 + 1024;      // barriers/hist + alignment slack
+
+// TMEM columns
+constexpr uint32_t kTPO = 0;     // out-projection accumulator [256]
+constexpr uint32_t kTQKV = 256;  // QKV_h [96]; router logits reuse [256, 512)
+constexpr uint32_t kTS = 352;    // S_h [128]
+constexpr uint32_t kTO = 480;    // PV_h [32]
+
+struct Bars {
+    uint64_t full[kStages], empty[kStages];
+    uint64_t x_full, x_free, qkv_full, qkv_drained, s_full, p_ready, o_full, o_drained;
+    uint64_t ao_ready, ao_free, po_full, po_drained, y_ready, lg_full, lg_drained, drain, y_all, ep_done;
+    uint32_t tmem_base;
+    int abort;
+    int hist[256];
+};
+
+struct Counter {  // phase bookkeeping of one barrier as seen by one role
+    uint32_t n = 0;
+    PRISM_DEV uint32_t next() { return (n++) & 1u; }          // consumer: wait phase parity
+    PRISM_DEV uint32_t next_free() { return ((n++) & 1u) ^ 1u; }  // producer of a free slot
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_tc_kernel(const AttnTcArgs a, const __grid_constant__ CUtensorMap tm_x,
+                   const __grid_constant__ CUtensorMap tm_y, const __grid_constant__ CUtensorMap tm_wqkv,
+                   const __grid_constant__ CUtensorMap tm_wo, const __grid_constant__ CUtensorMap tm_wr) {
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    unsigned char* sX = smem + kOffX;
+    unsigned char* sQ = smem + kOffQ;
+    unsigned char* sK = smem + kOffK;
+    unsigned char* sVt = smem + kOffVt;
+    unsigned char* sP = smem + kOffP;
+    unsigned char* sAO = smem + kOffAO;
+    unsigned char* sW = smem + kOffW;
+    Bars* bars = reinterpret_cast<Bars*>(smem + kOffBar);
+    volatile int* abort = &bars->abort;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int wx_n = (a.W + 7) >> 3, wy_n = (a.H + 7) >> 3;
+    const int win_per_frame = wx_n * wy_n;
+    const int n_windows = win_per_frame * a.frames;
+    const int n_tiles = (n_windows + 1) >> 1;
+    const bool router = a.n_experts > 0;
+    const int npad = a.n_experts_pad;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&bars->full[s], 1);
+            mbar_init(&bars->empty[s], 1);
+        }
+        mbar_init(&bars->x_full, 1);
+        mbar_init(&bars->x_free, 2);  // router/last MMA commit + store-read completion
+        mbar_init(&bars->qkv_full, 1);
+        mbar_init(&bars->qkv_drained, 4);
+        mbar_init(&bars->s_full, 1);
+        mbar_init(&bars->p_ready, 4);
+        mbar_init(&bars->o_full, 1);
+        mbar_init(&bars->o_drained, 4);
+        mbar_init(&bars->ao_ready, 4);
+        mbar_init(&bars->ao_free, 1);
+        mbar_init(&bars->po_full, 1);
+        mbar_init(&bars->po_drained, 4);
+        mbar_init(&bars->y_ready, 4);
+        mbar_init(&bars->lg_full, 1);
+        mbar_init(&bars->lg_drained, 4);
+        mbar_init(&bars->drain, 1);
+        mbar_init(&bars->y_all, 4);
+        mbar_init(&bars->ep_done, 4);
+        bars->abort = 0;
+        fence_barrier_init();
+        fence_async_shared();
+    }
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) bars->hist[i] = 0;
+    // P tile: the off-window half of every row stays zero for the whole kernel
+    for (int i = threadIdx.x; i < 32768 / 16; i += blockDim.x) reinterpret_cast<uint4*>(sP)[i] = make_uint4(0, 0, 0, 0);
+    fence_async_shared();
+    if (warp == 1) tmem_alloc(&bars->tmem_base, 512);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = bars->tmem_base;
+
+    if (warp == 0) {
+        // ============================ TMA producer ============================
+        if (lane == 0) {
+            prefetch_tmap(&tm_x);
+            prefetch_tmap(&tm_wqkv);
+            prefetch_tmap(&tm_wo);
+            if (router) prefetch_tmap(&tm_wr);
+            int stage = 0;
+            uint32_t phase = 0;
+            Counter c_xfree;
+            bool ok = true;
+            auto ring_load = [&](const CUtensorMap* map, int c0, int c1, uint32_t bytes) -> bool {
+                if (!mbar_wait(&bars->empty[stage], phase ^ 1, abort)) return false;
+                mbar_expect_tx(&bars->full[stage], bytes);
+                tma_load_2d(smem_u32(sW + stage * kStage), map, &bars->full[stage], c0, c1);
+                if (++stage == kStages) {
+                    stage = 0;
+                    phase ^= 1;
+                }
+                return true;
+            };
+            for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
+                if (!mbar_wait(&bars->x_free, c_xfree.next_free(), abort)) break;
+                mbar_expect_tx(&bars->x_full, 65536);
+                for (int half = 0; half < 2; ++half) {
+                    const int w = 2 * tile + half;
+                    // a missing second window loads an out-of-range frame: zero fill
+                    const int f = w < n_windows ? w / win_per_frame : a.frames;
+                    const int wl = w < n_windows ? w % win_per_frame : 0;
+                    const int wy = wl / wx_n, wx = wl % wx_n;
+                    for (int kb = 0; kb < 4; ++kb)
+                        tma_load_4d(smem_u32(sX + kb * 16384 + half * 8192), &tm_x, &bars->x_full, kb * 64, wx * 8,
+                                    wy * 8, f);
+                }
+                for (int h = 0; h < 8 && ok; ++h) {
+                    for (int kc = 0; kc < 4 && ok; ++kc) ok = ring_load(&tm_wqkv, kc * 64, h * 96, 96 * 128);
+                    if (h & 1)
+                        for (int nh = 0; nh < 2 && ok; ++nh) ok = ring_load(&tm_wo, (h >> 1) * 64, nh * 128, 128 * 128);
+                }
+                if (router)
+                    for (int kc = 0; kc < 4 && ok; ++kc)
+                        for (int nh = 0; nh * 128 < npad && ok; ++nh)
+                            ok = ring_load(&tm_wr, kc * 64, nh * 128, (uint32_t)min(128, npad) * 128);
+            }
+        }
+    } else if (warp == 1) {
+        // ============================ MMA issuer ==============================
+        if (lane == 0) {
+            const uint32_t id_qkv = idesc_f16(128, 96), id_s = idesc_f16(128, 128), id_pv = idesc_f16(128, 32),
+                           id_po = idesc_f16(128, 128);
+            const int rn = npad > 128 ? 128 : npad;
+            const uint32_t id_r = idesc_f16(128, rn);
+            int stage = 0;
+            uint32_t phase = 0;
+            Counter c_xfull, c_qkvd, c_pr, c_od, c_aor, c_pod, c_yr, c_lgd;
+            bool ok = true;
+            bool first_tile = true;
+            auto ring_wait = [&]() -> uint32_t {
+                if (!mbar_wait(&bars->full[stage], phase, abort)) {
+                    ok = false;
+                    return 0;
+                }
+                tc_fence_after();
+                return smem_u32(sW + stage * kStage);
+            };
+            auto ring_release = [&]() {
+                mma_commit(&bars->empty[stage]);
+                if (++stage == kStages) {
+                    stage = 0;
+                    phase ^= 1;
+                }
+            };
+            auto wait = [&](uint64_t* bar, uint32_t par) {
+                if (ok && !mbar_wait(bar, par, abort)) ok = false;
+                tc_fence_after();
+            };
+            for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
+                wait(&bars->x_full, c_xfull.next());
+                // logits of the previous tile live in the QKV/S/O columns
+                if (!first_tile) wait(&bars->lg_drained, c_lgd.next());
+                const uint32_t xs = smem_u32(sX);
+                for (int h = 0; h < 8 && ok; ++h) {
+                    // ---- QKV_h
+                    for (int kc = 0; kc < 4 && ok; ++kc) {
+                        const uint32_t b = ring_wait();
+                        if (!ok) break;
+#pragma unroll
+                        for (int k = 0; k < 4; ++k)
+                            mma_f16_ss(tmem + kTQKV, sdesc(xs + kc * 16384 + k * 32, SW128), sdesc(b + k * 32, SW128),
+                                       id_qkv, (kc | k) != 0);
+                        ring_release();
+                    }
+                    mma_commit(&bars->qkv_full);
+                    wait(&bars->qkv_drained, c_qkvd.next());
+                    // ---- S_h = Q K^T
+                    for (int k = 0; k < 2; ++k)
+                        mma_f16_ss(tmem + kTS, sdesc(smem_u32(sQ) + k * 32, SW64), sdesc(smem_u32(sK) + k * 32, SW64),
+                                   id_s, k != 0);
+                    mma_commit(&bars->s_full);
+                    wait(&bars->p_ready, c_pr.next());
+                    // O columns free once the epilogue drained the previous head
+                    if (h > 0 || !first_tile) wait(&bars->o_drained, c_od.next());
+                    // ---- O_h = P V
+                    for (int k = 0; k < 8; ++k)
+                        mma_f16_ss(tmem + kTO, sdesc(smem_u32(sP) + (k >> 2) * 16384 + (k & 3) * 32, SW128),
+                                   sdesc(smem_u32(sVt) + (k >> 2) * 4096 + (k & 3) * 32, SW128), id_pv, k != 0);
+                    mma_commit(&bars->o_full);
+                    if (h & 1) {
+                        // ---- PO += O_pair . Wo[:, pair]^T
+                        wait(&bars->ao_ready, c_aor.next());
+                        if (h == 1 && !first_tile) wait(&bars->po_drained, c_pod.next());
+                        for (int nh = 0; nh < 2 && ok; ++nh) {
+                            const uint32_t b = ring_wait();
+                            if (!ok) break;
+#pragma unroll
+                            for (int k = 0; k < 4; ++k)
+                                mma_f16_ss(tmem + kTPO + nh * 128, sdesc(smem_u32(sAO) + k * 32, SW128),
+                                           sdesc(b + k * 32, SW128), id_po, (h > 1) || (k != 0));
+                            ring_release();
+                        }
+                        mma_commit(&bars->ao_free);
+                    }
+                }
+                mma_commit(&bars->po_full);
+                // ---- router logits = y . Wr^T  (y overwrote X in smem)
+                wait(&bars->y_ready, c_yr.next());
+                if (router) {
+                    for (int kc = 0; kc < 4 && ok; ++kc)
+                        for (int nh = 0; nh * 128 < npad && ok; ++nh) {
+                            const uint32_t b = ring_wait();
+                            if (!ok) break;
+#pragma unroll
+                            for (int k = 0; k < 4; ++k)
+                                mma_f16_ss(tmem + kTQKV + nh * 128, sdesc(xs + kc * 16384 + k * 32, SW128),
+                                           sdesc(b + k * 32, SW128), id_r, (kc | k) != 0);
+                            ring_release();
+                        }
+                    mma_commit(&bars->lg_full);
+                }
+                mma_commit(&bars->x_free);
+                first_tile = false;
+            }
+            mma_commit(&bars->drain);
+            mbar_wait(&bars->drain, 0, abort);
+        }
+    } else {
+        // ============================ epilogue ================================
+        const int quad = warp & 3;
+        const int r = quad * 32 + lane;  // tile row = TMEM lane
+        const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
+        const int wnd = r >> 6;  // which window of the tile
+        const int li = r & 63;
+        const int ty = li >> 3, tx = li & 7;
+        const float scale = a.scale;
+        const int nkeys = a.n_keys;
+        Counter c_qkv, c_s, c_o, c_aof, c_po, c_lg, c_yall;
+        bool ok = true;
+        bool first_pair = true;
+        auto wait = [&](uint64_t* bar, uint32_t par) {
+            if (ok && !mbar_wait(bar, par, abort)) ok = false;
+            tc_fence_after();
+        };
+        auto arrive = [&](uint64_t* bar) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar);
+        };
+        for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
+            const int w = 2 * tile + wnd;
+            const bool win_ok = w < n_windows;
+            const int f = win_ok ? w / win_per_frame : 0;
+            const int wl = win_ok ? w % win_per_frame : 0;
+            const int wy = wl / wx_n, wx = wl % wx_n;
+            const int gy = wy * 8 + ty, gx = wx * 8 + tx;
+            const bool valid = win_ok && gy < a.H && gx < a.W;
+            const int64_t token = (int64_t)f * a.W * a.H + (int64_t)gy * a.W + gx;
+            for (int h = 0; h < 8 && ok; ++h) {
+                // ---- QKV_h -> fp16 Q, K (K-major SW64) and V^T (K-major SW128)
+                wait(&bars->qkv_full, c_qkv.next());
+                if (!ok) break;
+                const float* bq = a.bqkv + h * 96;
+                {
+                    uint32_t v[16];
+                    for (int part = 0; part < 2; ++part) {  // Q then K
+                        unsigned char* dst = part == 0 ? sQ : sK;
+#pragma unroll
+                        for (int g = 0; g < 2; ++g) {
+                            tmem_ld16(tmem + lane_addr + kTQKV + part * 32 + g * 16, v);
+                            tmem_ld_wait();
+                            uint32_t pk[8];
+#pragma unroll
+                            for (int j = 0; j < 8; ++j)
+                                pk[j] = pack_h2(__fadd_rn(__uint_as_float(v[2 * j]), bq[part * 32 + g * 16 + 2 * j]),
+                                                __fadd_rn(__uint_as_float(v[2 * j + 1]),
+                                                          bq[part * 32 + g * 16 + 2 * j + 1]));
+                            *reinterpret_cast<uint4*>(dst + sw64_off(r, 2 * g)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                            *reinterpret_cast<uint4*>(dst + sw64_off(r, 2 * g + 1)) =
+                                make_uint4(pk[4], pk[5], pk[6], pk[7]);
+                        }
+                    }
+                    // V^T: element (d, r) of a [32 x 128] K-major tile
+                    unsigned char* vt = sVt + (r >> 6) * 4096;
+                    const int vchunk = (r & 63) >> 3, velem = r & 7;
+#pragma unroll
+                    for (int g = 0; g < 2; ++g) {
+                        tmem_ld16(tmem + lane_addr + kTQKV + 64 + g * 16, v);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            const int d = g * 16 + j;
+                            const __half hv = __float2half_rn(__fadd_rn(__uint_as_float(v[j]), bq[64 + d]));
+                            *reinterpret_cast<__half*>(vt + sw128_off(d, vchunk) + velem * 2) = hv;
+                        }
+                    }
+                }
+                fence_async_shared();
+                tc_fence_before();
+                arrive(&bars->qkv_drained);
+
+                // ---- softmax over this row's window (split2_qkv_attn_d256.comp.glsl:59-66)
+                wait(&bars->s_full, c_s.next());
+                if (!ok) break;
+                float s[64];
+                {
+                    uint32_t v[16];
+#pragma unroll
+                    for (int g = 0; g < 4; ++g) {
+                        tmem_ld16(tmem + lane_addr + kTS + wnd * 64 + g * 16, v);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) s[g * 16 + j] = __fmul_rn(__uint_as_float(v[j]), scale);
+                    }
+                }
+                float mx = -1e9f;
+#pragma unroll
+                for (int j = 0; j < 64; ++j)
+                    if (j < nkeys && s[j] > mx) mx = s[j];
+                float se = 0.0f;
+                uint32_t pk[32];
+#pragma unroll
+                for (int j = 0; j < 64; j += 2) {
+                    const float p0 = j < nkeys ? __expf(__fsub_rn(s[j], mx)) : 0.0f;
+                    const float p1 = j + 1 < nkeys ? __expf(__fsub_rn(s[j + 1], mx)) : 0.0f;
+                    se = __fadd_rn(__fadd_rn(se, p0), p1);
+                    pk[j >> 1] = pack_h2(p0, p1);
+                }
+                const float inv = __frcp_rn(fmaxf(se, 1e-6f));
+                {
+                    unsigned char* prow = sP + wnd * 16384;
+#pragma unroll
+                    for (int c = 0; c < 8; ++c)
+                        *reinterpret_cast<uint4*>(prow + sw128_off(r, c)) =
+                            make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+                }
+                fence_async_shared();
+                tc_fence_before();
+                arrive(&bars->p_ready);
+
+                // ---- O_h = PV / sum -> fp16 attention output (head pair tile)
+                wait(&bars->o_full, c_o.next());
+                if (!ok) break;
+                if ((h & 1) == 0 && !first_pair) wait(&bars->ao_free, c_aof.next());
+                if (!ok) break;
+                {
+                    uint32_t v[16];
+#pragma unroll
+                    for (int g = 0; g < 2; ++g) {
+                        tmem_ld16(tmem + lane_addr + kTO + g * 16, v);
+                        tmem_ld_wait();
+                        uint32_t po[8];
+#pragma unroll
+                        for (int j = 0; j < 8; ++j)
+                            po[j] = pack_h2(__fmul_rn(__uint_as_float(v[2 * j]), inv),
+                                            __fmul_rn(__uint_as_float(v[2 * j + 1]), inv));
+                        const int c0 = (h & 1) * 4 + g * 2;
+                        *reinterpret_cast<uint4*>(sAO + sw128_off(r, c0)) = make_uint4(po[0], po[1], po[2], po[3]);
+                        *reinterpret_cast<uint4*>(sAO + sw128_off(r, c0 + 1)) = make_uint4(po[4], po[5], po[6], po[7]);
+                    }
+                }
+                tc_fence_before();
+                arrive(&bars->o_drained);
+                if (h & 1) {
+                    fence_async_shared();
+                    arrive(&bars->ao_ready);
+                    first_pair = false;
+                }
+            }
+            if (!ok) break;
+
+            // ---- y = fp16(fp16(PO + bo) + x), written over X (same swizzled slot)
+            wait(&bars->po_full, c_po.next());
+            if (!ok) break;
+#pragma unroll 1
+            for (int g = 0; g < 16; ++g) {
+                uint32_t v[16];
+                tmem_ld16(tmem + lane_addr + kTPO + g * 16, v);
+                tmem_ld_wait();
+                unsigned char* blk = sX + (g >> 2) * 16384;
+                const int ch = (g & 3) * 2;
+                uint4* p0 = reinterpret_cast<uint4*>(blk + sw128_off(r, ch));
+                uint4* p1 = reinterpret_cast<uint4*>(blk + sw128_off(r, ch + 1));
+                const uint4 x0 = *p0, x1 = *p1;
+                const uint32_t xs[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+                uint32_t yv[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const float b0 = a.bo[g * 16 + 2 * j], b1 = a.bo[g * 16 + 2 * j + 1];
+                    const float y0 = __fadd_rn(rh(__fadd_rn(__uint_as_float(v[2 * j]), b0)), lo_h2f(xs[j]));
+                    const float y1 = __fadd_rn(rh(__fadd_rn(__uint_as_float(v[2 * j + 1]), b1)), hi_h2f(xs[j]));
+                    yv[j] = pack_h2(y0, y1);
+                }
+                *p0 = make_uint4(yv[0], yv[1], yv[2], yv[3]);
+                *p1 = make_uint4(yv[4], yv[5], yv[6], yv[7]);
+            }
+            tc_fence_before();
+            arrive(&bars->po_drained);
+            fence_async_shared();
+            arrive(&bars->y_ready);
+            arrive(&bars->y_all);
+            // one thread stores both windows once every row of y is in smem
+            if (threadIdx.x == 64 && mbar_wait(&bars->y_all, c_yall.next(), abort)) {
+                for (int half = 0; half < 2; ++half) {
+                    const int w2 = 2 * tile + half;
+                    if (w2 >= n_windows) continue;
+                    const int f2 = w2 / win_per_frame, wl2 = w2 % win_per_frame;
+                    for (int kb = 0; kb < 4; ++kb)
+                        tma_store_4d(&tm_y, smem_u32(sX + kb * 16384 + half * 8192), kb * 64, (wl2 % wx_n) * 8,
+                                     (wl2 / wx_n) * 8, f2);
+                }
+                tma_store_commit();
+            }
+
+            // ---- router: logits = fp16(y . Wr^T + br), first maximum
+            if (router) {
+                wait(&bars->lg_full, c_lg.next());
+                if (!ok) break;
+                int best = 0;
+                float bv = 0.0f;
+#pragma unroll 1
+                for (int g = 0; g * 16 < npad; ++g) {
+                    uint32_t v[16];
+                    tmem_ld16(tmem + lane_addr + kTQKV + g * 16, v);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const int e = g * 16 + j;
+                        if (e < a.n_experts) {
+                            const float l = rh(__fadd_rn(__uint_as_float(v[j]), a.br[e]));
+                            if (e == 0 || l > bv) {
+                                bv = l;
+                                best = e;
+                            }
+                        }
+                    }
+                }
+                if (valid) {
+                    a.assign[token] = best;
+                    atomicAdd(&bars->hist[best], 1);
+                }
+            }
+            tc_fence_before();
+            arrive(&bars->lg_drained);
+            if (threadIdx.x == 64) {
+                tma_store_wait_read0();  // y left smem: X may be refilled
+                mbar_arrive(&bars->x_free);
+            }
+        }
+        if (threadIdx.x == 64) tma_store_wait0();
+        // flush the CTA's routing histogram once every epilogue warp is done
+        arrive(&bars->ep_done);
+        if (mbar_wait(&bars->ep_done, 0, abort) && router)
+            for (int e = threadIdx.x - 64; e < a.n_experts; e += kEpiThreads)
+                if (bars->hist[e]) atomicAdd(&a.counts[e], bars->hist[e]);
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (bars->abort) {
+        if (threadIdx.x == 0) atomicOr(a.err, ERR_TIMEOUT);
+        const uint64_t t0 = globaltimer();
+        while (globaltimer() - t0 < 1000000ull) {
+        }
+    }
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+}  // namespace
+
+int attn_tc_smem_bytes() { return kSmem; }
+
+cudaError_t launch_attn_tc(const AttnTcArgs& a, const CUtensorMap& x, const CUtensorMap& y, const CUtensorMap& wqkv,
+                           const CUtensorMap& wo, const CUtensorMap& wr, int grid, cudaStream_t s) {
+    cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    if (e != cudaSuccess) return e;
+    attn_tc_kernel<<<grid, kThreads, kSmem, s>>>(a, x, y, wqkv, wo, wr);
+    return cudaGetLastError();
+}
+
+}  // namespace prism

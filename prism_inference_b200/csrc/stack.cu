@@ -16,6 +16,7 @@
 #include <string>
 #include <vector>
 
+#include "attn_tc.cuh"
 #include "common.cuh"
 #include "pass_kernels.cuh"
 #include "route_kernels.cuh"
@@ -91,6 +92,23 @@ int make_map_2d(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, 
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(PRISM_E_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return PRISM_OK;
+}
+
+// 4-D fp16 activation tensor (C, X=W, Y=H, F) HWC per frame, box {64, 8, 8, 1}, 128B swizzle:
+// one box is one 8x8 window, 64 channels, rows in window-slot order.
+int make_map_act4d(CUtensorMap* m, const void* base, int C, int W, int H, int F) {
+    auto fn = encode_fn();
+    if (!fn) return fail(PRISM_E_CUDA, "cuTensorMapEncodeTiled is not available");
+    if ((uintptr_t)base & 15) return fail(PRISM_E_ALIGN, "activation buffer not 16-byte aligned");
+    cuuint64_t dims[4] = {(cuuint64_t)C, (cuuint64_t)W, (cuuint64_t)H, (cuuint64_t)F};
+    cuuint64_t strides[3] = {(cuuint64_t)C * 2, (cuuint64_t)C * 2 * W, (cuuint64_t)C * 2 * W * H};
+    cuuint32_t box[4] = {64, 8, 8, 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(PRISM_E_CUDA, "cuTensorMapEncodeTiled (4d) failed (%d)", (int)r);
     return PRISM_OK;
 }
 
@@ -319,6 +337,15 @@ struct FastBlock {
     float* b2 = nullptr;   // [E][256] / [256]
     CUtensorMap tm_w1, tm_w2;
     int moe_index = -1;
+    // fused attention (dim 256): head-major QKV, out-projection, padded router
+    __half* wqkv = nullptr;  // [768][256], rows of head h at 96h: q(32) k(32) v(32)
+    float* bqkv = nullptr;   // [768] same order
+    __half* wo = nullptr;    // [256][256]
+    float* bo = nullptr;     // [256]
+    __half* wr = nullptr;    // [npad][256], rows >= n_experts zero
+    float* br = nullptr;     // [npad]
+    int npad = 0;
+    CUtensorMap tm_wqkv, tm_wo, tm_wr;
 };
 
 }  // namespace
@@ -528,6 +555,34 @@ extern "C" int prism_stack_create(prism_ctx* ctx, const prism_stack_desc* desc, 
     for (int i = 0; i < desc->n_blocks; ++i) {
         FastBlock fb;
         fb.d = desc->blocks[i];
+        if (st->tc) {
+            std::vector<uint16_t> wqkv((size_t)768 * 256), wo((size_t)256 * 256);
+            std::vector<float> bqkv(768), bo(256);
+            for (int h = 0; h < 8; ++h)
+                for (int part = 0; part < 3; ++part) {
+                    copy_mat(wqkv, (size_t)(h * 96 + part * 32) * 256, fb.d.qkv_w + (int64_t)(part * 256 + h * 32) * 256,
+                             32, 256, 256);
+                    copy_bias(bqkv, h * 96 + part * 32, fb.d.qkv_b + part * 256 + h * 32, 32);
+                }
+            copy_mat(wo, 0, fb.d.out_w, 256, 256, 256);
+            copy_bias(bo, 0, fb.d.out_b, 256);
+            if ((rc = upload(st, (uint16_t**)&fb.wqkv, wqkv)) || (rc = upload(st, &fb.bqkv, bqkv)) ||
+                (rc = upload(st, (uint16_t**)&fb.wo, wo)) || (rc = upload(st, &fb.bo, bo)))
+                return fail_cleanup(rc);
+            if ((rc = make_map_2d(&fb.tm_wqkv, fb.wqkv, 768, 256, 96)) || (rc = make_map_2d(&fb.tm_wo, fb.wo, 256, 256, 128)))
+                return fail_cleanup(rc);
+            if (fb.d.kind == PRISM_BLOCK_MOE) {
+                fb.npad = (fb.d.n_experts + 15) / 16 * 16;
+                std::vector<uint16_t> wr((size_t)fb.npad * 256, 0);
+                std::vector<float> br(fb.npad, 0.0f);
+                copy_mat(wr, 0, fb.d.router_w, fb.d.n_experts, 256, 256);
+                copy_bias(br, 0, fb.d.router_b, fb.d.n_experts);
+                if ((rc = upload(st, (uint16_t**)&fb.wr, wr)) || (rc = upload(st, &fb.br, br))) return fail_cleanup(rc);
+                if ((rc = make_map_2d(&fb.tm_wr, fb.wr, fb.npad, 256, std::min(128, fb.npad)))) return fail_cleanup(rc);
+            } else {
+                fb.tm_wr = fb.tm_wo;  // unused without a router
+            }
+        }
         if (fb.d.kind == PRISM_BLOCK_MOE) {
             fb.moe_index = st->n_moe++;
             const int E = fb.d.n_experts;
@@ -598,7 +653,7 @@ extern "C" int prism_stack_tokens_per_frame(const prism_stack* st) { return st ?
 extern "C" int prism_stack_launch_count(const prism_stack* st, int frames) {
     if (!st || frames <= 0) return 0;
     int n = (st->desc.up_w >= 0 ? 1 : 0) + (st->desc.down_w >= 0 ? 1 : 0);
-    for (const auto& b : st->blocks) n += b.d.kind == PRISM_BLOCK_MOE ? 5 : 2;
+    for (const auto& b : st->blocks) n += b.d.kind == PRISM_BLOCK_MOE ? 4 : 2;
     if (st->desc.down_w < 0 && st->blocks.empty()) n += 1;  // plain copy
     return n;
 }
@@ -664,7 +719,83 @@ extern "C" int prism_stack_forward(prism_stack* st, const void* in, void* out, i
             nxt = st->act_a;
             nxt_map = &st->tm_act_a;
         }
-        // attention: x (cur) -> y (act_y)
+        if (st->tc) {
+            // fused tcgen05 attention (+ router, histogram): x (cur) -> y (act_y)
+            int32_t* asg = assign ? assign + (size_t)std::max(b.moe_index, 0) * rows : st->assign_ws;
+            CUtensorMap tm_x, tm_y;
+            if ((rc = make_map_act4d(&tm_x, cur, D, d.spatial_w, d.spatial_h, frames)) ||
+                (rc = make_map_act4d(&tm_y, st->act_y, D, d.spatial_w, d.spatial_h, frames)))
+                return rc;
+            AttnTcArgs ta;
+            ta.W = d.spatial_w;
+            ta.H = d.spatial_h;
+            ta.frames = frames;
+            ta.n_keys = std::min(64, T);
+            ta.n_experts = b.d.kind == PRISM_BLOCK_MOE ? b.d.n_experts : 0;
+            ta.n_experts_pad = b.npad;
+            ta.scale = 0.1767766953f;
+            ta.bqkv = b.bqkv;
+            ta.bo = b.bo;
+            ta.br = b.br;
+            ta.assign = asg;
+            ta.counts = st->counts;
+            ta.err = st->err;
+            const int n_win = ((d.spatial_w + 7) / 8) * ((d.spatial_h + 7) / 8) * frames;
+            {
+                KernelTimer kt(st, s, PRISM_K_ATTN);
+                CUDA_TRY(launch_attn_tc(ta, tm_x, tm_y, b.tm_wqkv, b.tm_wo, b.tm_wr, std::min(grid, (n_win + 1) / 2), s));
+            }
+            if (b.d.kind == PRISM_BLOCK_MOE) {
+                RoutePlanArgs rp;
+                rp.counts = st->counts;
+                rp.counts_out = nullptr;
+                rp.offsets = st->offsets;
+                rp.cursor = st->cursor;
+                rp.tiles = st->tiles;
+                rp.n_tiles = st->n_tiles;
+                rp.n_experts = b.d.n_experts;
+                rp.n_tokens = rows;
+                rp.err = st->err;
+                RouteScatterArgs rs;
+                rs.assign = asg;
+                rs.offsets = st->offsets;
+                rs.cursor = st->cursor;
+                rs.perm = st->perm;
+                rs.n_experts = b.d.n_experts;
+                rs.n_tokens = rows;
+                rs.err = st->err;
+                {
+                    KernelTimer kt(st, s, PRISM_K_ROUTE);
+                    CUDA_TRY(launch_route(rp, rs, s));
+                }
+                FfnArgs fa{};
+                fa.x = st->act_y;
+                fa.y = nxt;
+                fa.perm = st->perm;
+                fa.tiles = st->tiles;
+                fa.n_tiles = st->n_tiles;
+                fa.b1 = b.b1;
+                fa.b2 = b.b2;
+                fa.err = st->err;
+                KernelTimer kt(st, s, PRISM_K_EXPERT);
+                CUDA_TRY(launch_ffn_expert256(fa, b.tm_w1, b.tm_w2, std::min(grid, rows / 128 + b.d.n_experts), s));
+            } else {
+                FfnArgs fa{};
+                fa.x = st->act_y;
+                fa.y = nxt;
+                fa.n_rows = rows;
+                fa.b1 = b.b1;
+                fa.b2 = b.b2;
+                fa.err = st->err;
+                KernelTimer kt(st, s, PRISM_K_DENSE_FFN);
+                CUDA_TRY(launch_ffn_dense256(fa, st->tm_act_y, b.tm_w1, b.tm_w2, b.d.ffn_hidden / 256,
+                                             std::min(grid, (rows + 127) / 128), s));
+            }
+            cur = nxt;
+            cur_map = nxt_map;
+            continue;
+        }
+        // dim 128: CUDA-core attention + dense FFN
         AttnArgs at;
         at.weights = st->blob;
         at.x = cur;

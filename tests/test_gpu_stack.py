@@ -58,6 +58,16 @@ def test_stack_matches_oracle(prism_ctx, oracle, key, n_blocks, frames):
     _check(prism_ctx, oracle, cfg.layout, blob, x, key)
 
 
+@pytest.mark.parametrize("w,h,frames", [(4, 4, 2), (20, 12, 3), (8, 8, 1), (40, 9, 2)])
+def test_stack_odd_frame_shapes(prism_ctx, oracle, w, h, frames):
+    """Partial windows in x and y, frames of fewer than 64 tokens (keys = n_tokens),
+    odd window counts (a tile with one window)."""
+    L = layout.build_stack(256, 2, n_experts=8, up_adapter=True, down_adapter=True, spatial_w=w, spatial_h=h)
+    blob = synth.make_blob(L)
+    x = synth.make_frames(L, frames)
+    _check(prism_ctx, oracle, L, blob, x, f"{w}x{h}x{frames}")
+
+
 @pytest.mark.parametrize("key", ["dense256x12", "dense128x4"])
 def test_stack_reference_ffn_widths(prism_ctx, oracle, key):
     """The shader widths: FFN 1024 in four fp16-accumulated chunks (d256) and 512
