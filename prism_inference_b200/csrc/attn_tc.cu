@@ -39,14 +39,12 @@ constexpr int kStages = 4;
 
 // shared-memory map (offsets from the 1024-aligned base)
 constexpr int kOffX = 0;                          // 4 K-blocks x [128][128 B] = 64 KB
-constexpr int kOffQ = kOffX + 65536;              // [128][64 B]  SW64   8 KB
-constexpr int kOffK = kOffQ + 8192;               // [128][64 B]  SW64   8 KB
-constexpr int kOffVt = kOffK + 8192;              // 2 x [32][128 B] SW128 8 KB
-constexpr int kOffP = kOffVt + 8192;              // 2 x [128][128 B] SW128 32 KB
+constexpr int kOffQKV = kOffX + 65536;            // 2 buffers (head parity) x 24 KB:
+constexpr int kQKVBuf = 24576;                    //   Q [128][64 B] SW64 | K [128][64 B] SW64 | V^T 2 x [32][128 B] SW128
+constexpr int kOffP = kOffQKV + 2 * kQKVBuf;      // 2 x [128][128 B] SW128 32 KB
 constexpr int kOffAO = kOffP + 32768;             // [128][128 B] SW128 16 KB
 constexpr int kOffW = kOffAO + 16384;             // ring 4 x 16 KB
 constexpr int kOffBar = kOffW + kStages * kStage;
-constexpr int kSmem = kOffBar + 1024 + 1024;      // barriers/hist + alignment slack
 
 // TMEM columns
 constexpr uint32_t kTPO = 0;     // out-projection accumulator [256]
@@ -62,6 +60,8 @@ struct Bars {
     int abort;
     int hist[256];
 };
+constexpr int kSmem = kOffBar + (int)sizeof(Bars) + 1024;  // + alignment slack of the dynamic base
+static_assert(kSmem <= 232448, "shared memory budget");
 
 struct Counter {  // phase bookkeeping of one barrier as seen by one role
     uint32_t n = 0;
@@ -76,9 +76,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     unsigned char* sX = smem + kOffX;
-    unsigned char* sQ = smem + kOffQ;
-    unsigned char* sK = smem + kOffK;
-    unsigned char* sVt = smem + kOffVt;
+    unsigned char* sQKV = smem + kOffQKV;  // buffer b: Q at +0, K at +8192, V^T at +16384
     unsigned char* sP = smem + kOffP;
     unsigned char* sAO = smem + kOffAO;
     unsigned char* sW = smem + kOffW;
@@ -164,8 +162,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                         tma_load_4d(smem_u32(sX + kb * 16384 + half * 8192), &tm_x, &bars->x_full, kb * 64, wx * 8,
                                     wy * 8, f);
                 }
+                // same order as the MMA warp consumes: QKV_0, then per head h
+                // QKV_{h+1} and, after every second head, the Wo columns of the pair
+                for (int kc = 0; kc < 4 && ok; ++kc) ok = ring_load(&tm_wqkv, kc * 64, 0, 96 * 128);
                 for (int h = 0; h < 8 && ok; ++h) {
-                    for (int kc = 0; kc < 4 && ok; ++kc) ok = ring_load(&tm_wqkv, kc * 64, h * 96, 96 * 128);
+                    if (h < 7)
+                        for (int kc = 0; kc < 4 && ok; ++kc) ok = ring_load(&tm_wqkv, kc * 64, (h + 1) * 96, 96 * 128);
                     if (h & 1)
                         for (int nh = 0; nh < 2 && ok; ++nh) ok = ring_load(&tm_wo, (h >> 1) * 64, nh * 128, 128 * 128);
                 }
@@ -177,6 +179,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp == 1) {
         // ============================ MMA issuer ==============================
+        // Order per tile: QKV_0; for h: [Q,K,V^T of h drained] S_h, QKV_{h+1},
+        // [P_h ready, O columns free] PV_h, every second head [pair ready] PO += ...
+        // QKV_{h+1} overlaps the softmax of head h; Q/K/V^T smem is double-buffered.
         if (lane == 0) {
             const uint32_t id_qkv = idesc_f16(128, 96), id_s = idesc_f16(128, 128), id_pv = idesc_f16(128, 32),
                            id_po = idesc_f16(128, 128);
@@ -206,36 +211,39 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (ok && !mbar_wait(bar, par, abort)) ok = false;
                 tc_fence_after();
             };
+            const uint32_t xs = smem_u32(sX);
+            auto issue_qkv = [&]() {
+                for (int kc = 0; kc < 4 && ok; ++kc) {
+                    const uint32_t b = ring_wait();
+                    if (!ok) break;
+#pragma unroll
+                    for (int k = 0; k < 4; ++k)
+                        mma_f16_ss(tmem + kTQKV, sdesc(xs + kc * 16384 + k * 32, SW128), sdesc(b + k * 32, SW128),
+                                   id_qkv, (kc | k) != 0);
+                    ring_release();
+                }
+                mma_commit(&bars->qkv_full);
+            };
             for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
                 wait(&bars->x_full, c_xfull.next());
                 // logits of the previous tile live in the QKV/S/O columns
                 if (!first_tile) wait(&bars->lg_drained, c_lgd.next());
-                const uint32_t xs = smem_u32(sX);
+                issue_qkv();
                 for (int h = 0; h < 8 && ok; ++h) {
-                    // ---- QKV_h
-                    for (int kc = 0; kc < 4 && ok; ++kc) {
-                        const uint32_t b = ring_wait();
-                        if (!ok) break;
-#pragma unroll
-                        for (int k = 0; k < 4; ++k)
-                            mma_f16_ss(tmem + kTQKV, sdesc(xs + kc * 16384 + k * 32, SW128), sdesc(b + k * 32, SW128),
-                                       id_qkv, (kc | k) != 0);
-                        ring_release();
-                    }
-                    mma_commit(&bars->qkv_full);
+                    const uint32_t qb = smem_u32(sQKV + (h & 1) * kQKVBuf);
                     wait(&bars->qkv_drained, c_qkvd.next());
                     // ---- S_h = Q K^T
                     for (int k = 0; k < 2; ++k)
-                        mma_f16_ss(tmem + kTS, sdesc(smem_u32(sQ) + k * 32, SW64), sdesc(smem_u32(sK) + k * 32, SW64),
-                                   id_s, k != 0);
+                        mma_f16_ss(tmem + kTS, sdesc(qb + k * 32, SW64), sdesc(qb + 8192 + k * 32, SW64), id_s, k != 0);
                     mma_commit(&bars->s_full);
+                    if (h < 7) issue_qkv();
                     wait(&bars->p_ready, c_pr.next());
                     // O columns free once the epilogue drained the previous head
                     if (h > 0 || !first_tile) wait(&bars->o_drained, c_od.next());
                     // ---- O_h = P V
                     for (int k = 0; k < 8; ++k)
                         mma_f16_ss(tmem + kTO, sdesc(smem_u32(sP) + (k >> 2) * 16384 + (k & 3) * 32, SW128),
-                                   sdesc(smem_u32(sVt) + (k >> 2) * 4096 + (k & 3) * 32, SW128), id_pv, k != 0);
+                                   sdesc(qb + 16384 + (k >> 2) * 4096 + (k & 3) * 32, SW128), id_pv, k != 0);
                     mma_commit(&bars->o_full);
                     if (h & 1) {
                         // ---- PO += O_pair . Wo[:, pair]^T
@@ -277,6 +285,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else {
         // ============================ epilogue ================================
+        // Per head h: softmax_h -> drain QKV_{h+1} -> O_h (the drain of QKV_0 comes
+        // before the loop).
         const int quad = warp & 3;
         const int r = quad * 32 + lane;  // tile row = TMEM lane
         const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
@@ -296,6 +306,49 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(bar);
         };
+        // QKV_h (TMEM) -> fp16 Q, K (K-major SW64) and V^T (K-major SW128), buffer h&1
+        auto drain_qkv = [&](int h) {
+            wait(&bars->qkv_full, c_qkv.next());
+            if (!ok) return;
+            unsigned char* buf = sQKV + (h & 1) * kQKVBuf;
+            const float* bq = a.bqkv + h * 96;
+#pragma unroll
+            for (int part = 0; part < 3; ++part) {  // Q, K, V
+                float4 bb[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) bb[i] = ldg_f4(bq + part * 32 + 4 * i);
+                uint32_t v[32];
+                tmem_ld32(tmem + lane_addr + kTQKV + part * 32, v);
+                tmem_ld_wait();
+                uint32_t pk[16];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    pk[2 * i] = pack_h2(__fadd_rn(__uint_as_float(v[4 * i]), bb[i].x),
+                                        __fadd_rn(__uint_as_float(v[4 * i + 1]), bb[i].y));
+                    pk[2 * i + 1] = pack_h2(__fadd_rn(__uint_as_float(v[4 * i + 2]), bb[i].z),
+                                            __fadd_rn(__uint_as_float(v[4 * i + 3]), bb[i].w));
+                }
+                if (part < 2) {
+                    unsigned char* dst = buf + part * 8192;
+#pragma unroll
+                    for (int c = 0; c < 4; ++c)
+                        *reinterpret_cast<uint4*>(dst + sw64_off(r, c)) =
+                            make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+                } else {
+                    // V^T: element (d, r) of a [32 x 128] K-major tile
+                    unsigned char* vt = buf + 16384 + (r >> 6) * 4096 + (r & 7) * 2;
+                    const int vchunk = (r & 63) >> 3;
+#pragma unroll
+                    for (int d = 0; d < 32; d += 2) {
+                        *reinterpret_cast<unsigned short*>(vt + sw128_off(d, vchunk)) = (unsigned short)(pk[d >> 1] & 0xffff);
+                        *reinterpret_cast<unsigned short*>(vt + sw128_off(d + 1, vchunk)) = (unsigned short)(pk[d >> 1] >> 16);
+                    }
+                }
+            }
+            fence_async_shared();
+            tc_fence_before();
+            arrive(&bars->qkv_drained);
+        };
         for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
             const int w = 2 * tile + wnd;
             const bool win_ok = w < n_windows;
@@ -305,75 +358,61 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int gy = wy * 8 + ty, gx = wx * 8 + tx;
             const bool valid = win_ok && gy < a.H && gx < a.W;
             const int64_t token = (int64_t)f * a.W * a.H + (int64_t)gy * a.W + gx;
+            drain_qkv(0);
             for (int h = 0; h < 8 && ok; ++h) {
-                // ---- QKV_h -> fp16 Q, K (K-major SW64) and V^T (K-major SW128)
-                wait(&bars->qkv_full, c_qkv.next());
-                if (!ok) break;
-                const float* bq = a.bqkv + h * 96;
-                {
-                    uint32_t v[16];
-                    for (int part = 0; part < 2; ++part) {  // Q then K
-                        unsigned char* dst = part == 0 ? sQ : sK;
-#pragma unroll
-                        for (int g = 0; g < 2; ++g) {
-                            tmem_ld16(tmem + lane_addr + kTQKV + part * 32 + g * 16, v);
-                            tmem_ld_wait();
-                            uint32_t pk[8];
-#pragma unroll
-                            for (int j = 0; j < 8; ++j)
-                                pk[j] = pack_h2(__fadd_rn(__uint_as_float(v[2 * j]), bq[part * 32 + g * 16 + 2 * j]),
-                                                __fadd_rn(__uint_as_float(v[2 * j + 1]),
-                                                          bq[part * 32 + g * 16 + 2 * j + 1]));
-                            *reinterpret_cast<uint4*>(dst + sw64_off(r, 2 * g)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-                            *reinterpret_cast<uint4*>(dst + sw64_off(r, 2 * g + 1)) =
-                                make_uint4(pk[4], pk[5], pk[6], pk[7]);
-                        }
-                    }
-                    // V^T: element (d, r) of a [32 x 128] K-major tile
-                    unsigned char* vt = sVt + (r >> 6) * 4096;
-                    const int vchunk = (r & 63) >> 3, velem = r & 7;
-#pragma unroll
-                    for (int g = 0; g < 2; ++g) {
-                        tmem_ld16(tmem + lane_addr + kTQKV + 64 + g * 16, v);
-                        tmem_ld_wait();
-#pragma unroll
-                        for (int j = 0; j < 16; ++j) {
-                            const int d = g * 16 + j;
-                            const __half hv = __float2half_rn(__fadd_rn(__uint_as_float(v[j]), bq[64 + d]));
-                            *reinterpret_cast<__half*>(vt + sw128_off(d, vchunk) + velem * 2) = hv;
-                        }
-                    }
-                }
-                fence_async_shared();
-                tc_fence_before();
-                arrive(&bars->qkv_drained);
-
                 // ---- softmax over this row's window (split2_qkv_attn_d256.comp.glsl:59-66)
                 wait(&bars->s_full, c_s.next());
                 if (!ok) break;
-                float s[64];
-                {
-                    uint32_t v[16];
-#pragma unroll
-                    for (int g = 0; g < 4; ++g) {
-                        tmem_ld16(tmem + lane_addr + kTS + wnd * 64 + g * 16, v);
-                        tmem_ld_wait();
-#pragma unroll
-                        for (int j = 0; j < 16; ++j) s[g * 16 + j] = __fmul_rn(__uint_as_float(v[j]), scale);
-                    }
-                }
-                float mx = -1e9f;
-#pragma unroll
-                for (int j = 0; j < 64; ++j)
-                    if (j < nkeys && s[j] > mx) mx = s[j];
-                float se = 0.0f;
+                uint32_t sv[64];
+                tmem_ld32(tmem + lane_addr + kTS + wnd * 64, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+                tmem_ld32(tmem + lane_addr + kTS + wnd * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+                tmem_ld_wait();
+                // s_j = acc_j * scale; p_j = exp(s_j - max_j s_j).  scale > 0, so the max of
+                // the scaled scores is the scaled max; exp(x) = 2^(x log2 e).
+                const float c2 = scale * 1.4426950408889634f;
                 uint32_t pk[32];
+                float se;
+                if (nkeys >= 64) {
+                    float m0 = __uint_as_float(sv[0]), m1 = __uint_as_float(sv[1]), m2 = __uint_as_float(sv[2]),
+                          m3 = __uint_as_float(sv[3]);
 #pragma unroll
-                for (int j = 0; j < 64; j += 2) {
-                    const float p0 = j < nkeys ? __expf(__fsub_rn(s[j], mx)) : 0.0f;
-                    const float p1 = j + 1 < nkeys ? __expf(__fsub_rn(s[j + 1], mx)) : 0.0f;
-                    se = __fadd_rn(__fadd_rn(se, p0), p1);
-                    pk[j >> 1] = pack_h2(p0, p1);
+                    for (int j = 4; j < 64; j += 4) {
+                        m0 = fmaxf(m0, __uint_as_float(sv[j]));
+                        m1 = fmaxf(m1, __uint_as_float(sv[j + 1]));
+                        m2 = fmaxf(m2, __uint_as_float(sv[j + 2]));
+                        m3 = fmaxf(m3, __uint_as_float(sv[j + 3]));
+                    }
+                    const float mc = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3)) * c2;
+                    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll
+                    for (int j = 0; j < 64; j += 4) {
+                        const float p0 = ex2_approx(fmaf(__uint_as_float(sv[j]), c2, -mc));
+                        const float p1 = ex2_approx(fmaf(__uint_as_float(sv[j + 1]), c2, -mc));
+                        const float p2 = ex2_approx(fmaf(__uint_as_float(sv[j + 2]), c2, -mc));
+                        const float p3 = ex2_approx(fmaf(__uint_as_float(sv[j + 3]), c2, -mc));
+                        s0 += p0;
+                        s1 += p1;
+                        s2 += p2;
+                        s3 += p3;
+                        pk[j >> 1] = pack_h2(p0, p1);
+                        pk[(j >> 1) + 1] = pack_h2(p2, p3);
+                    }
+                    se = (s0 + s1) + (s2 + s3);
+                } else {
+                    // frames of fewer than 64 tokens: keys are the first n_keys slots (:33)
+                    float m = -1e9f;
+#pragma unroll
+                    for (int j = 0; j < 64; ++j)
+                        if (j < nkeys) m = fmaxf(m, __uint_as_float(sv[j]));
+                    const float mc = m * c2;
+                    se = 0.f;
+#pragma unroll
+                    for (int j = 0; j < 64; j += 2) {
+                        const float p0 = j < nkeys ? ex2_approx(fmaf(__uint_as_float(sv[j]), c2, -mc)) : 0.f;
+                        const float p1 = j + 1 < nkeys ? ex2_approx(fmaf(__uint_as_float(sv[j + 1]), c2, -mc)) : 0.f;
+                        se += p0 + p1;
+                        pk[j >> 1] = pack_h2(p0, p1);
+                    }
                 }
                 const float inv = __frcp_rn(fmaxf(se, 1e-6f));
                 {
@@ -387,26 +426,27 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_fence_before();
                 arrive(&bars->p_ready);
 
+                // ---- Q, K, V^T of the next head while PV_h runs
+                if (h < 7) drain_qkv(h + 1);
+                if (!ok) break;
+
                 // ---- O_h = PV / sum -> fp16 attention output (head pair tile)
                 wait(&bars->o_full, c_o.next());
                 if (!ok) break;
                 if ((h & 1) == 0 && !first_pair) wait(&bars->ao_free, c_aof.next());
                 if (!ok) break;
                 {
-                    uint32_t v[16];
+                    uint32_t v[32];
+                    tmem_ld32(tmem + lane_addr + kTO, v);
+                    tmem_ld_wait();
+                    uint32_t po[16];
 #pragma unroll
-                    for (int g = 0; g < 2; ++g) {
-                        tmem_ld16(tmem + lane_addr + kTO + g * 16, v);
-                        tmem_ld_wait();
-                        uint32_t po[8];
+                    for (int j = 0; j < 16; ++j)
+                        po[j] = pack_h2(__fmul_rn(__uint_as_float(v[2 * j]), inv), __fmul_rn(__uint_as_float(v[2 * j + 1]), inv));
 #pragma unroll
-                        for (int j = 0; j < 8; ++j)
-                            po[j] = pack_h2(__fmul_rn(__uint_as_float(v[2 * j]), inv),
-                                            __fmul_rn(__uint_as_float(v[2 * j + 1]), inv));
-                        const int c0 = (h & 1) * 4 + g * 2;
-                        *reinterpret_cast<uint4*>(sAO + sw128_off(r, c0)) = make_uint4(po[0], po[1], po[2], po[3]);
-                        *reinterpret_cast<uint4*>(sAO + sw128_off(r, c0 + 1)) = make_uint4(po[4], po[5], po[6], po[7]);
-                    }
+                    for (int c = 0; c < 4; ++c)
+                        *reinterpret_cast<uint4*>(sAO + sw128_off(r, (h & 1) * 4 + c)) =
+                            make_uint4(po[4 * c], po[4 * c + 1], po[4 * c + 2], po[4 * c + 3]);
                 }
                 tc_fence_before();
                 arrive(&bars->o_drained);
@@ -422,26 +462,28 @@ __global__ void __launch_bounds__(kThreads, 1)
             wait(&bars->po_full, c_po.next());
             if (!ok) break;
 #pragma unroll 1
-            for (int g = 0; g < 16; ++g) {
-                uint32_t v[16];
-                tmem_ld16(tmem + lane_addr + kTPO + g * 16, v);
-                tmem_ld_wait();
-                unsigned char* blk = sX + (g >> 2) * 16384;
-                const int ch = (g & 3) * 2;
-                uint4* p0 = reinterpret_cast<uint4*>(blk + sw128_off(r, ch));
-                uint4* p1 = reinterpret_cast<uint4*>(blk + sw128_off(r, ch + 1));
-                const uint4 x0 = *p0, x1 = *p1;
-                const uint32_t xs[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-                uint32_t yv[8];
+            for (int g = 0; g < 8; ++g) {  // 32 columns = 4 swizzle chunks of K-block g/2
+                float4 bb[8];
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const float b0 = a.bo[g * 16 + 2 * j], b1 = a.bo[g * 16 + 2 * j + 1];
-                    const float y0 = __fadd_rn(rh(__fadd_rn(__uint_as_float(v[2 * j]), b0)), lo_h2f(xs[j]));
-                    const float y1 = __fadd_rn(rh(__fadd_rn(__uint_as_float(v[2 * j + 1]), b1)), hi_h2f(xs[j]));
-                    yv[j] = pack_h2(y0, y1);
+                for (int i = 0; i < 8; ++i) bb[i] = ldg_f4(a.bo + g * 32 + 4 * i);
+                uint32_t v[32];
+                tmem_ld32(tmem + lane_addr + kTPO + g * 32, v);
+                tmem_ld_wait();
+                unsigned char* blk = sX + (g >> 1) * 16384;
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    uint4* px = reinterpret_cast<uint4*>(blk + sw128_off(r, (g & 1) * 4 + c));
+                    const uint4 x = *px;
+                    const float4 b0 = bb[2 * c], b1 = bb[2 * c + 1];
+                    const float* f = reinterpret_cast<const float*>(&v[8 * c]);
+                    // y = h( h(PO + bo) + x ): the second rounding is the fp16 add of :76
+                    uint4 y;
+                    y.x = hadd2_u32(pack_h2(__fadd_rn(f[0], b0.x), __fadd_rn(f[1], b0.y)), x.x);
+                    y.y = hadd2_u32(pack_h2(__fadd_rn(f[2], b0.z), __fadd_rn(f[3], b0.w)), x.y);
+                    y.z = hadd2_u32(pack_h2(__fadd_rn(f[4], b1.x), __fadd_rn(f[5], b1.y)), x.z);
+                    y.w = hadd2_u32(pack_h2(__fadd_rn(f[6], b1.z), __fadd_rn(f[7], b1.w)), x.w);
+                    *px = y;
                 }
-                *p0 = make_uint4(yv[0], yv[1], yv[2], yv[3]);
-                *p1 = make_uint4(yv[4], yv[5], yv[6], yv[7]);
             }
             tc_fence_before();
             arrive(&bars->po_drained);

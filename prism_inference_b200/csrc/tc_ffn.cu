@@ -262,37 +262,44 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const float* b1 = a.b1 + (size_t)e * HID * n_chunks + c * HID;
                 constexpr int kCols1 = HID / 2;
 #pragma unroll 1
-                for (int g = 0; g < kCols1 / 16; ++g) {
-                    const int col0 = half * kCols1 + g * 16;
-                    uint32_t r[16];
-                    tmem_ld16(tmem + lane_addr + col0, r);
-                    tmem_ld_wait();
-                    uint32_t packed[8];
+                for (int g = 0; g < kCols1 / 32; ++g) {
+                    const int col0 = half * kCols1 + g * 32;
+                    float4 bb[8];
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        float v0 = rh(__fadd_rn(__uint_as_float(r[2 * j]), b1[col0 + 2 * j]));
-                        float v1 = rh(__fadd_rn(__uint_as_float(r[2 * j + 1]), b1[col0 + 2 * j + 1]));
+                    for (int i = 0; i < 8; ++i) bb[i] = ldg_f4(b1 + col0 + 4 * i);
+                    uint32_t r[32];
+                    tmem_ld32(tmem + lane_addr + col0, r);
+                    tmem_ld_wait();
+                    uint32_t packed[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const float bx = (j & 1) ? bb[j >> 1].z : bb[j >> 1].x;
+                        const float by = (j & 1) ? bb[j >> 1].w : bb[j >> 1].y;
+                        // t = h(acc + b1): one rounding per coopVecMatMulAddNV result
+                        const uint32_t t = pack_h2(__fadd_rn(__uint_as_float(r[2 * j]), bx),
+                                                   __fadd_rn(__uint_as_float(r[2 * j + 1]), by));
                         if (MODE == FFN_EXPERT || MODE == FFN_DENSE) {
-                            v0 = gelu_f32(v0);
-                            v1 = gelu_f32(v1);
+                            packed[j] = pack_h2(gelu_f32(lo_h2f(t)), gelu_f32(hi_h2f(t)));
                         } else if (MODE == FFN_PROJ_UP) {
-                            v0 = v0 < 0.0f ? 0.0f : v0;
-                            v1 = v1 < 0.0f ? 0.0f : v1;
+                            const float v0 = lo_h2f(t), v1 = hi_h2f(t);
+                            packed[j] = pack_h2(v0 < 0.0f ? 0.0f : v0, v1 < 0.0f ? 0.0f : v1);
+                        } else {
+                            packed[j] = t;
                         }
-                        packed[j] = pack_h2(v0, v1);
                     }
                     if (Cfg::kTwoGemm) {
-                        // H tile, K-major SW128: column col0 -> K-block col0/64, chunk (col0%64)/8
+                        // H tile, K-major SW128: column col0 -> K-block col0/64, chunks (col0%64)/8 ..
                         unsigned char* blk = sH + (col0 >> 6) * 16384;
                         const int ch = (col0 & 63) >> 3;
-                        *reinterpret_cast<uint4*>(blk + sw128_off(row, ch)) =
-                            make_uint4(packed[0], packed[1], packed[2], packed[3]);
-                        *reinterpret_cast<uint4*>(blk + sw128_off(row, ch + 1)) =
-                            make_uint4(packed[4], packed[5], packed[6], packed[7]);
+#pragma unroll
+                        for (int q = 0; q < 4; ++q)
+                            *reinterpret_cast<uint4*>(blk + sw128_off(row, ch + q)) =
+                                make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
                     } else if (row_valid) {
                         uint4* dst = reinterpret_cast<uint4*>(a.y + (size_t)out_row * NOUT + col0);
-                        dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-                        dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+#pragma unroll
+                        for (int q = 0; q < 4; ++q)
+                            dst[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
                     }
                 }
                 tc_fence_before();
@@ -310,51 +317,59 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const bool last = (c == n_chunks - 1);
                 constexpr int kCols2 = NOUT / 2;
 #pragma unroll
-                for (int g = 0; g < kCols2 / 16; ++g) {
-                    const int col0 = half * kCols2 + g * 16;
-                    uint32_t r[16];
-                    tmem_ld16(tmem + Cfg::kAcc2 + lane_addr + col0, r);
+                for (int g = 0; g < kCols2 / 32; ++g) {
+                    const int col0 = half * kCols2 + g * 32;
+                    float4 bb[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) bb[i] = ldg_f4(b2 + col0 + 4 * i);
+                    uint32_t r[32];
+                    tmem_ld32(tmem + Cfg::kAcc2 + lane_addr + col0, r);
                     tmem_ld_wait();
-                    float part[16];
+                    uint32_t part[16];  // h(acc + b2)
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) part[j] = rh(__fadd_rn(__uint_as_float(r[j]), b2[col0 + j]));
+                    for (int j = 0; j < 16; ++j) {
+                        const float bx = (j & 1) ? bb[j >> 1].z : bb[j >> 1].x;
+                        const float by = (j & 1) ? bb[j >> 1].w : bb[j >> 1].y;
+                        part[j] = pack_h2(__fadd_rn(__uint_as_float(r[2 * j]), bx),
+                                          __fadd_rn(__uint_as_float(r[2 * j + 1]), by));
+                    }
                     if (MODE == FFN_DENSE) {
+                        // fp16 running sum of the chunk outputs (attention_windowed_d256.comp.glsl:167-168)
 #pragma unroll
-                        for (int j = 0; j < 8; ++j) {
-                            const uint32_t prev = accum[g * 8 + j];
-                            accum[g * 8 + j] = pack_h2(__fadd_rn(lo_h2f(prev), part[2 * j]),
-                                                       __fadd_rn(hi_h2f(prev), part[2 * j + 1]));
-                        }
+                        for (int j = 0; j < 16; ++j) accum[g * 16 + j] = hadd2_u32(accum[g * 16 + j], part[j]);
                     }
                     if (!last) continue;
-                    // residual x from the A tile (same row, column col0 of K-block col0/64)
+                    // residual x from the A tile (same row, columns col0.. of K-block col0/64)
                     const unsigned char* ablk = sA + (col0 >> 6) * 16384;
                     const int ch = (col0 & 63) >> 3;
-                    const uint4 x0 = *reinterpret_cast<const uint4*>(ablk + sw128_off(row, ch));
-                    const uint4 x1 = *reinterpret_cast<const uint4*>(ablk + sw128_off(row, ch + 1));
-                    const uint32_t xs[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-                    uint32_t packed[8];
+                    uint32_t packed[16];
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        float z0, z1;
-                        if (MODE == FFN_DENSE) {
-                            // out = h(acc - (n_chunks-1)*b2 + y)   (attention_windowed_d256.comp.glsl:171-177)
-                            const float corr = (float)(n_chunks - 1);
-                            const uint32_t acc = accum[g * 8 + j];
-                            z0 = __fadd_rn(__fsub_rn(lo_h2f(acc), __fmul_rn(corr, b2[col0 + 2 * j])), lo_h2f(xs[j]));
-                            z1 = __fadd_rn(__fsub_rn(hi_h2f(acc), __fmul_rn(corr, b2[col0 + 2 * j + 1])),
-                                           hi_h2f(xs[j]));
-                        } else {
-                            // z = h(r + y)   (moe_expert_skip.comp.glsl:52)
-                            z0 = __fadd_rn(part[2 * j], lo_h2f(xs[j]));
-                            z1 = __fadd_rn(part[2 * j + 1], hi_h2f(xs[j]));
+                    for (int q = 0; q < 4; ++q) {
+                        const uint4 x = *reinterpret_cast<const uint4*>(ablk + sw128_off(row, ch + q));
+                        const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            const int k = 4 * q + j;
+                            if (MODE == FFN_DENSE && n_chunks > 1) {
+                                // out = h(acc - (n_chunks-1)*b2 + y)   (attention_windowed_d256.comp.glsl:171-177)
+                                const float corr = (float)(n_chunks - 1);
+                                const float bx = (k & 1) ? bb[k >> 1].z : bb[k >> 1].x;
+                                const float by = (k & 1) ? bb[k >> 1].w : bb[k >> 1].y;
+                                const uint32_t acc = accum[g * 16 + k];
+                                packed[k] = pack_h2(
+                                    __fadd_rn(__fsub_rn(lo_h2f(acc), __fmul_rn(corr, bx)), lo_h2f(xs[j])),
+                                    __fadd_rn(__fsub_rn(hi_h2f(acc), __fmul_rn(corr, by)), hi_h2f(xs[j])));
+                            } else {
+                                // z = h(r + y), an fp16 add (moe_expert_skip.comp.glsl:52)
+                                packed[k] = hadd2_u32(part[k], xs[j]);
+                            }
                         }
-                        packed[j] = pack_h2(z0, z1);
                     }
                     if (row_valid) {
                         uint4* dst = reinterpret_cast<uint4*>(a.y + (size_t)out_row * NOUT + col0);
-                        dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-                        dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+#pragma unroll
+                        for (int q = 0; q < 4; ++q)
+                            dst[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
                     }
                 }
                 tc_fence_before();
