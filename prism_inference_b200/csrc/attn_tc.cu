@@ -14,16 +14,23 @@
 //   drain   Q_h, K_h (fp16, K-major SW64) and V_h^T (fp16, K-major SW128) to smem
 //   S_h     TMEM[128] = Q_h . K_h^T                   (both windows; rows use their own)
 //   softmax fp32 per row over its window's 64 keys (scale, max, exp, sum as :60-66),
-//           P = fp16(exp(s - max)) to smem, the other window's keys stay zero
-//   PV_h    TMEM[32]  = P[128x128] . V_h               (block-diagonal P)
+//           P = fp16(exp(s - max)) written over S in TMEM (tcgen05.st), the other
+//           window's keys zero
+//   PV_h    TMEM[32]  = P[128x128] (A from TMEM) . V_h  (block-diagonal P)
 //   O_h     = fp16(PV * 1/max(sum, 1e-6))  -> attention-output tile (head pair)
 //   PO     += O_pair[128x64] . Wo[:, pair]^T          (TMEM[256], K split by head pair)
 // then y = fp16(fp16(PO + bo) + x) overwrites X in smem, is stored with a 4-D TMA
 // store (rows outside the frame are clipped = the masked store :78), and the router
 // GEMM TMEM = y . Wr^T gives the logits for the argmax.
 //
-// Warp roles: warp 0 = TMA producer (X tile, weight ring), warp 1 = TMEM owner +
-// tcgen05.mma issuer, warps 2..5 = epilogue/softmax (thread = tile row = TMEM lane).
+// Warp roles (320 threads):
+//   warp 0      TMA producer: X tile (4-D window boxes), weight ring (QKV_h, Wo, Wr)
+//   warp 1      TMEM owner + tcgen05.mma issuer
+//   warps 2-5   softmax group: S_h -> P_h, O_h -> attention-output tile
+//   warps 6-9   drain group: QKV_h -> Q/K/V^T smem, y epilogue, store, router
+// Thread = tile row = TMEM lane in both groups (warp w reads lanes 32*(w%4)..).
+// The two groups run one head apart and the MMA warp issues QKV_{h+1} right after S_h;
+// the 7-stage weight ring (112 KB) keeps the L2 -> smem weight stream ahead of it.
 // Every wait is bounded (common.cuh); on timeout the CTA sets the error word and
 // winds down.  No TMA multicast.
 #include "attn_tc.cuh"
@@ -32,30 +39,29 @@
 namespace prism {
 namespace {
 
-constexpr int kThreads = 192;  // 6 warps
-constexpr int kEpiThreads = 128;
+constexpr int kThreads = 320;  // 10 warps
 constexpr int kStage = 16384;  // weight ring stage: [<=128 rows][64] fp16
-constexpr int kStages = 4;
+constexpr int kStages = 7;
 
 // shared-memory map (offsets from the 1024-aligned base)
-constexpr int kOffX = 0;                          // 4 K-blocks x [128][128 B] = 64 KB
-constexpr int kOffQKV = kOffX + 65536;            // 2 buffers (head parity) x 24 KB:
-constexpr int kQKVBuf = 24576;                    //   Q [128][64 B] SW64 | K [128][64 B] SW64 | V^T 2 x [32][128 B] SW128
-constexpr int kOffP = kOffQKV + 2 * kQKVBuf;      // 2 x [128][128 B] SW128 32 KB
-constexpr int kOffAO = kOffP + 32768;             // [128][128 B] SW128 16 KB
-constexpr int kOffW = kOffAO + 16384;             // ring 4 x 16 KB
+constexpr int kOffX = 0;                // 4 K-blocks x [128][128 B] = 64 KB; y overwrites it
+constexpr int kOffQ = kOffX + 65536;    // Q_h [128][64 B] SW64 8 KB
+constexpr int kOffK = kOffQ + 8192;     // K_h [128][64 B] SW64 8 KB
+constexpr int kOffVt = kOffK + 8192;    // V_h^T, 2 buffers (head parity) x 2 x [32][128 B] SW128 = 16 KB
+constexpr int kOffAO = kOffVt + 16384;  // [128][128 B] SW128 16 KB
+constexpr int kOffW = kOffAO + 16384;   // ring 7 x 16 KB
 constexpr int kOffBar = kOffW + kStages * kStage;
 
 // TMEM columns
 constexpr uint32_t kTPO = 0;     // out-projection accumulator [256]
 constexpr uint32_t kTQKV = 256;  // QKV_h [96]; router logits reuse [256, 512)
-constexpr uint32_t kTS = 352;    // S_h [128]
+constexpr uint32_t kTS = 352;    // S_h [128] fp32; P_h overwrites [352, 416) as fp16 pairs
 constexpr uint32_t kTO = 480;    // PV_h [32]
 
 struct Bars {
     uint64_t full[kStages], empty[kStages];
     uint64_t x_full, x_free, qkv_full, qkv_drained, s_full, p_ready, o_full, o_drained;
-    uint64_t ao_ready, ao_free, po_full, po_drained, y_ready, lg_full, lg_drained, drain, y_all, ep_done;
+    uint64_t ao_ready, ao_free, po_full, po_drained, y_ready, lg_full, lg_drained, drain, ep_done;
     uint32_t tmem_base;
     int abort;
     int hist[256];
@@ -65,7 +71,7 @@ static_assert(kSmem <= 232448, "shared memory budget");
 
 struct Counter {  // phase bookkeeping of one barrier as seen by one role
     uint32_t n = 0;
-    PRISM_DEV uint32_t next() { return (n++) & 1u; }          // consumer: wait phase parity
+    PRISM_DEV uint32_t next() { return (n++) & 1u; }              // consumer: wait phase parity
     PRISM_DEV uint32_t next_free() { return ((n++) & 1u) ^ 1u; }  // producer of a free slot
 };
 
@@ -76,8 +82,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     unsigned char* sX = smem + kOffX;
-    unsigned char* sQKV = smem + kOffQKV;  // buffer b: Q at +0, K at +8192, V^T at +16384
-    unsigned char* sP = smem + kOffP;
+    unsigned char* sQ = smem + kOffQ;
+    unsigned char* sK = smem + kOffK;
+    unsigned char* sVt = smem + kOffVt;  // buffer b at +8192*b
     unsigned char* sAO = smem + kOffAO;
     unsigned char* sW = smem + kOffW;
     Bars* bars = reinterpret_cast<Bars*>(smem + kOffBar);
@@ -97,7 +104,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&bars->empty[s], 1);
         }
         mbar_init(&bars->x_full, 1);
-        mbar_init(&bars->x_free, 2);  // router/last MMA commit + store-read completion
+        mbar_init(&bars->x_free, 1);  // y stored and routed: X may be refilled
         mbar_init(&bars->qkv_full, 1);
         mbar_init(&bars->qkv_drained, 4);
         mbar_init(&bars->s_full, 1);
@@ -112,16 +119,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_init(&bars->lg_full, 1);
         mbar_init(&bars->lg_drained, 4);
         mbar_init(&bars->drain, 1);
-        mbar_init(&bars->y_all, 4);
         mbar_init(&bars->ep_done, 4);
         bars->abort = 0;
         fence_barrier_init();
         fence_async_shared();
     }
     for (int i = threadIdx.x; i < 256; i += blockDim.x) bars->hist[i] = 0;
-    // P tile: the off-window half of every row stays zero for the whole kernel
-    for (int i = threadIdx.x; i < 32768 / 16; i += blockDim.x) reinterpret_cast<uint4*>(sP)[i] = make_uint4(0, 0, 0, 0);
-    fence_async_shared();
     if (warp == 1) tmem_alloc(&bars->tmem_base, 512);
     tc_fence_before();
     __syncthreads();
@@ -181,7 +184,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ============================ MMA issuer ==============================
         // Order per tile: QKV_0; for h: [Q,K,V^T of h drained] S_h, QKV_{h+1},
         // [P_h ready, O columns free] PV_h, every second head [pair ready] PO += ...
-        // QKV_{h+1} overlaps the softmax of head h; Q/K/V^T smem is double-buffered.
         if (lane == 0) {
             const uint32_t id_qkv = idesc_f16(128, 96), id_s = idesc_f16(128, 128), id_pv = idesc_f16(128, 32),
                            id_po = idesc_f16(128, 128);
@@ -230,20 +232,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!first_tile) wait(&bars->lg_drained, c_lgd.next());
                 issue_qkv();
                 for (int h = 0; h < 8 && ok; ++h) {
-                    const uint32_t qb = smem_u32(sQKV + (h & 1) * kQKVBuf);
+                    const uint32_t vt = smem_u32(sVt + (h & 1) * 8192);
                     wait(&bars->qkv_drained, c_qkvd.next());
                     // ---- S_h = Q K^T
                     for (int k = 0; k < 2; ++k)
-                        mma_f16_ss(tmem + kTS, sdesc(qb + k * 32, SW64), sdesc(qb + 8192 + k * 32, SW64), id_s, k != 0);
+                        mma_f16_ss(tmem + kTS, sdesc(smem_u32(sQ) + k * 32, SW64), sdesc(smem_u32(sK) + k * 32, SW64),
+                                   id_s, k != 0);
                     mma_commit(&bars->s_full);
                     if (h < 7) issue_qkv();
                     wait(&bars->p_ready, c_pr.next());
-                    // O columns free once the epilogue drained the previous head
+                    // O columns free once the softmax group drained the previous head
                     if (h > 0 || !first_tile) wait(&bars->o_drained, c_od.next());
-                    // ---- O_h = P V
+                    // ---- O_h = P V, P (fp16) read from TMEM: 16 keys = 8 columns per MMA
                     for (int k = 0; k < 8; ++k)
-                        mma_f16_ss(tmem + kTO, sdesc(smem_u32(sP) + (k >> 2) * 16384 + (k & 3) * 32, SW128),
-                                   sdesc(qb + 16384 + (k >> 2) * 4096 + (k & 3) * 32, SW128), id_pv, k != 0);
+                        mma_f16_ts(tmem + kTO, tmem + kTS + k * 8, sdesc(vt + (k >> 2) * 4096 + (k & 3) * 32, SW128),
+                                   id_pv, k != 0);
                     mma_commit(&bars->o_full);
                     if (h & 1) {
                         // ---- PO += O_pair . Wo[:, pair]^T
@@ -262,40 +265,36 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
                 mma_commit(&bars->po_full);
-                // ---- router logits = y . Wr^T  (y overwrote X in smem)
+                // ---- router logits = y . Wr^T
                 wait(&bars->y_ready, c_yr.next());
                 if (router) {
+                    const uint32_t ys = xs;  // y overwrote X
                     for (int kc = 0; kc < 4 && ok; ++kc)
                         for (int nh = 0; nh * 128 < npad && ok; ++nh) {
                             const uint32_t b = ring_wait();
                             if (!ok) break;
 #pragma unroll
                             for (int k = 0; k < 4; ++k)
-                                mma_f16_ss(tmem + kTQKV + nh * 128, sdesc(xs + kc * 16384 + k * 32, SW128),
+                                mma_f16_ss(tmem + kTQKV + nh * 128, sdesc(ys + kc * 16384 + k * 32, SW128),
                                            sdesc(b + k * 32, SW128), id_r, (kc | k) != 0);
                             ring_release();
                         }
-                    mma_commit(&bars->lg_full);
                 }
-                mma_commit(&bars->x_free);
+                mma_commit(&bars->lg_full);
                 first_tile = false;
             }
             mma_commit(&bars->drain);
             mbar_wait(&bars->drain, 0, abort);
         }
-    } else {
-        // ============================ epilogue ================================
-        // Per head h: softmax_h -> drain QKV_{h+1} -> O_h (the drain of QKV_0 comes
-        // before the loop).
+    } else if (warp < 6) {
+        // ============================ softmax group ===========================
         const int quad = warp & 3;
         const int r = quad * 32 + lane;  // tile row = TMEM lane
         const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
         const int wnd = r >> 6;  // which window of the tile
-        const int li = r & 63;
-        const int ty = li >> 3, tx = li & 7;
-        const float scale = a.scale;
+        const float c2 = a.scale * 1.4426950408889634f;  // scale * log2(e)
         const int nkeys = a.n_keys;
-        Counter c_qkv, c_s, c_o, c_aof, c_po, c_lg, c_yall;
+        Counter c_s, c_o, c_aof;
         bool ok = true;
         bool first_pair = true;
         auto wait = [&](uint64_t* bar, uint32_t par) {
@@ -306,59 +305,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(bar);
         };
-        // QKV_h (TMEM) -> fp16 Q, K (K-major SW64) and V^T (K-major SW128), buffer h&1
-        auto drain_qkv = [&](int h) {
-            wait(&bars->qkv_full, c_qkv.next());
-            if (!ok) return;
-            unsigned char* buf = sQKV + (h & 1) * kQKVBuf;
-            const float* bq = a.bqkv + h * 96;
-#pragma unroll
-            for (int part = 0; part < 3; ++part) {  // Q, K, V
-                float4 bb[8];
-#pragma unroll
-                for (int i = 0; i < 8; ++i) bb[i] = ldg_f4(bq + part * 32 + 4 * i);
-                uint32_t v[32];
-                tmem_ld32(tmem + lane_addr + kTQKV + part * 32, v);
-                tmem_ld_wait();
-                uint32_t pk[16];
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    pk[2 * i] = pack_h2(__fadd_rn(__uint_as_float(v[4 * i]), bb[i].x),
-                                        __fadd_rn(__uint_as_float(v[4 * i + 1]), bb[i].y));
-                    pk[2 * i + 1] = pack_h2(__fadd_rn(__uint_as_float(v[4 * i + 2]), bb[i].z),
-                                            __fadd_rn(__uint_as_float(v[4 * i + 3]), bb[i].w));
-                }
-                if (part < 2) {
-                    unsigned char* dst = buf + part * 8192;
-#pragma unroll
-                    for (int c = 0; c < 4; ++c)
-                        *reinterpret_cast<uint4*>(dst + sw64_off(r, c)) =
-                            make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-                } else {
-                    // V^T: element (d, r) of a [32 x 128] K-major tile
-                    unsigned char* vt = buf + 16384 + (r >> 6) * 4096 + (r & 7) * 2;
-                    const int vchunk = (r & 63) >> 3;
-#pragma unroll
-                    for (int d = 0; d < 32; d += 2) {
-                        *reinterpret_cast<unsigned short*>(vt + sw128_off(d, vchunk)) = (unsigned short)(pk[d >> 1] & 0xffff);
-                        *reinterpret_cast<unsigned short*>(vt + sw128_off(d + 1, vchunk)) = (unsigned short)(pk[d >> 1] >> 16);
-                    }
-                }
-            }
-            fence_async_shared();
-            tc_fence_before();
-            arrive(&bars->qkv_drained);
-        };
         for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
-            const int w = 2 * tile + wnd;
-            const bool win_ok = w < n_windows;
-            const int f = win_ok ? w / win_per_frame : 0;
-            const int wl = win_ok ? w % win_per_frame : 0;
-            const int wy = wl / wx_n, wx = wl % wx_n;
-            const int gy = wy * 8 + ty, gx = wx * 8 + tx;
-            const bool valid = win_ok && gy < a.H && gx < a.W;
-            const int64_t token = (int64_t)f * a.W * a.H + (int64_t)gy * a.W + gx;
-            drain_qkv(0);
             for (int h = 0; h < 8 && ok; ++h) {
                 // ---- softmax over this row's window (split2_qkv_attn_d256.comp.glsl:59-66)
                 wait(&bars->s_full, c_s.next());
@@ -369,7 +316,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tmem_ld_wait();
                 // s_j = acc_j * scale; p_j = exp(s_j - max_j s_j).  scale > 0, so the max of
                 // the scaled scores is the scaled max; exp(x) = 2^(x log2 e).
-                const float c2 = scale * 1.4426950408889634f;
                 uint32_t pk[32];
                 float se;
                 if (nkeys >= 64) {
@@ -416,19 +362,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 const float inv = __frcp_rn(fmaxf(se, 1e-6f));
                 {
-                    unsigned char* prow = sP + wnd * 16384;
+                    // P row: keys of window A in columns [0, 32), window B in [32, 64);
+                    // this row's keys get the weights, the other window's keys zero
+                    uint32_t zero[32];
 #pragma unroll
-                    for (int c = 0; c < 8; ++c)
-                        *reinterpret_cast<uint4*>(prow + sw128_off(r, c)) =
-                            make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+                    for (int j = 0; j < 32; ++j) zero[j] = 0u;
+                    tmem_st32(tmem + lane_addr + kTS + wnd * 32, pk);
+                    tmem_st32(tmem + lane_addr + kTS + (wnd ^ 1) * 32, zero);
+                    tmem_st_wait();
                 }
-                fence_async_shared();
                 tc_fence_before();
                 arrive(&bars->p_ready);
-
-                // ---- Q, K, V^T of the next head while PV_h runs
-                if (h < 7) drain_qkv(h + 1);
-                if (!ok) break;
 
                 // ---- O_h = PV / sum -> fp16 attention output (head pair tile)
                 wait(&bars->o_full, c_o.next());
@@ -456,6 +400,79 @@ __global__ void __launch_bounds__(kThreads, 1)
                     first_pair = false;
                 }
             }
+        }
+    } else {
+        // ============================ drain group =============================
+        const int quad = warp & 3;
+        const int r = quad * 32 + lane;  // tile row = TMEM lane
+        const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
+        const int wnd = r >> 6;
+        const int li = r & 63;
+        const int ty = li >> 3, tx = li & 7;
+        Counter c_qkv, c_po, c_lg, c_ystore;
+        bool ok = true;
+        bool first_tile = true;
+        const bool storer = (warp == 6 && lane == 0);
+        auto wait = [&](uint64_t* bar, uint32_t par) {
+            if (ok && !mbar_wait(bar, par, abort)) ok = false;
+            tc_fence_after();
+        };
+        auto arrive = [&](uint64_t* bar) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar);
+        };
+        // QKV_h (TMEM) -> fp16 Q, K (K-major SW64) and V^T (K-major SW128), buffer h&1
+        auto drain_qkv = [&](int h) {
+            wait(&bars->qkv_full, c_qkv.next());
+            if (!ok) return;
+            const float* bq = a.bqkv + h * 96;
+#pragma unroll
+            for (int part = 0; part < 3; ++part) {  // Q, K, V
+                float4 bb[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) bb[i] = ldg_f4(bq + part * 32 + 4 * i);
+                uint32_t v[32];
+                tmem_ld32(tmem + lane_addr + kTQKV + part * 32, v);
+                tmem_ld_wait();
+                uint32_t pk[16];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    pk[2 * i] = pack_h2(__fadd_rn(__uint_as_float(v[4 * i]), bb[i].x),
+                                        __fadd_rn(__uint_as_float(v[4 * i + 1]), bb[i].y));
+                    pk[2 * i + 1] = pack_h2(__fadd_rn(__uint_as_float(v[4 * i + 2]), bb[i].z),
+                                            __fadd_rn(__uint_as_float(v[4 * i + 3]), bb[i].w));
+                }
+                if (part < 2) {
+                    unsigned char* dst = part == 0 ? sQ : sK;
+#pragma unroll
+                    for (int c = 0; c < 4; ++c)
+                        *reinterpret_cast<uint4*>(dst + sw64_off(r, c)) =
+                            make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+                } else {
+                    // V^T: element (d, r) of a [32 x 128] K-major tile
+                    unsigned char* vt = sVt + (h & 1) * 8192 + (r >> 6) * 4096 + (r & 7) * 2;
+                    const int vchunk = (r & 63) >> 3;
+#pragma unroll
+                    for (int d = 0; d < 32; d += 2) {
+                        *reinterpret_cast<unsigned short*>(vt + sw128_off(d, vchunk)) = (unsigned short)(pk[d >> 1] & 0xffff);
+                        *reinterpret_cast<unsigned short*>(vt + sw128_off(d + 1, vchunk)) = (unsigned short)(pk[d >> 1] >> 16);
+                    }
+                }
+            }
+            fence_async_shared();
+            tc_fence_before();
+            arrive(&bars->qkv_drained);
+        };
+        for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
+            const int w = 2 * tile + wnd;
+            const bool win_ok = w < n_windows;
+            const int f = win_ok ? w / win_per_frame : 0;
+            const int wl = win_ok ? w % win_per_frame : 0;
+            const int wy = wl / wx_n, wx = wl % wx_n;
+            const int gy = wy * 8 + ty, gx = wx * 8 + tx;
+            const bool valid = win_ok && gy < a.H && gx < a.W;
+            const int64_t token = (int64_t)f * a.W * a.H + (int64_t)gy * a.W + gx;
+            for (int h = 0; h < 8 && ok; ++h) drain_qkv(h);
             if (!ok) break;
 
             // ---- y = fp16(fp16(PO + bo) + x), written over X (same swizzled slot)
@@ -469,29 +486,29 @@ __global__ void __launch_bounds__(kThreads, 1)
                 uint32_t v[32];
                 tmem_ld32(tmem + lane_addr + kTPO + g * 32, v);
                 tmem_ld_wait();
-                unsigned char* blk = sX + (g >> 1) * 16384;
+                unsigned char* xblk = sX + (g >> 1) * 16384;
+                unsigned char* yblk = xblk;
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
-                    uint4* px = reinterpret_cast<uint4*>(blk + sw128_off(r, (g & 1) * 4 + c));
-                    const uint4 x = *px;
+                    const int off = sw128_off(r, (g & 1) * 4 + c);
+                    const uint4 x = *reinterpret_cast<const uint4*>(xblk + off);
                     const float4 b0 = bb[2 * c], b1 = bb[2 * c + 1];
-                    const float* f = reinterpret_cast<const float*>(&v[8 * c]);
+                    const float* fv = reinterpret_cast<const float*>(&v[8 * c]);
                     // y = h( h(PO + bo) + x ): the second rounding is the fp16 add of :76
                     uint4 y;
-                    y.x = hadd2_u32(pack_h2(__fadd_rn(f[0], b0.x), __fadd_rn(f[1], b0.y)), x.x);
-                    y.y = hadd2_u32(pack_h2(__fadd_rn(f[2], b0.z), __fadd_rn(f[3], b0.w)), x.y);
-                    y.z = hadd2_u32(pack_h2(__fadd_rn(f[4], b1.x), __fadd_rn(f[5], b1.y)), x.z);
-                    y.w = hadd2_u32(pack_h2(__fadd_rn(f[6], b1.z), __fadd_rn(f[7], b1.w)), x.w);
-                    *px = y;
+                    y.x = hadd2_u32(pack_h2(__fadd_rn(fv[0], b0.x), __fadd_rn(fv[1], b0.y)), x.x);
+                    y.y = hadd2_u32(pack_h2(__fadd_rn(fv[2], b0.z), __fadd_rn(fv[3], b0.w)), x.y);
+                    y.z = hadd2_u32(pack_h2(__fadd_rn(fv[4], b1.x), __fadd_rn(fv[5], b1.y)), x.z);
+                    y.w = hadd2_u32(pack_h2(__fadd_rn(fv[6], b1.z), __fadd_rn(fv[7], b1.w)), x.w);
+                    *reinterpret_cast<uint4*>(yblk + off) = y;
                 }
             }
             tc_fence_before();
             arrive(&bars->po_drained);
             fence_async_shared();
             arrive(&bars->y_ready);
-            arrive(&bars->y_all);
             // one thread stores both windows once every row of y is in smem
-            if (threadIdx.x == 64 && mbar_wait(&bars->y_all, c_yall.next(), abort)) {
+            if (storer && mbar_wait(&bars->y_ready, c_ystore.next(), abort)) {
                 for (int half = 0; half < 2; ++half) {
                     const int w2 = 2 * tile + half;
                     if (w2 >= n_windows) continue;
@@ -504,9 +521,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
 
             // ---- router: logits = fp16(y . Wr^T + br), first maximum
+            wait(&bars->lg_full, c_lg.next());
+            if (!ok) break;
             if (router) {
-                wait(&bars->lg_full, c_lg.next());
-                if (!ok) break;
                 int best = 0;
                 float bv = 0.0f;
 #pragma unroll 1
@@ -533,16 +550,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             tc_fence_before();
             arrive(&bars->lg_drained);
-            if (threadIdx.x == 64) {
-                tma_store_wait_read0();  // y left smem: X may be refilled
+            if (storer) {
+                tma_store_wait_read0();  // y has left smem and the router MMA is done with it
                 mbar_arrive(&bars->x_free);
             }
+            first_tile = false;
         }
-        if (threadIdx.x == 64) tma_store_wait0();
-        // flush the CTA's routing histogram once every epilogue warp is done
+        if (storer) tma_store_wait0();
+        // flush the CTA's routing histogram once every drain warp is done
         arrive(&bars->ep_done);
         if (mbar_wait(&bars->ep_done, 0, abort) && router)
-            for (int e = threadIdx.x - 64; e < a.n_experts; e += kEpiThreads)
+            for (int e = threadIdx.x - 192; e < a.n_experts; e += 128)
                 if (bars->hist[e]) atomicAdd(&a.counts[e], bars->hist[e]);
     }
 
