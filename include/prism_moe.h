@@ -144,6 +144,29 @@ int prism_expert(prism_ctx* ctx, const prism_expert_params* p,
                  void* features, size_t feature_elems,
                  const int32_t* aux, size_t aux_elems, void* stream);
 
+/* No counterpart in the reference.  Every expert of one MoE pass in one call,
+ * without any device allocation: equivalent to calling prism_expert for expert ids
+ * p->expert_id .. p->expert_id + n_experts - 1, where expert k uses the weight
+ * offsets of p plus (k - p->expert_id) * expert_stride.  For callers that cannot
+ * allocate device memory while the pass runs (e.g. a hook inside a host
+ * application's frame loop, where cudaMalloc may synchronize the device and stall
+ * the frame, or is not allowed after start-up): the routing scratch (counts,
+ * offsets, token permutation, tile list) lives in a fixed device array of about
+ * 300 KB that every GPU loading the library keeps until the process exits.
+ * Limits and rules:
+ *  - p->n_tokens <= PRISM_STATIC_MAX_TOKENS, else PRISM_E_RANGE;
+ *  - the first call on a device looks up the array's device address (with the
+ *    context's device current); make that first call before any stream capture;
+ *  - every call reuses the same array, so calls that overlap on the GPU (other
+ *    streams, other host threads, other contexts on the same device) race: order
+ *    them on one stream. */
+#define PRISM_STATIC_MAX_TOKENS 65536
+int prism_expert_all_static(prism_ctx* ctx, const prism_expert_params* p,
+                            int32_t n_experts, int32_t expert_stride,
+                            const void* weights, size_t weight_elems,
+                            void* features, size_t feature_elems,
+                            const int32_t* aux, size_t aux_elems, void* stream);
+
 /* pw_project_128to256.comp.glsl: out = relu(Wu*x + bu) (prism_moe_bench.cpp:408-412) */
 int prism_proj_up(prism_ctx* ctx, const prism_proj_params* p,
                   const void* weights, size_t weight_elems,

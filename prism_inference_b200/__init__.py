@@ -72,6 +72,14 @@ class Prism:
                                               _ptr(features), features.numel(), _ptr(aux), aux.numel(),
                                               _stream(stream)))
 
+    def expert_all_static(self, p: ExpertParams, n_experts: int, expert_stride: int, weights, features, aux,
+                          stream=None):
+        """All experts of one pass in one call without device allocation
+        (prism_expert_all_static): scratch lives in a fixed per-device array."""
+        check(self.lib, self.lib.prism_expert_all_static(self.h, C.byref(p), n_experts, expert_stride, _ptr(weights),
+                                                         weights.numel(), _ptr(features), features.numel(), _ptr(aux),
+                                                         aux.numel(), _stream(stream)))
+
     def proj_up(self, p: ProjParams, weights, features, stream=None):
         check(self.lib, self.lib.prism_proj_up(self.h, C.byref(p), _ptr(weights), weights.numel(),
                                                _ptr(features), features.numel(), _stream(stream)))

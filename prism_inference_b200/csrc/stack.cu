@@ -18,22 +18,20 @@
 
 #include "attn_tc.cuh"
 #include "common.cuh"
+#include "host_util.h"
 #include "pass_kernels.cuh"
 #include "route_kernels.cuh"
 #include "tc_ffn.cuh"
 
 using namespace prism;
 
-struct prism_ctx {
-    int device;
-    int sm_count;
-};
-
 namespace {
 
 thread_local std::string g_err;
 
-int fail(int code, const char* fmt, ...) {
+}  // namespace
+
+int prism::set_error(int code, const char* fmt, ...) {
     char buf[512];
     va_list ap;
     va_start(ap, fmt);
@@ -43,16 +41,9 @@ int fail(int code, const char* fmt, ...) {
     return code;
 }
 
-struct DeviceGuard {
-    int prev = -1;
-    explicit DeviceGuard(int d) {
-        if (cudaGetDevice(&prev) == cudaSuccess && prev != d) cudaSetDevice(d);
-    }
-    ~DeviceGuard() {
-        int cur;
-        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
-    }
-};
+namespace {
+
+#define fail prism::set_error
 
 #define CUDA_TRY(x)                                                                          \
     do {                                                                                     \
@@ -61,11 +52,6 @@ struct DeviceGuard {
     } while (0)
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
-
-// [off, off + n) inside [0, limit)?
-inline bool in_range(int64_t off, int64_t n, size_t limit) {
-    return off >= 0 && n >= 0 && (uint64_t)(off + n) <= (uint64_t)limit;
-}
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
