@@ -60,13 +60,14 @@ PRISM_DEV float gelu_exact(float x) {
     float t = tanhf(inner);
     return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, t));
 }
+// Fast path: the same polynomial refactored for FMAs,
+// 0.5x(1 + tanh(x(0.7978846 + 0.7978846*0.044715 x^2))) = hx + hx*t with hx = 0.5x.
 PRISM_DEV float gelu_f32(float x) {
-    float c = __fmul_rn(0.044715f, x);
-    c = __fmul_rn(c, x);
-    c = __fmul_rn(c, x);
-    float inner = __fmul_rn(0.7978846f, __fadd_rn(x, c));
-    float t = tanh_approx(inner);
-    return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, t));
+    const float x2 = x * x;
+    const float inner = x * fmaf(0.035677408f, x2, 0.7978846f);
+    const float t = tanh_approx(inner);
+    const float hx = 0.5f * x;
+    return fmaf(hx, t, hx);
 }
 
 // ---- mbarrier -------------------------------------------------------------------

@@ -9,9 +9,11 @@
 // result is rounded to fp16 once (acc + bias), GELU is evaluated in fp32 on that
 // fp16 value and rounded again, the residual add is an fp16 add.
 //
-// Warp roles (320 threads):
-//   warp 0     producer: A rows (cp.async gather for experts, TMA otherwise) and the
-//              W1/W2 K-chunks (TMA, 128B swizzle) through a STAGES-deep ring
+// Warp roles (352 threads):
+//   warp 0     producer: A tile by TMA (contiguous rows) and the W1/W2 K-chunks (TMA,
+//              128B swizzle) through a STAGES-deep ring
+//   warp 10    expert mode: gathers the tile's token rows with cp.async (all row
+//              indices loaded first), independently of the weight ring
 //   warp 1     TMEM allocation + single-thread tcgen05.mma issue
 //   warps 2-9  epilogue: warp w reads TMEM lanes 32*(w%4).. (its rows) and one half
 //              of the columns
@@ -27,7 +29,7 @@ namespace prism {
 
 namespace {
 
-constexpr int kThreads = 320;
+constexpr int kThreads = 352;  // + warp 10: expert-row gather
 constexpr int kEpiWarps = 8;
 
 template <int MODE, int KIN, int HID, int NOUT>
@@ -44,9 +46,17 @@ struct FfnCfg {
     static constexpr int kSmem = kA + kH + kStages * kStage + kBarBytes + 1024;  // + alignment slack
 };
 
+// The epilogue writes the H tile by column halves (warps 2-5: K-blocks [0, n/2),
+// warps 6-9: [n/2, n)), each half in column order, so K-blocks become ready in the
+// order 0, n/2, 1, n/2+1, ...; GEMM2 consumes them (and the producer loads W2) in it.
+template <int HID>
+__host__ __device__ constexpr int h_block_order(int i) {
+    return (i & 1) ? (HID / 128) + (i >> 1) : (i >> 1);
+}
+
 struct Bars {
     uint64_t full[4], empty[4];
-    uint64_t a_full, a_empty, acc1_full, acc1_empty, h_full, acc2_full, acc2_empty, drain;
+    uint64_t a_full, a_empty, acc1_full, acc1_empty, h_full[4], acc2_full, acc2_empty, drain;
     uint32_t tmem_base;
     int abort;
 };
@@ -75,10 +85,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&bars->empty[s], 1);
         }
         mbar_init(&bars->a_full, MODE == FFN_EXPERT ? 32 : 1);
-        mbar_init(&bars->a_empty, Cfg::kTwoGemm ? kEpiWarps : 1);
+        mbar_init(&bars->a_empty, 1);  // the MMA warp's commit after the last GEMM1 reading A
         mbar_init(&bars->acc1_full, 1);
         mbar_init(&bars->acc1_empty, kEpiWarps);
-        mbar_init(&bars->h_full, kEpiWarps);
+        for (int kb = 0; kb < 4; ++kb) mbar_init(&bars->h_full[kb], kEpiWarps / 2);
         mbar_init(&bars->acc2_full, 1);
         mbar_init(&bars->acc2_empty, kEpiWarps);
         mbar_init(&bars->drain, 1);
@@ -113,26 +123,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             } else {
                 start = tile * 128;
             }
-            // --- A rows (wait until the previous tile released the A buffer)
-            if (!mbar_wait(&bars->a_empty, (it & 1) ^ 1, abort)) { ok = false; break; }
-            if (MODE == FFN_EXPERT) {
-                const uint32_t a_base = smem_u32(sA);
-                for (int r = lane; r < 128; r += 32) {
-                    const bool valid = r < rows;
-                    const int tok = valid ? a.perm[start + r] : 0;
-                    const __half* src = a.x + (size_t)tok * KIN;
+            // --- A rows by TMA (contiguous modes; the expert gather is warp 10's job)
+            if (MODE != FFN_EXPERT) {
+                if (!mbar_wait(&bars->a_empty, (it & 1) ^ 1, abort)) { ok = false; break; }
+                if (lane == 0) {
+                    mbar_expect_tx(&bars->a_full, Cfg::kA);
 #pragma unroll
                     for (int kb = 0; kb < KIN / 64; ++kb)
-#pragma unroll
-                        for (int c = 0; c < 8; ++c)
-                            cp_async16(a_base + kb * 16384 + sw128_off(r, c), src + kb * 64 + c * 8, valid ? 16u : 0u);
+                        tma_load_2d(smem_u32(sA + kb * 16384), &tm_x, &bars->a_full, kb * 64, start);
                 }
-                cp_async_mbar_arrive(&bars->a_full);
-            } else if (lane == 0) {
-                mbar_expect_tx(&bars->a_full, Cfg::kA);
-#pragma unroll
-                for (int kb = 0; kb < KIN / 64; ++kb)
-                    tma_load_2d(smem_u32(sA + kb * 16384), &tm_x, &bars->a_full, kb * 64, start);
             }
             // --- weight K-chunks, in the order the MMA warp consumes them
             for (int c = 0; c < n_chunks && ok; ++c) {
@@ -146,7 +145,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (++stage == Cfg::kStages) { stage = 0; phase ^= 1; }
                 }
                 if (!Cfg::kTwoGemm) continue;
-                for (int kc = 0; kc < HID / 64 && ok; ++kc) {  // GEMM2: W2 columns of this chunk
+                for (int i = 0; i < HID / 64 && ok; ++i) {  // GEMM2: W2 columns, in H hand-off order
+                    const int kc = h_block_order<HID>(i);
                     if (!mbar_wait(&bars->empty[stage], phase ^ 1, abort)) { ok = false; break; }
                     if (lane == 0) {
                         mbar_expect_tx(&bars->full[stage], NOUT * 128);
@@ -159,7 +159,35 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             __syncwarp();
         }
-        asm volatile("cp.async.wait_all;" ::: "memory");
+    } else if (warp == 10) {
+        // ===================== expert-row gather =====================
+        if (MODE == FFN_EXPERT) {
+            uint32_t it = 0;
+            const uint32_t a_base = smem_u32(sA);
+            for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
+                const ExpertTile t = a.tiles[tile];
+                int tok[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {  // every row index first: one round trip
+                    const int r = lane + 32 * i;
+                    tok[i] = r < t.rows ? a.perm[t.start + r] : -1;
+                }
+                if (!mbar_wait(&bars->a_empty, (it & 1) ^ 1, abort)) break;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int r = lane + 32 * i;
+                    const __half* src = a.x + (size_t)(tok[i] < 0 ? 0 : tok[i]) * KIN;
+#pragma unroll
+                    for (int kb = 0; kb < KIN / 64; ++kb)
+#pragma unroll
+                        for (int c = 0; c < 8; ++c)
+                            cp_async16(a_base + kb * 16384 + sw128_off(r, c), src + kb * 64 + c * 8,
+                                       tok[i] < 0 ? 0u : 16u);
+                }
+                cp_async_mbar_arrive(&bars->a_full);
+            }
+            asm volatile("cp.async.wait_all;" ::: "memory");
+        }
     } else if (warp == 1) {
         // ===================== MMA issuer =====================
         constexpr uint32_t idesc1 = idesc_f16(128, HID);
@@ -195,16 +223,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!ok) break;
                 if (lane == 0) {
                     mma_commit(&bars->acc1_full);
-                    if (!Cfg::kTwoGemm) mma_commit(&bars->a_empty);
+                    if (c == n_chunks - 1) mma_commit(&bars->a_empty);  // A tile no longer needed
                 }
                 __syncwarp();
                 if (!Cfg::kTwoGemm) continue;
-                // GEMM2 -> acc2 (columns [256, 256 + NOUT)), A = H from the epilogue
-                if (!mbar_wait(&bars->h_full, chunk_it & 1, abort)) { ok = false; break; }
-                if (!mbar_wait(&bars->acc2_empty, (chunk_it & 1) ^ 1, abort)) { ok = false; break; }
-                fence_async_shared();
-                tc_fence_after();
-                for (int kc = 0; kc < HID / 64; ++kc) {
+                // GEMM2 -> acc2 (columns [256, 256 + NOUT)), A = H from the epilogue,
+                // one K-block at a time as the epilogue hands them over
+                for (int i = 0; i < HID / 64; ++i) {
+                    const int kc = h_block_order<HID>(i);
+                    if (!mbar_wait(&bars->h_full[kc], chunk_it & 1, abort)) { ok = false; break; }
+                    if (i == 0 && !mbar_wait(&bars->acc2_empty, (chunk_it & 1) ^ 1, abort)) { ok = false; break; }
+                    fence_async_shared();
+                    tc_fence_after();
                     if (!mbar_wait(&bars->full[stage], phase, abort)) { ok = false; break; }
                     tc_fence_after();
                     if (lane == 0) {
@@ -213,7 +243,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                         for (int k = 0; k < 4; ++k)
                             mma_f16_ss(tmem + Cfg::kAcc2, sdesc(a0 + k * 32, SW128), sdesc(b0 + k * 32, SW128),
-                                       idesc2, (kc | k) != 0);
+                                       idesc2, (i | k) != 0);
                         mma_commit(&bars->empty[stage]);
                     }
                     __syncwarp();
@@ -228,7 +258,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) mma_commit(&bars->drain);
         __syncwarp();
         mbar_wait(&bars->drain, 0, abort);
-    } else {
+    } else if (warp >= 2 && warp < 2 + kEpiWarps) {
         // ===================== epilogue =====================
         const int quad = warp & 3;               // TMEM lanes 32*quad .. +31
         const int half = (warp - 2) >> 2;        // column half
@@ -295,6 +325,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                         for (int q = 0; q < 4; ++q)
                             *reinterpret_cast<uint4*>(blk + sw128_off(row, ch + q)) =
                                 make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+                        if (g & 1) {  // K-block col0/64 complete for this warp's rows: hand it to GEMM2
+                            fence_async_shared();
+                            __syncwarp();
+                            if (lane == 0) mbar_arrive(&bars->h_full[col0 >> 6]);
+                        }
                     } else if (row_valid) {
                         uint4* dst = reinterpret_cast<uint4*>(a.y + (size_t)out_row * NOUT + col0);
 #pragma unroll
@@ -306,16 +341,42 @@ __global__ void __launch_bounds__(kThreads, 1)
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&bars->acc1_empty);
                 if (!Cfg::kTwoGemm) continue;
-                fence_async_shared();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&bars->h_full);
 
-                // ---- epi2: acc2 -> bias -> fp16 -> (+ residual) -> store
+                // ---- epi2: acc2 -> bias -> fp16 -> (+ residual) -> store.
+                // The residual rows (the A tile, already released to the next gather) are
+                // re-read from global memory (L2) while GEMM2 runs, and the output goes
+                // out through this warp's own slice of the H tile (free once GEMM2 is
+                // done): both global transfers are row-contiguous, 16 lanes per 256 B.
+                const bool last = (c == n_chunks - 1);
+                constexpr int kCols2 = NOUT / 2;           // this warp's column half
+                constexpr int kRowsPerLd = 512 / (kCols2 * 2);  // rows per 512-B warp access
+                constexpr int kLanesPerRow = 32 / kRowsPerLd;
+                constexpr int kIters = 32 / kRowsPerLd;
+                const int sub_row = lane / kLanesPerRow, sub_col = (lane % kLanesPerRow) * 8;  // 8 halves / lane
+                uint4 xres[Cfg::kTwoGemm ? kIters : 1];
+                if (last) {
+#pragma unroll
+                    for (int i = 0; i < kIters; ++i) {
+                        const int lr = i * kRowsPerLd + sub_row;
+                        const int tk = __shfl_sync(0xffffffffu, out_row, lr);
+                        const int vld = __shfl_sync(0xffffffffu, (int)row_valid, lr);
+                        xres[i] = vld ? __ldg(reinterpret_cast<const uint4*>(a.x + (size_t)tk * KIN + half * kCols2 + sub_col))
+                                      : make_uint4(0, 0, 0, 0);
+                    }
+                }
                 if (!mbar_wait(&bars->acc2_full, chunk_it & 1, abort)) { ok = false; break; }
                 tc_fence_after();
                 const float* b2 = a.b2 + (size_t)e * NOUT;
-                const bool last = (c == n_chunks - 1);
-                constexpr int kCols2 = NOUT / 2;
+                // H-tile address of (tile row R, column col) in the K-major SW128 layout
+                auto hslot = [&](int R, int col) -> unsigned char* {
+                    return sH + (col >> 6) * 16384 + sw128_off(R, (col & 63) >> 3);
+                };
+                if (last) {
+#pragma unroll
+                    for (int i = 0; i < kIters; ++i)
+                        *reinterpret_cast<uint4*>(hslot(quad * 32 + i * kRowsPerLd + sub_row, half * kCols2 + sub_col)) = xres[i];
+                    __syncwarp();
+                }
 #pragma unroll
                 for (int g = 0; g < kCols2 / 32; ++g) {
                     const int col0 = half * kCols2 + g * 32;
@@ -339,14 +400,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                         for (int j = 0; j < 16; ++j) accum[g * 16 + j] = hadd2_u32(accum[g * 16 + j], part[j]);
                     }
                     if (!last) continue;
-                    // residual x from the A tile (same row, columns col0.. of K-block col0/64)
-                    const unsigned char* ablk = sA + (col0 >> 6) * 16384;
-                    const int ch = (col0 & 63) >> 3;
-                    uint32_t packed[16];
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
-                        const uint4 x = *reinterpret_cast<const uint4*>(ablk + sw128_off(row, ch + q));
+                        uint4* slot = reinterpret_cast<uint4*>(hslot(row, col0 + 8 * q));
+                        const uint4 x = *slot;
                         const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
+                        uint32_t z[4];
 #pragma unroll
                         for (int j = 0; j < 4; ++j) {
                             const int k = 4 * q + j;
@@ -356,29 +415,30 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 const float bx = (k & 1) ? bb[k >> 1].z : bb[k >> 1].x;
                                 const float by = (k & 1) ? bb[k >> 1].w : bb[k >> 1].y;
                                 const uint32_t acc = accum[g * 16 + k];
-                                packed[k] = pack_h2(
-                                    __fadd_rn(__fsub_rn(lo_h2f(acc), __fmul_rn(corr, bx)), lo_h2f(xs[j])),
-                                    __fadd_rn(__fsub_rn(hi_h2f(acc), __fmul_rn(corr, by)), hi_h2f(xs[j])));
+                                z[j] = pack_h2(__fadd_rn(__fsub_rn(lo_h2f(acc), __fmul_rn(corr, bx)), lo_h2f(xs[j])),
+                                               __fadd_rn(__fsub_rn(hi_h2f(acc), __fmul_rn(corr, by)), hi_h2f(xs[j])));
                             } else {
                                 // z = h(r + y), an fp16 add (moe_expert_skip.comp.glsl:52)
-                                packed[k] = hadd2_u32(part[k], xs[j]);
+                                z[j] = hadd2_u32(part[k], xs[j]);
                             }
                         }
+                        *slot = make_uint4(z[0], z[1], z[2], z[3]);
                     }
-                    if (row_valid) {
-                        uint4* dst = reinterpret_cast<uint4*>(a.y + (size_t)out_row * NOUT + col0);
+                }
+                if (last) {
+                    __syncwarp();
 #pragma unroll
-                        for (int q = 0; q < 4; ++q)
-                            dst[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+                    for (int i = 0; i < kIters; ++i) {
+                        const int lr = i * kRowsPerLd + sub_row;
+                        const int tk = __shfl_sync(0xffffffffu, out_row, lr);
+                        const int vld = __shfl_sync(0xffffffffu, (int)row_valid, lr);
+                        const uint4 v = *reinterpret_cast<const uint4*>(hslot(quad * 32 + lr, half * kCols2 + sub_col));
+                        if (vld) *reinterpret_cast<uint4*>(a.y + (size_t)tk * NOUT + half * kCols2 + sub_col) = v;
                     }
                 }
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&bars->acc2_empty);
-            }
-            if (Cfg::kTwoGemm && ok) {
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&bars->a_empty);  // residual read done
             }
         }
     }
