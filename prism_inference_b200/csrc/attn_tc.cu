@@ -184,7 +184,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ============================ MMA issuer ==============================
         // Order per tile: QKV_0; for h: [Q,K,V^T of h drained] S_h, QKV_{h+1},
         // [P_h ready, O columns free] PV_h, every second head [pair ready] PO += ...
-        if (lane == 0) {
+        {
             const uint32_t id_qkv = idesc_f16(128, 96), id_s = idesc_f16(128, 128), id_pv = idesc_f16(128, 32),
                            id_po = idesc_f16(128, 128);
             const int rn = npad > 128 ? 128 : npad;
@@ -195,7 +195,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool ok = true;
             bool first_tile = true;
             auto ring_wait = [&]() -> uint32_t {
-                if (!mbar_wait(&bars->full[stage], phase, abort)) {
+                if (!mbar_wait_w(&bars->full[stage], phase, abort)) {
                     ok = false;
                     return 0;
                 }
@@ -203,14 +203,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 return smem_u32(sW + stage * kStage);
             };
             auto ring_release = [&]() {
-                mma_commit(&bars->empty[stage]);
+                mma_commit_w(&bars->empty[stage]);
                 if (++stage == kStages) {
                     stage = 0;
                     phase ^= 1;
                 }
             };
             auto wait = [&](uint64_t* bar, uint32_t par) {
-                if (ok && !mbar_wait(bar, par, abort)) ok = false;
+                if (ok && !mbar_wait_w(bar, par, abort)) ok = false;
                 tc_fence_after();
             };
             const uint32_t xs = smem_u32(sX);
@@ -220,11 +220,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (!ok) break;
 #pragma unroll
                     for (int k = 0; k < 4; ++k)
-                        mma_f16_ss(tmem + kTQKV, sdesc(xs + kc * 16384 + k * 32, SW128), sdesc(b + k * 32, SW128),
+                        mma_f16_ss_w(tmem + kTQKV, sdesc(xs + kc * 16384 + k * 32, SW128), sdesc(b + k * 32, SW128),
                                    id_qkv, (kc | k) != 0);
                     ring_release();
                 }
-                mma_commit(&bars->qkv_full);
+                mma_commit_w(&bars->qkv_full);
             };
             for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
                 wait(&bars->x_full, c_xfull.next());
@@ -236,18 +236,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                     wait(&bars->qkv_drained, c_qkvd.next());
                     // ---- S_h = Q K^T
                     for (int k = 0; k < 2; ++k)
-                        mma_f16_ss(tmem + kTS, sdesc(smem_u32(sQ) + k * 32, SW64), sdesc(smem_u32(sK) + k * 32, SW64),
+                        mma_f16_ss_w(tmem + kTS, sdesc(smem_u32(sQ) + k * 32, SW64), sdesc(smem_u32(sK) + k * 32, SW64),
                                    id_s, k != 0);
-                    mma_commit(&bars->s_full);
+                    mma_commit_w(&bars->s_full);
                     if (h < 7) issue_qkv();
                     wait(&bars->p_ready, c_pr.next());
                     // O columns free once the softmax group drained the previous head
                     if (h > 0 || !first_tile) wait(&bars->o_drained, c_od.next());
                     // ---- O_h = P V, P (fp16) read from TMEM: 16 keys = 8 columns per MMA
                     for (int k = 0; k < 8; ++k)
-                        mma_f16_ts(tmem + kTO, tmem + kTS + k * 8, sdesc(vt + (k >> 2) * 4096 + (k & 3) * 32, SW128),
+                        mma_f16_ts_w(tmem + kTO, tmem + kTS + k * 8, sdesc(vt + (k >> 2) * 4096 + (k & 3) * 32, SW128),
                                    id_pv, k != 0);
-                    mma_commit(&bars->o_full);
+                    mma_commit_w(&bars->o_full);
                     if (h & 1) {
                         // ---- PO += O_pair . Wo[:, pair]^T
                         wait(&bars->ao_ready, c_aor.next());
@@ -257,14 +257,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                             if (!ok) break;
 #pragma unroll
                             for (int k = 0; k < 4; ++k)
-                                mma_f16_ss(tmem + kTPO + nh * 128, sdesc(smem_u32(sAO) + k * 32, SW128),
+                                mma_f16_ss_w(tmem + kTPO + nh * 128, sdesc(smem_u32(sAO) + k * 32, SW128),
                                            sdesc(b + k * 32, SW128), id_po, (h > 1) || (k != 0));
                             ring_release();
                         }
-                        mma_commit(&bars->ao_free);
+                        mma_commit_w(&bars->ao_free);
                     }
                 }
-                mma_commit(&bars->po_full);
+                mma_commit_w(&bars->po_full);
                 // ---- router logits = y . Wr^T
                 wait(&bars->y_ready, c_yr.next());
                 if (router) {
@@ -275,16 +275,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                             if (!ok) break;
 #pragma unroll
                             for (int k = 0; k < 4; ++k)
-                                mma_f16_ss(tmem + kTQKV + nh * 128, sdesc(ys + kc * 16384 + k * 32, SW128),
+                                mma_f16_ss_w(tmem + kTQKV + nh * 128, sdesc(ys + kc * 16384 + k * 32, SW128),
                                            sdesc(b + k * 32, SW128), id_r, (kc | k) != 0);
                             ring_release();
                         }
                 }
-                mma_commit(&bars->lg_full);
+                mma_commit_w(&bars->lg_full);
                 first_tile = false;
             }
-            mma_commit(&bars->drain);
-            mbar_wait(&bars->drain, 0, abort);
+            mma_commit_w(&bars->drain);
+            mbar_wait_w(&bars->drain, 0, abort);
         }
     } else if (warp < 6) {
         // ============================ softmax group ===========================

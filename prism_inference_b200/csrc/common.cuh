@@ -112,6 +112,11 @@ PRISM_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
         }
     }
 }
+// Bounded wait by a whole warp with a warp-uniform result: a lane whose wait timed
+// out raises *abort, which ends every other lane's wait at its next check.
+PRISM_DEV bool mbar_wait_w(uint64_t* bar, uint32_t parity, volatile int* abort) {
+    return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort));
+}
 // cp.async (non-bulk) completion tracked by an mbarrier: one arrival per thread.
 PRISM_DEV void cp_async_mbar_arrive(uint64_t* bar) {
     asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
@@ -187,6 +192,38 @@ PRISM_DEV void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint
         "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
+// Warp-collective issue.  The whole issuing warp runs the control flow around its
+// MMAs (loops, waits, branches) converged, and `elect.sync` picks the lane that
+// issues.  Measured on B200: a 128x128x16 MMA issued from a lane that has branched
+// away from its warp costs ~128 cycles whenever any branch or wait separates it from
+// the next MMA, against 64 cycles of tensor-pipe time when issued converged.
+PRISM_DEV void mma_f16_ss_w(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p, e;\n\t.reg .b32 r;\n\t"
+        "elect.sync r|e, 0xffffffff;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+PRISM_DEV void mma_f16_ts_w(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p, e;\n\t.reg .b32 r;\n\t"
+        "elect.sync r|e, 0xffffffff;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+PRISM_DEV void mma_commit_w(uint64_t* bar) {
+    asm volatile(
+        "{\n\t.reg .pred e;\n\t.reg .b32 r;\n\t"
+        "elect.sync r|e, 0xffffffff;\n\t"
+        "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(
+            smem_u32(bar))
+        : "memory");
+}
+
 // tcgen05.st 32 lanes x 32 bit, 32 consecutive columns from 32 registers per thread
 PRISM_DEV void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
     asm volatile(

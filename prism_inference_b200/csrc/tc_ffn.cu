@@ -190,6 +190,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp == 1) {
         // ===================== MMA issuer =====================
+        // the whole warp runs this role converged; one elected lane issues
         constexpr uint32_t idesc1 = idesc_f16(128, HID);
         constexpr uint32_t idesc2 = idesc_f16(128, NOUT);
         int stage = 0;
@@ -198,66 +199,59 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t chunk_it = 0;  // counts (tile, chunk) pairs for the acc barriers
         bool ok = true;
         for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, ++it) {
-            if (!mbar_wait(&bars->a_full, it & 1, abort)) { ok = false; break; }
+            if (!mbar_wait_w(&bars->a_full, it & 1, abort)) { ok = false; break; }
             fence_async_shared();
             tc_fence_after();
             for (int c = 0; c < n_chunks && ok; ++c, ++chunk_it) {
                 // GEMM1 -> acc1 (columns [0, HID))
-                if (!mbar_wait(&bars->acc1_empty, (chunk_it & 1) ^ 1, abort)) { ok = false; break; }
+                if (!mbar_wait_w(&bars->acc1_empty, (chunk_it & 1) ^ 1, abort)) { ok = false; break; }
                 tc_fence_after();
                 for (int kc = 0; kc < KIN / 64; ++kc) {
-                    if (!mbar_wait(&bars->full[stage], phase, abort)) { ok = false; break; }
+                    if (!mbar_wait_w(&bars->full[stage], phase, abort)) { ok = false; break; }
                     tc_fence_after();
-                    if (lane == 0) {
+                    {
                         const uint32_t a0 = smem_u32(sA + kc * 16384);
                         const uint32_t b0 = smem_u32(sW + stage * Cfg::kStage);
 #pragma unroll
                         for (int k = 0; k < 4; ++k)
-                            mma_f16_ss(tmem, sdesc(a0 + k * 32, SW128), sdesc(b0 + k * 32, SW128), idesc1,
-                                       (kc | k) != 0);
-                        mma_commit(&bars->empty[stage]);
+                            mma_f16_ss_w(tmem, sdesc(a0 + k * 32, SW128), sdesc(b0 + k * 32, SW128), idesc1,
+                                         (kc | k) != 0);
+                        mma_commit_w(&bars->empty[stage]);
                     }
-                    __syncwarp();
                     if (++stage == Cfg::kStages) { stage = 0; phase ^= 1; }
                 }
                 if (!ok) break;
-                if (lane == 0) {
-                    mma_commit(&bars->acc1_full);
-                    if (c == n_chunks - 1) mma_commit(&bars->a_empty);  // A tile no longer needed
-                }
-                __syncwarp();
+                mma_commit_w(&bars->acc1_full);
+                if (c == n_chunks - 1) mma_commit_w(&bars->a_empty);  // A tile no longer needed
                 if (!Cfg::kTwoGemm) continue;
                 // GEMM2 -> acc2 (columns [256, 256 + NOUT)), A = H from the epilogue,
                 // one K-block at a time as the epilogue hands them over
                 for (int i = 0; i < HID / 64; ++i) {
                     const int kc = h_block_order<HID>(i);
-                    if (!mbar_wait(&bars->h_full[kc], chunk_it & 1, abort)) { ok = false; break; }
-                    if (i == 0 && !mbar_wait(&bars->acc2_empty, (chunk_it & 1) ^ 1, abort)) { ok = false; break; }
+                    if (!mbar_wait_w(&bars->h_full[kc], chunk_it & 1, abort)) { ok = false; break; }
+                    if (i == 0 && !mbar_wait_w(&bars->acc2_empty, (chunk_it & 1) ^ 1, abort)) { ok = false; break; }
                     fence_async_shared();
                     tc_fence_after();
-                    if (!mbar_wait(&bars->full[stage], phase, abort)) { ok = false; break; }
+                    if (!mbar_wait_w(&bars->full[stage], phase, abort)) { ok = false; break; }
                     tc_fence_after();
-                    if (lane == 0) {
+                    {
                         const uint32_t a0 = smem_u32(sH + kc * 16384);
                         const uint32_t b0 = smem_u32(sW + stage * Cfg::kStage);
 #pragma unroll
                         for (int k = 0; k < 4; ++k)
-                            mma_f16_ss(tmem + Cfg::kAcc2, sdesc(a0 + k * 32, SW128), sdesc(b0 + k * 32, SW128),
-                                       idesc2, (i | k) != 0);
-                        mma_commit(&bars->empty[stage]);
+                            mma_f16_ss_w(tmem + Cfg::kAcc2, sdesc(a0 + k * 32, SW128), sdesc(b0 + k * 32, SW128),
+                                         idesc2, (i | k) != 0);
+                        mma_commit_w(&bars->empty[stage]);
                     }
-                    __syncwarp();
                     if (++stage == Cfg::kStages) { stage = 0; phase ^= 1; }
                 }
                 if (!ok) break;
-                if (lane == 0) mma_commit(&bars->acc2_full);
-                __syncwarp();
+                mma_commit_w(&bars->acc2_full);
             }
         }
         // every issued MMA has completed before TMEM is released
-        if (lane == 0) mma_commit(&bars->drain);
-        __syncwarp();
-        mbar_wait(&bars->drain, 0, abort);
+        mma_commit_w(&bars->drain);
+        mbar_wait_w(&bars->drain, 0, abort);
     } else if (warp >= 2 && warp < 2 + kEpiWarps) {
         // ===================== epilogue =====================
         const int quad = warp & 3;               // TMEM lanes 32*quad .. +31
