@@ -29,8 +29,11 @@
 //   warps 2-5   softmax group: S_h -> P_h, O_h -> attention-output tile
 //   warps 6-9   drain group: QKV_h -> Q/K/V^T smem, y epilogue, store, router
 // Thread = tile row = TMEM lane in both groups (warp w reads lanes 32*(w%4)..).
-// The two groups run one head apart and the MMA warp issues QKV_{h+1} right after S_h;
-// the 7-stage weight ring (112 KB) keeps the L2 -> smem weight stream ahead of it.
+// The two groups run one head apart and the MMA warp issues QKV_{h+1} right after S_h.
+// Weights stream through a 2 x 48 KB ring in whole operands, one TMA load each: a
+// head's Wqkv rows at full K (K-block-major copy, 3-D map), a head pair's Wo columns,
+// up to 96 router rows.  On B200 every load costs the producer/consumer hand-off
+// (~300-400 cycles) whatever its size, so few large loads keep the stream ahead.
 // Every wait is bounded (common.cuh); on timeout the CTA sets the error word and
 // winds down.  No TMA multicast.
 #include "attn_tc.cuh"
@@ -40,8 +43,9 @@ namespace prism {
 namespace {
 
 constexpr int kThreads = 320;  // 10 warps
-constexpr int kStage = 16384;  // weight ring stage: [<=128 rows][64] fp16
-constexpr int kStages = 7;
+constexpr int kStage = 49152;  // weight ring stage: up to 4 K-blocks x [96 rows][128 B], or [256][128 B]
+constexpr int kStages = 2;
+constexpr int kRouterRows = 96;  // router rows per ring stage
 
 // shared-memory map (offsets from the 1024-aligned base)
 constexpr int kOffX = 0;                // 4 K-blocks x [128][128 B] = 64 KB; y overwrites it
@@ -49,7 +53,7 @@ constexpr int kOffQ = kOffX + 65536;    // Q_h [128][64 B] SW64 8 KB
 constexpr int kOffK = kOffQ + 8192;     // K_h [128][64 B] SW64 8 KB
 constexpr int kOffVt = kOffK + 8192;    // V_h^T, 2 buffers (head parity) x 2 x [32][128 B] SW128 = 16 KB
 constexpr int kOffAO = kOffVt + 16384;  // [128][128 B] SW128 16 KB
-constexpr int kOffW = kOffAO + 16384;   // ring 7 x 16 KB
+constexpr int kOffW = kOffAO + 16384;   // ring 2 x 48 KB
 constexpr int kOffBar = kOffW + kStages * kStage;
 
 // TMEM columns
@@ -142,16 +146,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t phase = 0;
             Counter c_xfree;
             bool ok = true;
-            auto ring_load = [&](const CUtensorMap* map, int c0, int c1, uint32_t bytes) -> bool {
+            // one ring stage = one TMA load (3-D maps: rows c1.. at every K-block)
+            auto ring_load = [&](const CUtensorMap* map, bool kb3d, int c0, int c1, uint32_t bytes) -> bool {
                 if (!mbar_wait(&bars->empty[stage], phase ^ 1, abort)) return false;
                 mbar_expect_tx(&bars->full[stage], bytes);
-                tma_load_2d(smem_u32(sW + stage * kStage), map, &bars->full[stage], c0, c1);
+                if (kb3d)
+                    tma_load_3d(smem_u32(sW + stage * kStage), map, &bars->full[stage], 0, c1, 0);
+                else
+                    tma_load_2d(smem_u32(sW + stage * kStage), map, &bars->full[stage], c0, c1);
                 if (++stage == kStages) {
                     stage = 0;
                     phase ^= 1;
                 }
                 return true;
             };
+            const int r_rows = npad < kRouterRows ? npad : kRouterRows;  // rows per router load
             for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
                 if (!mbar_wait(&bars->x_free, c_xfree.next_free(), abort)) break;
                 mbar_expect_tx(&bars->x_full, 65536);
@@ -167,17 +176,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 // same order as the MMA warp consumes: QKV_0, then per head h
                 // QKV_{h+1} and, after every second head, the Wo columns of the pair
-                for (int kc = 0; kc < 4 && ok; ++kc) ok = ring_load(&tm_wqkv, kc * 64, 0, 96 * 128);
+                ok = ring_load(&tm_wqkv, true, 0, 0, 96 * 512);
                 for (int h = 0; h < 8 && ok; ++h) {
-                    if (h < 7)
-                        for (int kc = 0; kc < 4 && ok; ++kc) ok = ring_load(&tm_wqkv, kc * 64, (h + 1) * 96, 96 * 128);
-                    if (h & 1)
-                        for (int nh = 0; nh < 2 && ok; ++nh) ok = ring_load(&tm_wo, (h >> 1) * 64, nh * 128, 128 * 128);
+                    if (h < 7) ok = ring_load(&tm_wqkv, true, 0, (h + 1) * 96, 96 * 512);
+                    if ((h & 1) && ok) ok = ring_load(&tm_wo, false, (h >> 1) * 64, 0, 256 * 128);
                 }
                 if (router)
-                    for (int kc = 0; kc < 4 && ok; ++kc)
-                        for (int nh = 0; nh * 128 < npad && ok; ++nh)
-                            ok = ring_load(&tm_wr, kc * 64, nh * 128, (uint32_t)min(128, npad) * 128);
+                    for (int r0 = 0; r0 < npad && ok; r0 += kRouterRows)
+                        ok = ring_load(&tm_wr, true, 0, r0, (uint32_t)r_rows * 512);
             }
         }
     } else if (warp == 1) {
@@ -187,8 +193,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         {
             const uint32_t id_qkv = idesc_f16(128, 96), id_s = idesc_f16(128, 128), id_pv = idesc_f16(128, 32),
                            id_po = idesc_f16(128, 128);
-            const int rn = npad > 128 ? 128 : npad;
-            const uint32_t id_r = idesc_f16(128, rn);
+            const int r_rows = npad < kRouterRows ? npad : kRouterRows;
             int stage = 0;
             uint32_t phase = 0;
             Counter c_xfull, c_qkvd, c_pr, c_od, c_aor, c_pod, c_yr, c_lgd;
@@ -215,13 +220,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             };
             const uint32_t xs = smem_u32(sX);
             auto issue_qkv = [&]() {
-                for (int kc = 0; kc < 4 && ok; ++kc) {
-                    const uint32_t b = ring_wait();
-                    if (!ok) break;
+                const uint32_t b = ring_wait();  // Wqkv_h: K-block kc at +kc * 96 rows
+                if (ok) {
 #pragma unroll
-                    for (int k = 0; k < 4; ++k)
-                        mma_f16_ss_w(tmem + kTQKV, sdesc(xs + kc * 16384 + k * 32, SW128), sdesc(b + k * 32, SW128),
-                                   id_qkv, (kc | k) != 0);
+                    for (int kc = 0; kc < 4; ++kc)
+#pragma unroll
+                        for (int k = 0; k < 4; ++k)
+                            mma_f16_ss_w(tmem + kTQKV, sdesc(xs + kc * 16384 + k * 32, SW128),
+                                         sdesc(b + kc * 12288 + k * 32, SW128), id_qkv, (kc | k) != 0);
                     ring_release();
                 }
                 mma_commit_w(&bars->qkv_full);
@@ -252,13 +258,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                         // ---- PO += O_pair . Wo[:, pair]^T
                         wait(&bars->ao_ready, c_aor.next());
                         if (h == 1 && !first_tile) wait(&bars->po_drained, c_pod.next());
-                        for (int nh = 0; nh < 2 && ok; ++nh) {
-                            const uint32_t b = ring_wait();
-                            if (!ok) break;
+                        const uint32_t b = ring_wait();  // Wo[:, pair]: output rows 128 nh.. at +16 KB nh
+                        if (ok) {
 #pragma unroll
-                            for (int k = 0; k < 4; ++k)
-                                mma_f16_ss_w(tmem + kTPO + nh * 128, sdesc(smem_u32(sAO) + k * 32, SW128),
-                                           sdesc(b + k * 32, SW128), id_po, (h > 1) || (k != 0));
+                            for (int nh = 0; nh < 2; ++nh)
+#pragma unroll
+                                for (int k = 0; k < 4; ++k)
+                                    mma_f16_ss_w(tmem + kTPO + nh * 128, sdesc(smem_u32(sAO) + k * 32, SW128),
+                                                 sdesc(b + nh * 16384 + k * 32, SW128), id_po, (h > 1) || (k != 0));
                             ring_release();
                         }
                         mma_commit_w(&bars->ao_free);
@@ -269,16 +276,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                 wait(&bars->y_ready, c_yr.next());
                 if (router) {
                     const uint32_t ys = xs;  // y overwrote X
-                    for (int kc = 0; kc < 4 && ok; ++kc)
-                        for (int nh = 0; nh * 128 < npad && ok; ++nh) {
-                            const uint32_t b = ring_wait();
-                            if (!ok) break;
+                    // up to 96 expert rows per stage (K-block kc at +kc * r_rows rows);
+                    // their logits land in columns kTQKV + r0 ..
+                    for (int r0 = 0; r0 < npad && ok; r0 += kRouterRows) {
+                        const uint32_t b = ring_wait();
+                        if (!ok) break;
+                        const int n = npad - r0 < r_rows ? npad - r0 : r_rows;
+                        const uint32_t id_r = idesc_f16(128, n);
+#pragma unroll
+                        for (int kc = 0; kc < 4; ++kc)
 #pragma unroll
                             for (int k = 0; k < 4; ++k)
-                                mma_f16_ss_w(tmem + kTQKV + nh * 128, sdesc(ys + kc * 16384 + k * 32, SW128),
-                                           sdesc(b + k * 32, SW128), id_r, (kc | k) != 0);
-                            ring_release();
-                        }
+                                mma_f16_ss_w(tmem + kTQKV + r0, sdesc(ys + kc * 16384 + k * 32, SW128),
+                                             sdesc(b + kc * r_rows * 128 + k * 32, SW128), id_r, (kc | k) != 0);
+                        ring_release();
+                    }
                 }
                 mma_commit_w(&bars->lg_full);
                 first_tile = false;

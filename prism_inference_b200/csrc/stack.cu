@@ -81,6 +81,32 @@ int make_map_2d(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, 
     return PRISM_OK;
 }
 
+// K-block-major fp16 weight [cols/64][rows][64] (see kb_major), box {64, box_rows, cols/64}:
+// one load brings box_rows rows at their full K, one [box_rows][128 B] swizzled tile per
+// 64-wide K-block.
+int make_map_kb3d(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+    auto fn = encode_fn();
+    if (!fn) return fail(PRISM_E_CUDA, "cuTensorMapEncodeTiled is not available");
+    if (((uintptr_t)base & 15) || cols % 64) return fail(PRISM_E_ALIGN, "K-block weight map: bad base or width");
+    cuuint64_t dims[3] = {64, rows, cols / 64};
+    cuuint64_t strides[2] = {128, rows * 128};
+    cuuint32_t box[3] = {64, box_rows, (cuuint32_t)(cols / 64)};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(PRISM_E_CUDA, "cuTensorMapEncodeTiled (3d) failed (%d)", (int)r);
+    return PRISM_OK;
+}
+
+// [rows][cols] -> [cols/64][rows][64]
+std::vector<uint16_t> kb_major(const std::vector<uint16_t>& m, size_t rows, size_t cols) {
+    std::vector<uint16_t> o(m.size());
+    for (size_t r = 0; r < rows; ++r)
+        for (size_t c = 0; c < cols; ++c) o[(c / 64) * rows * 64 + r * 64 + (c % 64)] = m[r * cols + c];
+    return o;
+}
+
 // 4-D fp16 activation tensor (C, X=W, Y=H, F) HWC per frame, box {64, 8, 8, 1}, 128B swizzle:
 // one box is one 8x8 window, 64 channels, rows in window-slot order.
 int make_map_act4d(CUtensorMap* m, const void* base, int C, int W, int H, int F) {
@@ -552,10 +578,11 @@ extern "C" int prism_stack_create(prism_ctx* ctx, const prism_stack_desc* desc, 
                 }
             copy_mat(wo, 0, fb.d.out_w, 256, 256, 256);
             copy_bias(bo, 0, fb.d.out_b, 256);
-            if ((rc = upload(st, (uint16_t**)&fb.wqkv, wqkv)) || (rc = upload(st, &fb.bqkv, bqkv)) ||
+            // Wqkv K-block-major: one TMA load brings a head's 96 rows at full K
+            if ((rc = upload(st, (uint16_t**)&fb.wqkv, kb_major(wqkv, 768, 256))) || (rc = upload(st, &fb.bqkv, bqkv)) ||
                 (rc = upload(st, (uint16_t**)&fb.wo, wo)) || (rc = upload(st, &fb.bo, bo)))
                 return fail_cleanup(rc);
-            if ((rc = make_map_2d(&fb.tm_wqkv, fb.wqkv, 768, 256, 96)) || (rc = make_map_2d(&fb.tm_wo, fb.wo, 256, 256, 128)))
+            if ((rc = make_map_kb3d(&fb.tm_wqkv, fb.wqkv, 768, 256, 96)) || (rc = make_map_2d(&fb.tm_wo, fb.wo, 256, 256, 256)))
                 return fail_cleanup(rc);
             if (fb.d.kind == PRISM_BLOCK_MOE) {
                 fb.npad = (fb.d.n_experts + 15) / 16 * 16;
@@ -563,8 +590,9 @@ extern "C" int prism_stack_create(prism_ctx* ctx, const prism_stack_desc* desc, 
                 std::vector<float> br(fb.npad, 0.0f);
                 copy_mat(wr, 0, fb.d.router_w, fb.d.n_experts, 256, 256);
                 copy_bias(br, 0, fb.d.router_b, fb.d.n_experts);
-                if ((rc = upload(st, (uint16_t**)&fb.wr, wr)) || (rc = upload(st, &fb.br, br))) return fail_cleanup(rc);
-                if ((rc = make_map_2d(&fb.tm_wr, fb.wr, fb.npad, 256, std::min(128, fb.npad)))) return fail_cleanup(rc);
+                if ((rc = upload(st, (uint16_t**)&fb.wr, kb_major(wr, fb.npad, 256))) || (rc = upload(st, &fb.br, br)))
+                    return fail_cleanup(rc);
+                if ((rc = make_map_kb3d(&fb.tm_wr, fb.wr, fb.npad, 256, std::min(96, fb.npad)))) return fail_cleanup(rc);
             } else {
                 fb.tm_wr = fb.tm_wo;  // unused without a router
             }
