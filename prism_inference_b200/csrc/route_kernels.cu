@@ -8,8 +8,9 @@
 //   route_plan     one CTA: exclusive scan of the counts -> segment offsets, the list
 //                  of 128-row tiles (expert, first sorted row, rows) and the tile
 //                  count, then resets the counters for the next block;
-//   route_scatter  every token takes a slot in its expert's segment (warp-aggregated
-//                  atomics), giving perm[sorted row] = token.
+//   route_scatter  every token takes a slot in its expert's segment, giving
+//                  perm[sorted row] = token: ranks inside a 2048-token chunk from
+//                  shared-memory atomics, one global atomic per (chunk, expert).
 // The order of tokens inside a segment is not fixed, but each output row of the
 // grouped GEMM depends only on its own input row, so results do not depend on it.
 #include "common.cuh"
@@ -58,29 +59,42 @@ __global__ void __launch_bounds__(256) route_plan_kernel(RoutePlanArgs a) {
     }
 }
 
+// Tokens per scatter CTA: ranks inside an expert's share of the chunk come from shared
+// atomics; one global atomic per (CTA, expert) reserves the share's rows.
+constexpr int kScatterChunk = 2048;
+
 __global__ void __launch_bounds__(256) route_scatter_kernel(RouteScatterArgs a) {
-    const int t = blockIdx.x * blockDim.x + threadIdx.x;
-    const bool active = t < a.n_tokens;
-    int e = active ? a.assign[t] : -1;
-    if (active && (e < 0 || e >= a.n_experts)) {
-        atomicOr(a.err, ERR_ROUTE);
-        e = -1;
+    __shared__ int s_cnt[256], s_base[256];
+    constexpr int kPer = kScatterChunk / 256;
+    const int t0 = blockIdx.x * kScatterChunk;
+    s_cnt[threadIdx.x] = 0;
+    __syncthreads();
+    int ex[kPer], rk[kPer];
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+        const int t = t0 + i * 256 + threadIdx.x;
+        int e = t < a.n_tokens ? a.assign[t] : -1;
+        if (t < a.n_tokens && (e < 0 || e >= a.n_experts)) {
+            atomicOr(a.err, ERR_ROUTE);
+            e = -1;
+        }
+        ex[i] = e;
+        rk[i] = e >= 0 ? atomicAdd(&s_cnt[e], 1) : 0;
     }
-    const unsigned lanes = __activemask();
-    const unsigned peers = __match_any_sync(lanes, e);
-    const int leader = __ffs(peers) - 1;
-    const int rank = __popc(peers & ((1u << (threadIdx.x & 31)) - 1));
-    int base = 0;
-    if (e >= 0 && (int)(threadIdx.x & 31) == leader) base = atomicAdd(&a.cursor[e], __popc(peers));
-    base = __shfl_sync(lanes, base, leader);
-    if (e >= 0) a.perm[a.offsets[e] + base + rank] = t;
+    __syncthreads();
+    const int e = threadIdx.x;
+    if (e < a.n_experts && s_cnt[e]) s_base[e] = a.offsets[e] + atomicAdd(&a.cursor[e], s_cnt[e]);
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < kPer; ++i)
+        if (ex[i] >= 0) a.perm[s_base[ex[i]] + rk[i]] = t0 + i * 256 + threadIdx.x;
 }
 
 cudaError_t launch_route(const RoutePlanArgs& p, const RouteScatterArgs& s, cudaStream_t st) {
     route_plan_kernel<<<1, 256, 0, st>>>(p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    if (s.n_tokens > 0) route_scatter_kernel<<<(s.n_tokens + 255) / 256, 256, 0, st>>>(s);
+    if (s.n_tokens > 0) route_scatter_kernel<<<(s.n_tokens + kScatterChunk - 1) / kScatterChunk, 256, 0, st>>>(s);
     return cudaGetLastError();
 }
 
