@@ -173,16 +173,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tok[i] = r < t.rows ? a.perm[t.start + r] : -1;
                 }
                 if (!mbar_wait(&bars->a_empty, (it & 1) ^ 1, abort)) break;
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const int r = lane + 32 * i;
-                    const __half* src = a.x + (size_t)(tok[i] < 0 ? 0 : tok[i]) * KIN;
-#pragma unroll
-                    for (int kb = 0; kb < KIN / 64; ++kb)
-#pragma unroll
-                        for (int c = 0; c < 8; ++c)
-                            cp_async16(a_base + kb * 16384 + sw128_off(r, c), src + kb * 64 + c * 8,
-                                       tok[i] < 0 ? 0u : 16u);
+                // one row per instruction: lane l copies 16 B of K-block l / 8, chunk l % 8,
+                // so every warp access reads one contiguous KIN * 2-byte row
+                static_assert(MODE != FFN_EXPERT || KIN == 256, "the row gather covers 256 columns with 32 lanes");
+                const int kb = lane >> 3, c = lane & 7;
+#pragma unroll 4
+                for (int r = 0; r < 128; ++r) {
+                    const int tk = __shfl_sync(0xffffffffu, tok[r >> 5], r & 31);
+                    const __half* src = a.x + (size_t)(tk < 0 ? 0 : tk) * KIN + kb * 64 + c * 8;
+                    cp_async16(a_base + kb * 16384 + sw128_off(r, c), src, tk < 0 ? 0u : 16u);
                 }
                 cp_async_mbar_arrive(&bars->a_full);
             }
@@ -273,6 +272,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             const bool row_valid = row < rows;
             const int out_row = MODE == FFN_EXPERT ? (row_valid ? a.perm[start + row] : 0) : start + row;
+            // This warp's bias columns, lane l holding columns 4l .. 4l+3 of its half (HID / 2 and
+            // NOUT / 2 are 128 here); loaded as the tile starts so the L2 latency hides behind the
+            // GEMM, and handed to the column groups by shuffles.
+            static_assert(HID / 2 <= 128 && NOUT / 2 <= 128, "one float4 of bias per lane");
             // fp16 running sum of the dense FFN chunk outputs (attention_windowed_d256.comp.glsl:167-168)
             uint32_t accum[MODE == FFN_DENSE ? NOUT / 4 : 1];
             if (MODE == FFN_DENSE) {
@@ -281,24 +284,23 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             for (int c = 0; c < n_chunks && ok; ++c, ++chunk_it) {
                 // ---- epi1: acc1 -> bias -> fp16 -> activation -> fp16
-                if (!mbar_wait(&bars->acc1_full, chunk_it & 1, abort)) { ok = false; break; }
-                tc_fence_after();
                 const float* b1 = a.b1 + (size_t)e * HID * n_chunks + c * HID;
                 constexpr int kCols1 = HID / 2;
+                const float4 bias1 = 4 * lane < kCols1 ? ldg_f4(b1 + half * kCols1 + 4 * lane) : make_float4(0, 0, 0, 0);
+                if (!mbar_wait(&bars->acc1_full, chunk_it & 1, abort)) { ok = false; break; }
+                tc_fence_after();
 #pragma unroll 1
                 for (int g = 0; g < kCols1 / 32; ++g) {
                     const int col0 = half * kCols1 + g * 32;
-                    float4 bb[8];
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) bb[i] = ldg_f4(b1 + col0 + 4 * i);
                     uint32_t r[32];
                     tmem_ld32(tmem + lane_addr + col0, r);
                     tmem_ld_wait();
                     uint32_t packed[16];
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
-                        const float bx = (j & 1) ? bb[j >> 1].z : bb[j >> 1].x;
-                        const float by = (j & 1) ? bb[j >> 1].w : bb[j >> 1].y;
+                        // columns col0 + 2j, +1 live in lane g * 8 + j / 2
+                        const float bx = __shfl_sync(0xffffffffu, (j & 1) ? bias1.z : bias1.x, g * 8 + (j >> 1));
+                        const float by = __shfl_sync(0xffffffffu, (j & 1) ? bias1.w : bias1.y, g * 8 + (j >> 1));
                         // t = h(acc + b1): one rounding per coopVecMatMulAddNV result
                         const uint32_t t = pack_h2(__fadd_rn(__uint_as_float(r[2 * j]), bx),
                                                    __fadd_rn(__uint_as_float(r[2 * j + 1]), by));
@@ -358,9 +360,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                                       : make_uint4(0, 0, 0, 0);
                     }
                 }
+                const float* b2 = a.b2 + (size_t)e * NOUT;
+                const float4 bias2 = 4 * lane < kCols2 ? ldg_f4(b2 + half * kCols2 + 4 * lane) : make_float4(0, 0, 0, 0);
                 if (!mbar_wait(&bars->acc2_full, chunk_it & 1, abort)) { ok = false; break; }
                 tc_fence_after();
-                const float* b2 = a.b2 + (size_t)e * NOUT;
                 // H-tile address of (tile row R, column col) in the K-major SW128 layout
                 auto hslot = [&](int R, int col) -> unsigned char* {
                     return sH + (col >> 6) * 16384 + sw128_off(R, (col & 63) >> 3);
@@ -374,17 +377,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int g = 0; g < kCols2 / 32; ++g) {
                     const int col0 = half * kCols2 + g * 32;
-                    float4 bb[8];
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) bb[i] = ldg_f4(b2 + col0 + 4 * i);
                     uint32_t r[32];
                     tmem_ld32(tmem + Cfg::kAcc2 + lane_addr + col0, r);
                     tmem_ld_wait();
                     uint32_t part[16];  // h(acc + b2)
+                    float bxs[MODE == FFN_DENSE ? 16 : 1], bys[MODE == FFN_DENSE ? 16 : 1];  // for the dense rule
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
-                        const float bx = (j & 1) ? bb[j >> 1].z : bb[j >> 1].x;
-                        const float by = (j & 1) ? bb[j >> 1].w : bb[j >> 1].y;
+                        const float bx = __shfl_sync(0xffffffffu, (j & 1) ? bias2.z : bias2.x, g * 8 + (j >> 1));
+                        const float by = __shfl_sync(0xffffffffu, (j & 1) ? bias2.w : bias2.y, g * 8 + (j >> 1));
+                        if constexpr (MODE == FFN_DENSE) {
+                            bxs[j] = bx;
+                            bys[j] = by;
+                        }
                         part[j] = pack_h2(__fadd_rn(__uint_as_float(r[2 * j]), bx),
                                           __fadd_rn(__uint_as_float(r[2 * j + 1]), by));
                     }
@@ -406,8 +411,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             if (MODE == FFN_DENSE && n_chunks > 1) {
                                 // out = h(acc - (n_chunks-1)*b2 + y)   (attention_windowed_d256.comp.glsl:171-177)
                                 const float corr = (float)(n_chunks - 1);
-                                const float bx = (k & 1) ? bb[k >> 1].z : bb[k >> 1].x;
-                                const float by = (k & 1) ? bb[k >> 1].w : bb[k >> 1].y;
+                                const float bx = bxs[MODE == FFN_DENSE ? k : 0], by = bys[MODE == FFN_DENSE ? k : 0];
                                 const uint32_t acc = accum[g * 16 + k];
                                 z[j] = pack_h2(__fadd_rn(__fsub_rn(lo_h2f(acc), __fmul_rn(corr, bx)), lo_h2f(xs[j])),
                                                __fadd_rn(__fsub_rn(hi_h2f(acc), __fmul_rn(corr, by)), hi_h2f(xs[j])));
