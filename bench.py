@@ -148,14 +148,14 @@ def load_peaks():
     return 1400.0, 6650.0, "fallback"
 
 
-def load_traffic(kind):
-    """DRAM bytes per launch of a kernel kind from the committed ncu summary, if any."""
+def load_traffic(kind, frames):
+    """DRAM bytes (read + write) per launch of a kernel kind: the committed ncu capture's
+    bytes per frame times the frames one launch processes, or None without a capture."""
     p = ROOT / "profiles" / "traffic.json"
     if p.exists():
-        d = json.loads(p.read_text())
-        e = d.get(kind)
+        e = json.loads(p.read_text()).get(kind)
         if e:
-            return e
+            return e["dram_bytes_per_frame"] * frames
     return None
 
 
@@ -194,24 +194,28 @@ def reference_cpu_forward(L, blob, x, n_blocks=None):
     return time.perf_counter() - t0
 
 
-def cpu_baseline(cfg, blob):
-    """1 frame of the full stack through the reference shader sources on all host cores."""
+def cpu_baseline(cfg, blob, min_seconds=10.0):
+    """Whole frames of the full stack through the reference shader sources on all host
+    cores, one frame at a time until at least min_seconds of CPU work were timed."""
     from oracle import REF_LIB
     L = cfg.layout
-    x = synth.make_frames(L, 1)
     threads = os.cpu_count()
-    if REF_LIB.exists():
-        dt = reference_cpu_forward(L, blob, x)
-        kind = "reference"
-    else:
-        from oracle import Oracle
-        o = Oracle()
-        t0 = time.perf_counter()
-        o.stack(L, blob, x)
-        dt = time.perf_counter() - t0
-        kind = "port"
-    return {"value": L.tokens / dt, "unit": "tokens/s", "cores": threads, "kind": kind,
-            "sample": f"1 frame x {len(L.blocks)} blocks of {cfg.key} ({dt:.1f} s)"}
+    total, frames = 0.0, 0
+    while total < min_seconds and frames < 16:
+        x = synth.make_frames(L, 1, first=frames)
+        if REF_LIB.exists():
+            total += reference_cpu_forward(L, blob, x)
+            kind = "reference"
+        else:
+            from oracle import Oracle
+            o = Oracle()
+            t0 = time.perf_counter()
+            o.stack(L, blob, x)
+            total += time.perf_counter() - t0
+            kind = "port"
+        frames += 1
+    return {"value": frames * L.tokens / total, "unit": "tokens/s", "cores": threads, "kind": kind,
+            "sample": f"{frames} frames x {len(L.blocks)} blocks of {cfg.key} ({total:.1f} s)"}
 
 
 def run_reference(args):
@@ -359,7 +363,8 @@ def run_ours(args):
         achieved = fl / (per_launch_ms / 1e3) / 1e12
         roof = {"kernel": kind, "bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
                 "frac": achieved / peak_tf, "peak_source": f"{peak_src} bf16_tflops_sustained",
-                "traffic": load_traffic(kind), "ms_per_launch": per_launch_ms,
+                "traffic": load_traffic(kind, B), "traffic_source": "profiles/traffic.json (ncu, scaled by frames)",
+                "ms_per_launch": per_launch_ms,
                 "share": tot_ms / (ms * args.steps)}
     kernel_ms = {k: round(v[0] / args.steps, 4) for k, v in prof.items()}
 

@@ -37,24 +37,33 @@ __global__ void __launch_bounds__(256) route_plan_kernel(RoutePlanArgs a) {
         __syncthreads();
     }
     const int off = s_off[e] - c;                 // exclusive
-    const int nt = (c + 127) / 128;
-    const int toff = s_toff[e] - nt;
     if (e < n) {
         a.offsets[e] = off;
         a.cursor[e] = 0;
         if (a.counts_out) a.counts_out[e] = c;
         a.counts[e] = 0;  // ready for the next block's router
-        for (int j = 0; j < nt; ++j) {
-            ExpertTile t;
-            t.expert = e;
-            t.start = off + j * 128;
-            t.rows = min(128, c - j * 128);
-            t.pad = 0;
-            a.tiles[toff + j] = t;
+    }
+    // tile i belongs to the first expert whose inclusive tile count exceeds i; every
+    // thread writes tiles i = tid, tid + 256, ... (coalesced records)
+    const int n_tiles = s_toff[255];
+    for (int i = e; i < n_tiles; i += 256) {
+        int lo = 0, hi = 255;
+        while (lo < hi) {
+            const int mid = (lo + hi) >> 1;
+            if (s_toff[mid] > i) hi = mid;
+            else lo = mid + 1;
         }
+        const int cnt = s_off[lo] - (lo > 0 ? s_off[lo - 1] : 0);
+        const int j = i - (s_toff[lo] - (cnt + 127) / 128);  // tile index inside expert lo
+        ExpertTile t;
+        t.expert = lo;
+        t.start = s_off[lo] - cnt + j * 128;
+        t.rows = min(128, cnt - j * 128);
+        t.pad = 0;
+        a.tiles[i] = t;
     }
     if (e == 255) {
-        *a.n_tiles = s_toff[255];
+        *a.n_tiles = n_tiles;
         if (s_off[255] != a.n_tokens) atomicOr(a.err, ERR_ROUTE);  // every token routed exactly once
     }
 }
