@@ -197,9 +197,9 @@ def reference_cpu_forward(L, blob, x, n_blocks=None):
 def cpu_baseline(cfg, blob, min_seconds=10.0):
     """Whole frames of the full stack through the reference shader sources on all host
     cores, one frame at a time until at least min_seconds of CPU work were timed."""
-    from oracle import REF_LIB
+    from oracle import REF_LIB, use_host_threads
     L = cfg.layout
-    threads = os.cpu_count()
+    threads = use_host_threads()
     total, frames = 0.0, 0
     while total < min_seconds and frames < 16:
         x = synth.make_frames(L, 1, first=frames)
@@ -224,11 +224,12 @@ def run_reference(args):
         return
     cfg = configs.get(args.config)
     L = cfg.layout
-    from oracle import REF_LIB
+    from oracle import REF_LIB, use_host_threads
     if not REF_LIB.exists():
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref (the reference shader sources "
                           "compiled for the host) is not built"}))
         return
+    threads = use_host_threads()  # all host cores, also under torchrun (OMP_NUM_THREADS=1)
     blob = synth.make_blob(L, router_skew=cfg.router_skew, skew_bias=cfg.skew_bias)
     x = synth.make_frames(L, 1)
     nb = min(4, len(L.blocks))  # bounded sample per step: 1 frame x nb blocks (+ adapters)
@@ -244,7 +245,7 @@ def run_reference(args):
             "config": {"workload": f"{cfg.key}: {cfg.description}, 1 frame per step (sampled)",
                        "frames_per_step": 1},
             "impl": "reference",
-            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "reference",
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "reference",
                              "sample": f"1 frame x {nb} of {len(L.blocks)} blocks per step, scaled by blocks"},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line))

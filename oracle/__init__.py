@@ -108,6 +108,16 @@ class Oracle:
         return self.lib.oracle_gelu_h(x)
 
 
+def use_host_threads(n: int | None = None) -> int:
+    """Let the OpenMP runtime of the host libraries (the system libgomp, which reads
+    OMP_NUM_THREADS once at start-up - torchrun sets it to 1) use n threads (default: all
+    host cores) in parallel regions started from this thread.  Returns n."""
+    import os
+    n = n or os.cpu_count() or 1
+    C.CDLL("libgomp.so.1").omp_set_num_threads(C.c_int(n))
+    return n
+
+
 class GlslRef:
     """The reference's shader sources, executed on the host (see glsl_ref/)."""
 
