@@ -12,8 +12,9 @@
 // Warp roles (352 threads):
 //   warp 0     producer: A tile by TMA (contiguous rows) and the W1/W2 K-chunks (TMA,
 //              128B swizzle) through a STAGES-deep ring
-//   warp 10    expert mode: gathers the tile's token rows with cp.async (all row
-//              indices loaded first), independently of the weight ring
+//   warp 10    expert mode: gathers the tile's token rows with TMA tile::gather4 (four
+//              rows per copy, one copy per lane and K-block), independently of the
+//              weight ring
 //   warp 1     TMEM allocation + single-thread tcgen05.mma issue
 //   warps 2-9  epilogue: warp w reads TMEM lanes 32*(w%4).. (its rows) and one half
 //              of the columns
@@ -84,7 +85,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&bars->full[s], 1);
             mbar_init(&bars->empty[s], 1);
         }
-        mbar_init(&bars->a_full, MODE == FFN_EXPERT ? 32 : 1);
+        mbar_init(&bars->a_full, 1);
         mbar_init(&bars->a_empty, 1);  // the MMA warp's commit after the last GEMM1 reading A
         mbar_init(&bars->acc1_full, 1);
         mbar_init(&bars->acc1_empty, kEpiWarps);
@@ -107,7 +108,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             prefetch_tmap(&tm_w1);
             if (Cfg::kTwoGemm) prefetch_tmap(&tm_w2);
-            if (MODE != FFN_EXPERT) prefetch_tmap(&tm_x);
+            prefetch_tmap(&tm_x);
         }
         int stage = 0;
         uint32_t phase = 0;
@@ -166,26 +167,23 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t a_base = smem_u32(sA);
             for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
                 const ExpertTile t = a.tiles[tile];
+                // lane l gathers tile rows 4l .. 4l+3 with TMA (tile::gather4): token rows of
+                // the attention output; rows past the tile take row n_rows, outside the map,
+                // which the copy zero-fills
                 int tok[4];
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {  // every row index first: one round trip
-                    const int r = lane + 32 * i;
-                    tok[i] = r < t.rows ? a.perm[t.start + r] : -1;
+                for (int i = 0; i < 4; ++i) {
+                    const int r = 4 * lane + i;
+                    tok[i] = r < t.rows ? a.perm[t.start + r] : a.n_rows;
                 }
                 if (!mbar_wait(&bars->a_empty, (it & 1) ^ 1, abort)) break;
-                // one row per instruction: lane l copies 16 B of K-block l / 8, chunk l % 8,
-                // so every warp access reads one contiguous KIN * 2-byte row
-                static_assert(MODE != FFN_EXPERT || KIN == 256, "the row gather covers 256 columns with 32 lanes");
-                const int kb = lane >> 3, c = lane & 7;
-#pragma unroll 4
-                for (int r = 0; r < 128; ++r) {
-                    const int tk = __shfl_sync(0xffffffffu, tok[r >> 5], r & 31);
-                    const __half* src = a.x + (size_t)(tk < 0 ? 0 : tk) * KIN + kb * 64 + c * 8;
-                    cp_async16(a_base + kb * 16384 + sw128_off(r, c), src, tk < 0 ? 0u : 16u);
-                }
-                cp_async_mbar_arrive(&bars->a_full);
+                if (lane == 0) mbar_expect_tx(&bars->a_full, Cfg::kA);
+                __syncwarp();
+#pragma unroll
+                for (int kb = 0; kb < KIN / 64; ++kb)
+                    tma_gather4(a_base + kb * 16384 + lane * 512, &tm_x, &bars->a_full, kb * 64, tok[0], tok[1],
+                                tok[2], tok[3]);
             }
-            asm volatile("cp.async.wait_all;" ::: "memory");
         }
     } else if (warp == 1) {
         // ===================== MMA issuer =====================
@@ -470,9 +468,9 @@ cudaError_t launch_ffn(const FfnArgs& a, const CUtensorMap& tx, const CUtensorMa
 
 }  // namespace
 
-cudaError_t launch_ffn_expert256(const FfnArgs& a, const CUtensorMap& w1, const CUtensorMap& w2, int grid,
-                                 cudaStream_t s) {
-    return launch_ffn<FFN_EXPERT, 256, 256, 256>(a, w1, w1, w2, 1, grid, s);
+cudaError_t launch_ffn_expert256(const FfnArgs& a, const CUtensorMap& x_rows, const CUtensorMap& w1,
+                                 const CUtensorMap& w2, int grid, cudaStream_t s) {
+    return launch_ffn<FFN_EXPERT, 256, 256, 256>(a, x_rows, w1, w2, 1, grid, s);
 }
 cudaError_t launch_ffn_dense256(const FfnArgs& a, const CUtensorMap& x, const CUtensorMap& w1, const CUtensorMap& w2,
                                 int n_chunks, int grid, cudaStream_t s) {

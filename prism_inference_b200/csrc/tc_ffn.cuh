@@ -26,14 +26,16 @@ struct FfnArgs {
     const int32_t* perm;       // FFN_EXPERT: sorted row -> token
     const ExpertTile* tiles;   // FFN_EXPERT: tile list
     const int32_t* n_tiles;    // FFN_EXPERT: device tile count
-    int n_rows;                // other modes: number of rows
+    int n_rows;                // rows of x (expert mode: of the gather map), other modes: rows to process
     const float* b1;           // fp32 biases [experts][HID*NCH]
     const float* b2;           // fp32 biases [experts][NOUT]
     uint32_t* err;             // device error word
 };
 
-cudaError_t launch_ffn_expert256(const FfnArgs& a, const CUtensorMap& w1, const CUtensorMap& w2, int grid,
-                                 cudaStream_t s);
+// x_rows: 2-D [n_rows][256] map of a.x with box {64, 1} (one row) for the tile::gather4 row gather;
+// a.n_rows = its row count.
+cudaError_t launch_ffn_expert256(const FfnArgs& a, const CUtensorMap& x_rows, const CUtensorMap& w1,
+                                 const CUtensorMap& w2, int grid, cudaStream_t s);
 cudaError_t launch_ffn_dense256(const FfnArgs& a, const CUtensorMap& x, const CUtensorMap& w1, const CUtensorMap& w2,
                                 int n_chunks, int grid, cudaStream_t s);
 cudaError_t launch_ffn_proj_up(const FfnArgs& a, const CUtensorMap& x, const CUtensorMap& w, int grid,
