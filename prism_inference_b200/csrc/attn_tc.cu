@@ -26,8 +26,8 @@
 // Warp roles (320 threads):
 //   warp 0      TMA producer: X tile (4-D window boxes), weight ring (QKV_h, Wo, Wr)
 //   warp 1      TMEM owner + tcgen05.mma issuer
-//   warps 2-5   softmax group: S_h -> P_h, O_h -> attention-output tile
-//   warps 6-9   drain group: QKV_h -> Q/K/V^T smem, y epilogue, store, router
+//   warps 2-5   softmax group: S_h -> P_h, O_h -> attention-output tile, y columns 128..255
+//   warps 6-9   drain group: QKV_h -> Q/K/V^T smem, y columns 0..127, store, router
 // Thread = tile row = TMEM lane in both groups (warp w reads lanes 32*(w%4)..).
 // The two groups run one head apart and the MMA warp issues QKV_{h+1} right after S_h.
 // Weights stream through a 2 x 48 KB ring in whole operands, one TMA load each: a
@@ -79,6 +79,36 @@ struct Counter {  // phase bookkeeping of one barrier as seen by one role
     PRISM_DEV uint32_t next_free() { return ((n++) & 1u) ^ 1u; }  // producer of a free slot
 };
 
+// y = fp16(fp16(PO + bo) + x) for column groups [g0, g1) (32 columns each) of tile row r,
+// written over X in its swizzled slot.  The drain group does groups 0-3, the softmax group
+// (idle at the end of a tile) groups 4-7.
+PRISM_DEV void y_groups(unsigned char* sX, uint32_t row_taddr, int r, const float* bo, int g0, int g1) {
+#pragma unroll 1
+    for (int g = g0; g < g1; ++g) {  // 32 columns = 4 swizzle chunks of K-block g/2
+        float4 bb[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) bb[i] = ldg_f4(bo + g * 32 + 4 * i);
+        uint32_t v[32];
+        tmem_ld32(row_taddr + kTPO + g * 32, v);
+        tmem_ld_wait();
+        unsigned char* xblk = sX + (g >> 1) * 16384;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const int off = sw128_off(r, (g & 1) * 4 + c);
+            const uint4 x = *reinterpret_cast<const uint4*>(xblk + off);
+            const float4 b0 = bb[2 * c], b1 = bb[2 * c + 1];
+            const float* fv = reinterpret_cast<const float*>(&v[8 * c]);
+            // y = h( h(PO + bo) + x ): the second rounding is the fp16 add of :76
+            uint4 y;
+            y.x = hadd2_u32(pack_h2(__fadd_rn(fv[0], b0.x), __fadd_rn(fv[1], b0.y)), x.x);
+            y.y = hadd2_u32(pack_h2(__fadd_rn(fv[2], b0.z), __fadd_rn(fv[3], b0.w)), x.y);
+            y.z = hadd2_u32(pack_h2(__fadd_rn(fv[4], b1.x), __fadd_rn(fv[5], b1.y)), x.z);
+            y.w = hadd2_u32(pack_h2(__fadd_rn(fv[6], b1.z), __fadd_rn(fv[7], b1.w)), x.w);
+            *reinterpret_cast<uint4*>(xblk + off) = y;
+        }
+    }
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     attn_tc_kernel(const AttnTcArgs a, const __grid_constant__ CUtensorMap tm_x,
                    const __grid_constant__ CUtensorMap tm_y, const __grid_constant__ CUtensorMap tm_wqkv,
@@ -118,8 +148,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_init(&bars->ao_ready, 4);
         mbar_init(&bars->ao_free, 1);
         mbar_init(&bars->po_full, 1);
-        mbar_init(&bars->po_drained, 4);
-        mbar_init(&bars->y_ready, 4);
+        mbar_init(&bars->po_drained, 8);  // both SIMT groups write y
+        mbar_init(&bars->y_ready, 8);
         mbar_init(&bars->lg_full, 1);
         mbar_init(&bars->lg_drained, 4);
         mbar_init(&bars->drain, 1);
@@ -306,7 +336,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int wnd = r >> 6;  // which window of the tile
         const float c2 = a.scale * 1.4426950408889634f;  // scale * log2(e)
         const int nkeys = a.n_keys;
-        Counter c_s, c_o, c_aof;
+        Counter c_s, c_o, c_aof, c_po;
         bool ok = true;
         bool first_pair = true;
         auto wait = [&](uint64_t* bar, uint32_t par) {
@@ -412,6 +442,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                     first_pair = false;
                 }
             }
+            if (!ok) break;
+            // ---- y, column groups 4-7
+            wait(&bars->po_full, c_po.next());
+            if (!ok) break;
+            y_groups(sX, tmem + lane_addr, r, a.bo, 4, 8);
+            tc_fence_before();
+            arrive(&bars->po_drained);
+            fence_async_shared();
+            arrive(&bars->y_ready);
         }
     } else {
         // ============================ drain group =============================
@@ -487,34 +526,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int h = 0; h < 8 && ok; ++h) drain_qkv(h);
             if (!ok) break;
 
-            // ---- y = fp16(fp16(PO + bo) + x), written over X (same swizzled slot)
+            // ---- y, column groups 0-3 (the softmax group writes 4-7)
             wait(&bars->po_full, c_po.next());
             if (!ok) break;
-#pragma unroll 1
-            for (int g = 0; g < 8; ++g) {  // 32 columns = 4 swizzle chunks of K-block g/2
-                float4 bb[8];
-#pragma unroll
-                for (int i = 0; i < 8; ++i) bb[i] = ldg_f4(a.bo + g * 32 + 4 * i);
-                uint32_t v[32];
-                tmem_ld32(tmem + lane_addr + kTPO + g * 32, v);
-                tmem_ld_wait();
-                unsigned char* xblk = sX + (g >> 1) * 16384;
-                unsigned char* yblk = xblk;
-#pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    const int off = sw128_off(r, (g & 1) * 4 + c);
-                    const uint4 x = *reinterpret_cast<const uint4*>(xblk + off);
-                    const float4 b0 = bb[2 * c], b1 = bb[2 * c + 1];
-                    const float* fv = reinterpret_cast<const float*>(&v[8 * c]);
-                    // y = h( h(PO + bo) + x ): the second rounding is the fp16 add of :76
-                    uint4 y;
-                    y.x = hadd2_u32(pack_h2(__fadd_rn(fv[0], b0.x), __fadd_rn(fv[1], b0.y)), x.x);
-                    y.y = hadd2_u32(pack_h2(__fadd_rn(fv[2], b0.z), __fadd_rn(fv[3], b0.w)), x.y);
-                    y.z = hadd2_u32(pack_h2(__fadd_rn(fv[4], b1.x), __fadd_rn(fv[5], b1.y)), x.z);
-                    y.w = hadd2_u32(pack_h2(__fadd_rn(fv[6], b1.z), __fadd_rn(fv[7], b1.w)), x.w);
-                    *reinterpret_cast<uint4*>(yblk + off) = y;
-                }
-            }
+            y_groups(sX, tmem + lane_addr, r, a.bo, 0, 4);
             tc_fence_before();
             arrive(&bars->po_drained);
             fence_async_shared();
@@ -535,6 +550,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             // ---- router: logits = fp16(y . Wr^T + br), first maximum
             wait(&bars->lg_full, c_lg.next());
             if (!ok) break;
+            if (storer) {
+                // the router GEMM is done with y and the store has read it: X may be refilled
+                tma_store_wait_read0();
+                mbar_arrive(&bars->x_free);
+            }
             if (router) {
                 int best = 0;
                 float bv = 0.0f;
@@ -562,10 +582,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             tc_fence_before();
             arrive(&bars->lg_drained);
-            if (storer) {
-                tma_store_wait_read0();  // y has left smem and the router MMA is done with it
-                mbar_arrive(&bars->x_free);
-            }
             first_tile = false;
         }
         if (storer) tma_store_wait0();
