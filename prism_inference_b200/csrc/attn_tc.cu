@@ -11,7 +11,8 @@
 // the 4-D TMA load zero-fills them and they take part as keys, :31-37, :60).
 // Per tile and head h (8 heads x 32):
 //   QKV_h   TMEM[96]  = X[128x256] . Wqkv_h^T        (tcgen05, K = 256)
-//   drain   Q_h, K_h (fp16, K-major SW64) and V_h^T (fp16, K-major SW128) to smem
+//   drain   Q_h, K_h (fp16, K-major SW64) and V_h (fp16, key-major SW64: the MN-major B
+//           operand of PV, so it is stored like K, no transpose) to smem
 //   S_h     TMEM[128] = Q_h . K_h^T                   (both windows; rows use their own)
 //   softmax fp32 per row over its window's 64 keys (scale, max, exp, sum as :60-66),
 //           P = fp16(exp(s - max)) written over S in TMEM (tcgen05.st), the other
@@ -27,7 +28,7 @@
 //   warp 0      TMA producer: X tile (4-D window boxes), weight ring (QKV_h, Wo, Wr)
 //   warp 1      TMEM owner + tcgen05.mma issuer
 //   warps 2-5   softmax group: S_h -> P_h, O_h -> attention-output tile, y columns 128..255
-//   warps 6-9   drain group: QKV_h -> Q/K/V^T smem, y columns 0..127, store, router
+//   warps 6-9   drain group: QKV_h -> Q/K/V smem, y columns 0..127, store, router
 // Thread = tile row = TMEM lane in both groups (warp w reads lanes 32*(w%4)..).
 // The two groups run one head apart and the MMA warp issues QKV_{h+1} right after S_h.
 // Weights stream through a 2 x 48 KB ring in whole operands, one TMA load each: a
@@ -51,8 +52,8 @@ constexpr int kRouterRows = 96;  // router rows per ring stage
 constexpr int kOffX = 0;                // 4 K-blocks x [128][128 B] = 64 KB; y overwrites it
 constexpr int kOffQ = kOffX + 65536;    // Q_h [128][64 B] SW64 8 KB
 constexpr int kOffK = kOffQ + 8192;     // K_h [128][64 B] SW64 8 KB
-constexpr int kOffVt = kOffK + 8192;    // V_h^T, 2 buffers (head parity) x 2 x [32][128 B] SW128 = 16 KB
-constexpr int kOffAO = kOffVt + 16384;  // [128][128 B] SW128 16 KB
+constexpr int kOffV = kOffK + 8192;     // V_h, 2 buffers (head parity) x [128 keys][64 B] SW64 = 16 KB
+constexpr int kOffAO = kOffV + 16384;   // [128][128 B] SW128 16 KB
 constexpr int kOffW = kOffAO + 16384;   // ring 2 x 48 KB
 constexpr int kOffBar = kOffW + kStages * kStage;
 
@@ -118,7 +119,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     unsigned char* sX = smem + kOffX;
     unsigned char* sQ = smem + kOffQ;
     unsigned char* sK = smem + kOffK;
-    unsigned char* sVt = smem + kOffVt;  // buffer b at +8192*b
+    unsigned char* sV = smem + kOffV;  // buffer b at +8192*b
     unsigned char* sAO = smem + kOffAO;
     unsigned char* sW = smem + kOffW;
     Bars* bars = reinterpret_cast<Bars*>(smem + kOffBar);
@@ -218,10 +219,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp == 1) {
         // ============================ MMA issuer ==============================
-        // Order per tile: QKV_0; for h: [Q,K,V^T of h drained] S_h, QKV_{h+1},
+        // Order per tile: QKV_0; for h: [Q,K,V of h drained] S_h, QKV_{h+1},
         // [P_h ready, O columns free] PV_h, every second head [pair ready] PO += ...
         {
-            const uint32_t id_qkv = idesc_f16(128, 96), id_s = idesc_f16(128, 128), id_pv = idesc_f16(128, 32),
+            const uint32_t id_qkv = idesc_f16(128, 96), id_s = idesc_f16(128, 128), id_pv = idesc_f16(128, 32) | (1u << 16) /* B = V MN-major */,
                            id_po = idesc_f16(128, 128);
             const int r_rows = npad < kRouterRows ? npad : kRouterRows;
             int stage = 0;
@@ -268,7 +269,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!first_tile) wait(&bars->lg_drained, c_lgd.next());
                 issue_qkv();
                 for (int h = 0; h < 8 && ok; ++h) {
-                    const uint32_t vt = smem_u32(sVt + (h & 1) * 8192);
+                    const uint32_t vs = smem_u32(sV + (h & 1) * 8192);
                     wait(&bars->qkv_drained, c_qkvd.next());
                     // ---- S_h = Q K^T
                     for (int k = 0; k < 2; ++k)
@@ -281,8 +282,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (h > 0 || !first_tile) wait(&bars->o_drained, c_od.next());
                     // ---- O_h = P V, P (fp16) read from TMEM: 16 keys = 8 columns per MMA
                     for (int k = 0; k < 8; ++k)
-                        mma_f16_ts_w(tmem + kTO, tmem + kTS + k * 8, sdesc(vt + (k >> 2) * 4096 + (k & 3) * 32, SW128),
-                                   id_pv, k != 0);
+                        mma_f16_ts_w(tmem + kTO, tmem + kTS + k * 8, sdesc(vs + k * 1024, SW64), id_pv, k != 0);
                     mma_commit_w(&bars->o_full);
                     if (h & 1) {
                         // ---- PO += O_pair . Wo[:, pair]^T
@@ -472,7 +472,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(bar);
         };
-        // QKV_h (TMEM) -> fp16 Q, K (K-major SW64) and V^T (K-major SW128), buffer h&1
+        // QKV_h (TMEM) -> fp16 Q, K (K-major SW64) and V (key-major SW64, buffer h&1)
         auto drain_qkv = [&](int h) {
             wait(&bars->qkv_full, c_qkv.next());
             if (!ok) return;
@@ -493,22 +493,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                     pk[2 * i + 1] = pack_h2(__fadd_rn(__uint_as_float(v[4 * i + 2]), bb[i].z),
                                             __fadd_rn(__uint_as_float(v[4 * i + 3]), bb[i].w));
                 }
-                if (part < 2) {
-                    unsigned char* dst = part == 0 ? sQ : sK;
+                // Q, K and V rows alike: row r, 32 fp16 = four 16-byte chunks, SW64 (V is the
+                // MN-major B operand of PV, which has exactly this layout)
+                unsigned char* dst = part == 0 ? sQ : part == 1 ? sK : sV + (h & 1) * 8192;
 #pragma unroll
-                    for (int c = 0; c < 4; ++c)
-                        *reinterpret_cast<uint4*>(dst + sw64_off(r, c)) =
-                            make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-                } else {
-                    // V^T: element (d, r) of a [32 x 128] K-major tile
-                    unsigned char* vt = sVt + (h & 1) * 8192 + (r >> 6) * 4096 + (r & 7) * 2;
-                    const int vchunk = (r & 63) >> 3;
-#pragma unroll
-                    for (int d = 0; d < 32; d += 2) {
-                        *reinterpret_cast<unsigned short*>(vt + sw128_off(d, vchunk)) = (unsigned short)(pk[d >> 1] & 0xffff);
-                        *reinterpret_cast<unsigned short*>(vt + sw128_off(d + 1, vchunk)) = (unsigned short)(pk[d >> 1] >> 16);
-                    }
-                }
+                for (int c = 0; c < 4; ++c)
+                    *reinterpret_cast<uint4*>(dst + sw64_off(r, c)) =
+                        make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
             }
             fence_async_shared();
             tc_fence_before();
