@@ -349,6 +349,41 @@ def run_ours(args):
     ms_b1 = max_over_ranks(e0.elapsed_time(e1) / n1)
     st.status()
 
+    # ---- the same frame, the whole stack replayed as one CUDA graph (prism_stack_forward
+    # is stream-ordered without host synchronisation, so it can be captured)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        st.forward(x1, o1)
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(n1):
+        g.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms_b1_graph = max_over_ranks(e0.elapsed_time(e1) / n1)
+    del g
+    st.status()
+
+    # ---- N > 1: the sharded output collected on rank 0 (NCCL over NVLink), timed apart
+    # from the compute (the frames are independent: this is the only exchange)
+    gather = None
+    if ws > 1:
+        recv = [torch.empty_like(out) for _ in range(ws)] if rank == 0 else None
+        for _ in range(2):
+            dist.gather(out, recv, dst=0)
+        torch.cuda.synchronize()
+        barrier()
+        e0.record(stream)
+        dist.gather(out, recv, dst=0)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        gms = max_over_ranks(e0.elapsed_time(e1))
+        nbytes = out.numel() * out.element_size() * (ws - 1)
+        gather = {"ms": gms, "bytes_to_rank0": nbytes, "GB_per_s": nbytes / (gms / 1e3) / 1e9}
+        del recv
+
     tokens_per_step = B * T * ws
     value = tokens_per_step / (ms / 1e3)
     e2e = tokens_per_step / (ms_e2e / 1e3)
@@ -382,7 +417,8 @@ def run_ours(args):
                            "tokens_per_frame": T, "seq_len": T, "global_batch": B * ws,
                            "parallelism": f"frame-sharded x{ws}, weights replicated",
                            "l2": "inputs/activations larger than L2 (134 MB in, 267 MB per activation buffer)",
-                           "frames_per_s": B * ws / (ms / 1e3), "batch1_ms": ms_b1,
+                           "frames_per_s": B * ws / (ms / 1e3), "batch1_ms": ms_b1, "batch1_graph_ms": ms_b1_graph,
+                           "output_gather": gather,
                            "tflops_effective": flops_step / (ms / 1e3) / 1e12,
                            "kernel_ms_per_step": kernel_ms},
                 "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": int(xh.numel() * 2),
