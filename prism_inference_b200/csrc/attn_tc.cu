@@ -65,8 +65,8 @@ constexpr uint32_t kTO = 480;    // PV_h [32]
 
 struct Bars {
     uint64_t full[kStages], empty[kStages];
-    uint64_t x_full, x_free, qkv_full, qkv_drained, s_full, p_ready, o_full, o_drained;
-    uint64_t ao_ready, ao_free, po_full, po_drained, y_ready, lg_full, lg_drained, drain, ep_done;
+    uint64_t x_full[4], x_free[4], qkv_full, qkv_drained, s_full, p_ready, o_full, o_drained;
+    uint64_t ao_ready, ao_free, po_full, po_drained, y_ready[4], lg_full, lg_drained, drain, ep_done;
     uint32_t tmem_base;
     int abort;
     int hist[256];
@@ -138,8 +138,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&bars->full[s], 1);
             mbar_init(&bars->empty[s], 1);
         }
-        mbar_init(&bars->x_full, 1);
-        mbar_init(&bars->x_free, 1);  // y stored and routed: X may be refilled
+        for (int kb = 0; kb < 4; ++kb) {  // the X tile moves K-block by K-block at tile ends
+            mbar_init(&bars->x_full[kb], 1);
+            mbar_init(&bars->x_free[kb], 2);   // y K-block stored (storer) and read by the router GEMM (commit)
+            mbar_init(&bars->y_ready[kb], 4);  // y K-block written (the group that owns it)
+        }
         mbar_init(&bars->qkv_full, 1);
         mbar_init(&bars->qkv_drained, 4);
         mbar_init(&bars->s_full, 1);
@@ -150,7 +153,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_init(&bars->ao_free, 1);
         mbar_init(&bars->po_full, 1);
         mbar_init(&bars->po_drained, 8);  // both SIMT groups write y
-        mbar_init(&bars->y_ready, 8);
         mbar_init(&bars->lg_full, 1);
         mbar_init(&bars->lg_drained, 4);
         mbar_init(&bars->drain, 1);
@@ -175,7 +177,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (router) prefetch_tmap(&tm_wr);
             int stage = 0;
             uint32_t phase = 0;
-            Counter c_xfree;
+            Counter c_xfree[4];
             bool ok = true;
             // one ring stage = one TMA load (3-D maps: rows c1.. at every K-block)
             auto ring_load = [&](const CUtensorMap* map, bool kb3d, int c0, int c1, uint32_t bytes) -> bool {
@@ -193,18 +195,27 @@ __global__ void __launch_bounds__(kThreads, 1)
             };
             const int r_rows = npad < kRouterRows ? npad : kRouterRows;  // rows per router load
             for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
-                if (!mbar_wait(&bars->x_free, c_xfree.next_free(), abort)) break;
-                mbar_expect_tx(&bars->x_full, 65536);
+                int wf[2], wxx[2], wyy[2];
                 for (int half = 0; half < 2; ++half) {
                     const int w = 2 * tile + half;
                     // a missing second window loads an out-of-range frame: zero fill
-                    const int f = w < n_windows ? w / win_per_frame : a.frames;
+                    wf[half] = w < n_windows ? w / win_per_frame : a.frames;
                     const int wl = w < n_windows ? w % win_per_frame : 0;
-                    const int wy = wl / wx_n, wx = wl % wx_n;
-                    for (int kb = 0; kb < 4; ++kb)
-                        tma_load_4d(smem_u32(sX + kb * 16384 + half * 8192), &tm_x, &bars->x_full, kb * 64, wx * 8,
-                                    wy * 8, f);
+                    wyy[half] = wl / wx_n;
+                    wxx[half] = wl % wx_n;
                 }
+                // each K-block as soon as the previous tile has stored and routed it
+                for (int kb = 0; kb < 4 && ok; ++kb) {
+                    if (!mbar_wait(&bars->x_free[kb], c_xfree[kb].next_free(), abort)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(&bars->x_full[kb], 16384);
+                    for (int half = 0; half < 2; ++half)
+                        tma_load_4d(smem_u32(sX + kb * 16384 + half * 8192), &tm_x, &bars->x_full[kb], kb * 64,
+                                    wxx[half] * 8, wyy[half] * 8, wf[half]);
+                }
+                if (!ok) break;
                 // same order as the MMA warp consumes: QKV_0, then per head h
                 // QKV_{h+1} and, after every second head, the Wo columns of the pair
                 ok = ring_load(&tm_wqkv, true, 0, 0, 96 * 512);
@@ -223,11 +234,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         // [P_h ready, O columns free] PV_h, every second head [pair ready] PO += ...
         {
             const uint32_t id_qkv = idesc_f16(128, 96), id_s = idesc_f16(128, 128), id_pv = idesc_f16(128, 32) | (1u << 16) /* B = V MN-major */,
-                           id_po = idesc_f16(128, 128);
+                           id_po = idesc_f16(128, 256);
             const int r_rows = npad < kRouterRows ? npad : kRouterRows;
             int stage = 0;
             uint32_t phase = 0;
-            Counter c_xfull, c_qkvd, c_pr, c_od, c_aor, c_pod, c_yr, c_lgd;
+            Counter c_xfull[4], c_qkvd, c_pr, c_od, c_aor, c_pod, c_yr[4], c_lgd;
             bool ok = true;
             bool first_tile = true;
             auto ring_wait = [&]() -> uint32_t {
@@ -250,24 +261,25 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_fence_after();
             };
             const uint32_t xs = smem_u32(sX);
-            auto issue_qkv = [&]() {
+            auto issue_qkv = [&](bool first_of_tile) {  // the tile's first: X K-blocks as they land
                 const uint32_t b = ring_wait();  // Wqkv_h: K-block kc at +kc * 96 rows
                 if (ok) {
 #pragma unroll
-                    for (int kc = 0; kc < 4; ++kc)
+                    for (int kc = 0; kc < 4; ++kc) {
+                        if (first_of_tile) wait(&bars->x_full[kc], c_xfull[kc].next());
 #pragma unroll
                         for (int k = 0; k < 4; ++k)
                             mma_f16_ss_w(tmem + kTQKV, sdesc(xs + kc * 16384 + k * 32, SW128),
                                          sdesc(b + kc * 12288 + k * 32, SW128), id_qkv, (kc | k) != 0);
+                    }
                     ring_release();
                 }
                 mma_commit_w(&bars->qkv_full);
             };
             for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
-                wait(&bars->x_full, c_xfull.next());
                 // logits of the previous tile live in the QKV/S/O columns
                 if (!first_tile) wait(&bars->lg_drained, c_lgd.next());
-                issue_qkv();
+                issue_qkv(true);
                 for (int h = 0; h < 8 && ok; ++h) {
                     const uint32_t vs = smem_u32(sV + (h & 1) * 8192);
                     wait(&bars->qkv_drained, c_qkvd.next());
@@ -276,7 +288,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         mma_f16_ss_w(tmem + kTS, sdesc(smem_u32(sQ) + k * 32, SW64), sdesc(smem_u32(sK) + k * 32, SW64),
                                    id_s, k != 0);
                     mma_commit_w(&bars->s_full);
-                    if (h < 7) issue_qkv();
+                    if (h < 7) issue_qkv(false);
                     wait(&bars->p_ready, c_pr.next());
                     // O columns free once the softmax group drained the previous head
                     if (h > 0 || !first_tile) wait(&bars->o_drained, c_od.next());
@@ -288,22 +300,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                         // ---- PO += O_pair . Wo[:, pair]^T
                         wait(&bars->ao_ready, c_aor.next());
                         if (h == 1 && !first_tile) wait(&bars->po_drained, c_pod.next());
-                        const uint32_t b = ring_wait();  // Wo[:, pair]: output rows 128 nh.. at +16 KB nh
+                        const uint32_t b = ring_wait();  // Wo[:, pair]: all 256 output rows, N = 256
                         if (ok) {
 #pragma unroll
-                            for (int nh = 0; nh < 2; ++nh)
-#pragma unroll
-                                for (int k = 0; k < 4; ++k)
-                                    mma_f16_ss_w(tmem + kTPO + nh * 128, sdesc(smem_u32(sAO) + k * 32, SW128),
-                                                 sdesc(b + nh * 16384 + k * 32, SW128), id_po, (h > 1) || (k != 0));
+                            for (int k = 0; k < 4; ++k)
+                                mma_f16_ss_w(tmem + kTPO, sdesc(smem_u32(sAO) + k * 32, SW128), sdesc(b + k * 32, SW128),
+                                             id_po, (h > 1) || (k != 0));
                             ring_release();
                         }
                         mma_commit_w(&bars->ao_free);
                     }
                 }
                 mma_commit_w(&bars->po_full);
-                // ---- router logits = y . Wr^T
-                wait(&bars->y_ready, c_yr.next());
+                // ---- router logits = y . Wr^T, K-block by K-block as y lands; each X K-block
+                // is released (x_free, with the storer's arrival) after its last router MMA
                 if (router) {
                     const uint32_t ys = xs;  // y overwrote X
                     // up to 96 expert rows per stage (K-block kc at +kc * r_rows rows);
@@ -313,13 +323,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (!ok) break;
                         const int n = npad - r0 < r_rows ? npad - r0 : r_rows;
                         const uint32_t id_r = idesc_f16(128, n);
+                        const bool last_stage = r0 + kRouterRows >= npad;
 #pragma unroll
-                        for (int kc = 0; kc < 4; ++kc)
+                        for (int kc = 0; kc < 4; ++kc) {
+                            if (r0 == 0) wait(&bars->y_ready[kc], c_yr[kc].next());
 #pragma unroll
                             for (int k = 0; k < 4; ++k)
                                 mma_f16_ss_w(tmem + kTQKV + r0, sdesc(ys + kc * 16384 + k * 32, SW128),
                                              sdesc(b + kc * r_rows * 128 + k * 32, SW128), id_r, (kc | k) != 0);
+                            if (last_stage) mma_commit_w(&bars->x_free[kc]);
+                        }
                         ring_release();
+                    }
+                } else {
+                    for (int kc = 0; kc < 4; ++kc) {
+                        wait(&bars->y_ready[kc], c_yr[kc].next());
+                        mma_commit_w(&bars->x_free[kc]);
                     }
                 }
                 mma_commit_w(&bars->lg_full);
@@ -443,14 +462,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
             if (!ok) break;
-            // ---- y, column groups 4-7
+            // ---- y, K-blocks 2 and 3 (column groups 4-7)
             wait(&bars->po_full, c_po.next());
             if (!ok) break;
-            y_groups(sX, tmem + lane_addr, r, a.bo, 4, 8);
+            for (int kb = 2; kb < 4; ++kb) {
+                y_groups(sX, tmem + lane_addr, r, a.bo, 2 * kb, 2 * kb + 2);
+                fence_async_shared();
+                arrive(&bars->y_ready[kb]);
+            }
             tc_fence_before();
             arrive(&bars->po_drained);
-            fence_async_shared();
-            arrive(&bars->y_ready);
         }
     } else {
         // ============================ drain group =============================
@@ -460,7 +481,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int wnd = r >> 6;
         const int li = r & 63;
         const int ty = li >> 3, tx = li & 7;
-        Counter c_qkv, c_po, c_lg, c_ystore;
+        Counter c_qkv, c_po, c_lg, c_ystore[4];
         bool ok = true;
         bool first_tile = true;
         const bool storer = (warp == 6 && lane == 0);
@@ -517,35 +538,44 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int h = 0; h < 8 && ok; ++h) drain_qkv(h);
             if (!ok) break;
 
-            // ---- y, column groups 0-3 (the softmax group writes 4-7)
+            // ---- y, K-blocks 0 and 1 (column groups 0-3; the softmax group writes 2 and 3)
             wait(&bars->po_full, c_po.next());
             if (!ok) break;
-            y_groups(sX, tmem + lane_addr, r, a.bo, 0, 4);
+            for (int kb = 0; kb < 2; ++kb) {
+                y_groups(sX, tmem + lane_addr, r, a.bo, 2 * kb, 2 * kb + 2);
+                fence_async_shared();
+                arrive(&bars->y_ready[kb]);
+            }
             tc_fence_before();
             arrive(&bars->po_drained);
-            fence_async_shared();
-            arrive(&bars->y_ready);
-            // one thread stores both windows once every row of y is in smem
-            if (storer && mbar_wait(&bars->y_ready, c_ystore.next(), abort)) {
-                for (int half = 0; half < 2; ++half) {
-                    const int w2 = 2 * tile + half;
-                    if (w2 >= n_windows) continue;
-                    const int f2 = w2 / win_per_frame, wl2 = w2 % win_per_frame;
-                    for (int kb = 0; kb < 4; ++kb)
+            // one thread stores both windows K-block by K-block as y lands, and hands each
+            // K-block of X back to the producer (x_free, with the router GEMM's commit) as
+            // soon as its store has read it
+            if (storer) {
+                for (int kb = 0; kb < 4; ++kb) {
+                    if (!mbar_wait(&bars->y_ready[kb], c_ystore[kb].next(), abort)) break;
+                    for (int half = 0; half < 2; ++half) {
+                        const int w2 = 2 * tile + half;
+                        if (w2 >= n_windows) continue;
+                        const int f2 = w2 / win_per_frame, wl2 = w2 % win_per_frame;
                         tma_store_4d(&tm_y, smem_u32(sX + kb * 16384 + half * 8192), kb * 64, (wl2 % wx_n) * 8,
                                      (wl2 / wx_n) * 8, f2);
+                    }
+                    tma_store_commit();
                 }
-                tma_store_commit();
+                tma_store_wait_read<3>();
+                mbar_arrive(&bars->x_free[0]);
+                tma_store_wait_read<2>();
+                mbar_arrive(&bars->x_free[1]);
+                tma_store_wait_read<1>();
+                mbar_arrive(&bars->x_free[2]);
+                tma_store_wait_read<0>();
+                mbar_arrive(&bars->x_free[3]);
             }
 
             // ---- router: logits = fp16(y . Wr^T + br), first maximum
             wait(&bars->lg_full, c_lg.next());
             if (!ok) break;
-            if (storer) {
-                // the router GEMM is done with y and the store has read it: X may be refilled
-                tma_store_wait_read0();
-                mbar_arrive(&bars->x_free);
-            }
             if (router) {
                 int best = 0;
                 float bv = 0.0f;

@@ -172,6 +172,11 @@ PRISM_DEV void tma_store_4d(const CUtensorMap* map, uint32_t src, int c0, int c1
 }
 PRISM_DEV void tma_store_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 PRISM_DEV void tma_store_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// until at most N of this thread's committed bulk store groups still read shared memory
+template <int N>
+PRISM_DEV void tma_store_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
 PRISM_DEV void tma_store_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 PRISM_DEV void prefetch_tmap(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
