@@ -58,6 +58,18 @@ def test_stack_matches_oracle(prism_ctx, oracle, key, n_blocks, frames):
     _check(prism_ctx, oracle, cfg.layout, blob, x, key)
 
 
+@pytest.mark.parametrize("n_experts", [1, 100, 256])
+def test_stack_expert_counts(prism_ctx, oracle, n_experts):
+    """Router widths at the edges: one expert (16 padded logits), 100 (two router weight
+    stages of 96 + 16 rows), 256 (three stages, logits up to the last TMEM column); the
+    route plan's tile list with many partial tiles."""
+    L = layout.build_stack(256, 1, n_experts=n_experts, up_adapter=True, down_adapter=True)
+    blob = synth.make_blob(L, seed=synth.WEIGHT_SEED + n_experts)
+    x = synth.make_frames(L, 2)
+    _, a = _check(prism_ctx, oracle, L, blob, x, f"{n_experts} experts")
+    assert a.min() >= 0 and a.max() < n_experts
+
+
 @pytest.mark.parametrize("w,h,frames", [(4, 4, 2), (20, 12, 3), (8, 8, 1), (40, 9, 2)])
 def test_stack_odd_frame_shapes(prism_ctx, oracle, w, h, frames):
     """Partial windows in x and y, frames of fewer than 64 tokens (keys = n_tokens),
