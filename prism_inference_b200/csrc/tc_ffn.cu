@@ -12,11 +12,12 @@
 // Warp roles (352 threads):
 //   warp 0     producer: A tile by TMA (contiguous rows) and the W1/W2 K-chunks (TMA,
 //              128B swizzle) through a STAGES-deep ring
-//   warp 10    expert mode: gathers the tile's token rows with TMA tile::gather4 (four
+//   warp 18    expert mode: gathers the tile's token rows with TMA tile::gather4 (four
 //              rows per copy, one copy per lane and K-block), independently of the
 //              weight ring
 //   warp 1     TMEM allocation + single-thread tcgen05.mma issue
-//   warps 2-9  epilogue: warp w reads TMEM lanes 32*(w%4).. (its rows) and one half
+//   warps 2-17 epilogue (four per SM sub-partition, to hide the latency of the per-element
+//              chains): warp w reads TMEM lanes 32*(w%4).. (its rows) and one quarter
 //              of the columns
 // Expert mode replaces the reference's per-expert early-return dispatch loop
 // (moe_expert_skip.comp.glsl:25-54 dispatched N times by prism_moe_bench.cpp:428-436):
@@ -30,8 +31,10 @@ namespace prism {
 
 namespace {
 
-constexpr int kThreads = 352;  // + warp 10: expert-row gather
-constexpr int kEpiWarps = 8;
+constexpr int kEpiWarps = 16;                 // epilogue: 4 per SM sub-partition
+constexpr int kParts = kEpiWarps / 4;          // column parts: warp 2 + 4p + q owns rows 32q.., part p
+constexpr int kGatherWarp = 2 + kEpiWarps;     // expert-row gather
+constexpr int kThreads = 32 * (kGatherWarp + 1);
 
 template <int MODE, int KIN, int HID, int NOUT>
 struct FfnCfg {
@@ -47,12 +50,18 @@ struct FfnCfg {
     static constexpr int kSmem = kA + kH + kStages * kStage + kBarBytes + 1024;  // + alignment slack
 };
 
-// The epilogue writes the H tile by column halves (warps 2-5: K-blocks [0, n/2),
-// warps 6-9: [n/2, n)), each half in column order, so K-blocks become ready in the
+// The epilogue writes the H tile by column parts (kParts of them, each in column
+// order), so K-blocks become ready part by part, interleaved; in the
 // order 0, n/2, 1, n/2+1, ...; GEMM2 consumes them (and the producer loads W2) in it.
 template <int HID>
 __host__ __device__ constexpr int h_block_order(int i) {
-    return (i & 1) ? (HID / 128) + (i >> 1) : (i >> 1);
+    constexpr int bpp = HID / kParts / 64 > 0 ? HID / kParts / 64 : 1;  // K-blocks per column part
+    return (i % kParts) * bpp + i / kParts;
+}
+// Warps that write one 64-column K-block of H (4 row quads x the parts it spans).
+template <int HID>
+__host__ __device__ constexpr int h_block_writers() {
+    return HID / kParts >= 64 ? 4 : 4 * (64 / (HID / kParts));
 }
 
 struct Bars {
@@ -89,7 +98,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_init(&bars->a_empty, 1);  // the MMA warp's commit after the last GEMM1 reading A
         mbar_init(&bars->acc1_full, 1);
         mbar_init(&bars->acc1_empty, kEpiWarps);
-        for (int kb = 0; kb < 4; ++kb) mbar_init(&bars->h_full[kb], kEpiWarps / 2);
+        for (int kb = 0; kb < 4; ++kb) mbar_init(&bars->h_full[kb], h_block_writers<HID>());
         mbar_init(&bars->acc2_full, 1);
         mbar_init(&bars->acc2_empty, kEpiWarps);
         mbar_init(&bars->drain, 1);
@@ -124,7 +133,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             } else {
                 start = tile * 128;
             }
-            // --- A rows by TMA (contiguous modes; the expert gather is warp 10's job)
+            // --- A rows by TMA (contiguous modes; the expert gather is the gather warp's job)
             if (MODE != FFN_EXPERT) {
                 if (!mbar_wait(&bars->a_empty, (it & 1) ^ 1, abort)) { ok = false; break; }
                 if (lane == 0) {
@@ -160,7 +169,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             __syncwarp();
         }
-    } else if (warp == 10) {
+    } else if (warp == kGatherWarp) {
         // ===================== expert-row gather =====================
         if (MODE == FFN_EXPERT) {
             uint32_t it = 0;
@@ -252,7 +261,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp >= 2 && warp < 2 + kEpiWarps) {
         // ===================== epilogue =====================
         const int quad = warp & 3;               // TMEM lanes 32*quad .. +31
-        const int half = (warp - 2) >> 2;        // column half
+        const int half = (warp - 2) >> 2;        // column part (0 .. kParts-1)
         const int row = quad * 32 + lane;        // tile row of this thread
         const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
         uint32_t it = 0, chunk_it = 0;
@@ -270,20 +279,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             const bool row_valid = row < rows;
             const int out_row = MODE == FFN_EXPERT ? (row_valid ? a.perm[start + row] : 0) : start + row;
-            // This warp's bias columns, lane l holding columns 4l .. 4l+3 of its half (HID / 2 and
+            // This warp's bias columns, lane l holding columns 4l .. 4l+3 of its part (HID / kParts and
             // NOUT / 2 are 128 here); loaded as the tile starts so the L2 latency hides behind the
             // GEMM, and handed to the column groups by shuffles.
             static_assert(HID / 2 <= 128 && NOUT / 2 <= 128, "one float4 of bias per lane");
             // fp16 running sum of the dense FFN chunk outputs (attention_windowed_d256.comp.glsl:167-168)
-            uint32_t accum[MODE == FFN_DENSE ? NOUT / 4 : 1];
+            uint32_t accum[MODE == FFN_DENSE ? NOUT / kParts / 2 : 1];
             if (MODE == FFN_DENSE) {
 #pragma unroll
-                for (int i = 0; i < NOUT / 4; ++i) accum[i] = 0u;
+                for (int i = 0; i < NOUT / kParts / 2; ++i) accum[i] = 0u;
             }
             for (int c = 0; c < n_chunks && ok; ++c, ++chunk_it) {
                 // ---- epi1: acc1 -> bias -> fp16 -> activation -> fp16
                 const float* b1 = a.b1 + (size_t)e * HID * n_chunks + c * HID;
-                constexpr int kCols1 = HID / 2;
+                constexpr int kCols1 = HID / kParts;
                 const float4 bias1 = 4 * lane < kCols1 ? ldg_f4(b1 + half * kCols1 + 4 * lane) : make_float4(0, 0, 0, 0);
                 if (!mbar_wait(&bars->acc1_full, chunk_it & 1, abort)) { ok = false; break; }
                 tc_fence_after();
@@ -342,7 +351,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // out through this warp's own slice of the H tile (free once GEMM2 is
                 // done): both global transfers are row-contiguous, 16 lanes per 256 B.
                 const bool last = (c == n_chunks - 1);
-                constexpr int kCols2 = NOUT / 2;           // this warp's column half
+                constexpr int kCols2 = NOUT / kParts;      // this warp's column part
                 constexpr int kRowsPerLd = 512 / (kCols2 * 2);  // rows per 512-B warp access
                 constexpr int kLanesPerRow = 32 / kRowsPerLd;
                 constexpr int kIters = 32 / kRowsPerLd;
