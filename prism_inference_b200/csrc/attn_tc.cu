@@ -48,6 +48,10 @@ constexpr int kStage = 49152;  // weight ring stage: up to 4 K-blocks x [96 rows
 constexpr int kStages = 2;
 constexpr int kRouterRows = 96;  // router rows per ring stage
 
+// Head pair whose out-projection the MMA warp issues at head h: pair p = (2p, 2p + 1) at
+// head 2p + 2 (behind QKV_{2p+3}), the last pair after PV_7; -1 at the other heads.
+PRISM_DEV constexpr int po_pair(int h) { return h == 7 ? 3 : (h >= 2 && (h & 1) == 0) ? h / 2 - 1 : -1; }
+
 // shared-memory map (offsets from the 1024-aligned base)
 constexpr int kOffX = 0;                // 4 K-blocks x [128][128 B] = 64 KB; y overwrites it
 constexpr int kOffQ = kOffX + 65536;    // Q_h [128][64 B] SW64 8 KB
@@ -58,12 +62,15 @@ constexpr int kOffW = kOffAO + 16384;   // ring 2 x 48 KB
 constexpr int kOffBar = kOffW + kStages * kStage;
 
 // TMEM columns
-constexpr uint32_t kTPO = 0;     // out-projection accumulator [256]
-constexpr uint32_t kTQKV = 256;  // QKV_h [96]; router logits reuse [256, 512)
+constexpr uint32_t kTPO = 0;     // out-projection accumulator [256]; router logits reuse [0, npad)
+constexpr uint32_t kTQKV = 256;  // QKV_h [96]
 constexpr uint32_t kTS = 352;    // S_h [128] fp32; P_h overwrites [352, 416) as fp16 pairs
 constexpr uint32_t kTO = 480;    // PV_h [32]
 
 struct Bars {
+    float bqkv[768];  // biases staged once per CTA (read as warp-uniform broadcasts)
+    float bo[256];
+    float br[256];
     uint64_t full[kStages], empty[kStages];
     uint64_t x_full[4], x_free[4], qkv_full, qkv_drained, s_full, p_ready, o_full, o_drained;
     uint64_t ao_ready, ao_free, po_full, po_drained, y_ready[4], lg_full, lg_drained, drain, ep_done;
@@ -80,17 +87,16 @@ struct Counter {  // phase bookkeeping of one barrier as seen by one role
     PRISM_DEV uint32_t next_free() { return ((n++) & 1u) ^ 1u; }  // producer of a free slot
 };
 
-// y = fp16(fp16(PO + bo) + x) for column groups [g0, g1) (32 columns each) of tile row r,
-// written over X in its swizzled slot.  The drain group does groups 0-3, the softmax group
-// (idle at the end of a tile) groups 4-7.
-PRISM_DEV void y_groups(unsigned char* sX, uint32_t row_taddr, int r, const float* bo, int g0, int g1) {
-#pragma unroll 1
-    for (int g = g0; g < g1; ++g) {  // 32 columns = 4 swizzle chunks of K-block g/2
-        float4 bb[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) bb[i] = ldg_f4(bo + g * 32 + 4 * i);
+// y = fp16(fp16(PO + bo) + x) for the 32 columns [32g, 32g + 32) of tile row r, written
+// over X in its swizzled slot (bo staged in shared memory).  K-block kb is chunks 2kb (drain
+// group) and 2kb + 1 (softmax group), so the K-blocks complete in order.
+PRISM_DEV void y_chunk(unsigned char* sX, uint32_t row_taddr, int r, const float* bo, int g) {
+    {
         uint32_t v[32];
         tmem_ld32(row_taddr + kTPO + g * 32, v);
+        float4 bb[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) bb[i] = *reinterpret_cast<const float4*>(bo + g * 32 + 4 * i);
         tmem_ld_wait();
         unsigned char* xblk = sX + (g >> 1) * 16384;
 #pragma unroll
@@ -140,8 +146,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int kb = 0; kb < 4; ++kb) {  // the X tile moves K-block by K-block at tile ends
             mbar_init(&bars->x_full[kb], 1);
-            mbar_init(&bars->x_free[kb], 2);   // y K-block stored (storer) and read by the router GEMM (commit)
-            mbar_init(&bars->y_ready[kb], 4);  // y K-block written (the group that owns it)
+            mbar_init(&bars->x_free[kb], 1);   // y K-block read by the router GEMM (commit)
+            mbar_init(&bars->y_ready[kb], 8);  // y K-block written (both SIMT groups, a chunk each)
         }
         mbar_init(&bars->qkv_full, 1);
         mbar_init(&bars->qkv_drained, 4);
@@ -161,7 +167,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_barrier_init();
         fence_async_shared();
     }
-    for (int i = threadIdx.x; i < 256; i += blockDim.x) bars->hist[i] = 0;
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) {
+        bars->hist[i] = 0;
+        bars->bo[i] = a.bo[i];
+        bars->br[i] = router && i < a.n_experts ? a.br[i] : 0.0f;
+    }
+    for (int i = threadIdx.x; i < 768; i += blockDim.x) bars->bqkv[i] = a.bqkv[i];
     if (warp == 1) tmem_alloc(&bars->tmem_base, 512);
     tc_fence_before();
     __syncthreads();
@@ -194,6 +205,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                 return true;
             };
             const int r_rows = npad < kRouterRows ? npad : kRouterRows;  // rows per router load
+            // y of the previous tile: the TMA store of K-block kb as soon as both groups wrote it
+            int prev = -1;  // previous tile
+            Counter c_yst[4];
+            auto store_y = [&](int t) {
+                for (int kb = 0; kb < 4; ++kb) {
+                    if (!mbar_wait(&bars->y_ready[kb], c_yst[kb].next(), abort)) return false;
+                    for (int half = 0; half < 2; ++half) {
+                        const int w = 2 * t + half;
+                        if (w >= n_windows) continue;
+                        const int f = w / win_per_frame, wl = w % win_per_frame;
+                        tma_store_4d(&tm_y, smem_u32(sX + kb * 16384 + half * 8192), kb * 64, (wl % wx_n) * 8,
+                                     (wl / wx_n) * 8, f);
+                    }
+                    tma_store_commit();
+                }
+                return true;
+            };
             for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
                 int wf[2], wxx[2], wyy[2];
                 for (int half = 0; half < 2; ++half) {
@@ -204,8 +232,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                     wyy[half] = wl / wx_n;
                     wxx[half] = wl % wx_n;
                 }
-                // each K-block as soon as the previous tile has stored and routed it
+                // same order as the MMA warp consumes: QKV_0 (its stage frees when the previous
+                // tile's last out-projection completes), then per head h QKV_{h+1} and, at heads
+                // 2, 4, 6 and after head 7, the Wo columns of the pair before
+                ok = ring_load(&tm_wqkv, true, 0, 0, 96 * 512);
+                if (ok && prev >= 0) ok = store_y(prev);
+                // each X K-block once the previous tile's y K-block has been read by its store
+                // and by the router GEMM (x_free)
                 for (int kb = 0; kb < 4 && ok; ++kb) {
+                    if (prev >= 0) {
+                        if (kb == 0) tma_store_wait_read<3>();
+                        else if (kb == 1) tma_store_wait_read<2>();
+                        else if (kb == 2) tma_store_wait_read<1>();
+                        else tma_store_wait_read<0>();
+                    }
                     if (!mbar_wait(&bars->x_free[kb], c_xfree[kb].next_free(), abort)) {
                         ok = false;
                         break;
@@ -216,22 +256,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                                     wxx[half] * 8, wyy[half] * 8, wf[half]);
                 }
                 if (!ok) break;
-                // same order as the MMA warp consumes: QKV_0, then per head h
-                // QKV_{h+1} and, after every second head, the Wo columns of the pair
-                ok = ring_load(&tm_wqkv, true, 0, 0, 96 * 512);
+                prev = tile;
                 for (int h = 0; h < 8 && ok; ++h) {
                     if (h < 7) ok = ring_load(&tm_wqkv, true, 0, (h + 1) * 96, 96 * 512);
-                    if ((h & 1) && ok) ok = ring_load(&tm_wo, false, (h >> 1) * 64, 0, 256 * 128);
+                    if (po_pair(h) >= 0 && ok) ok = ring_load(&tm_wo, false, po_pair(h) * 64, 0, 256 * 128);
                 }
                 if (router)
                     for (int r0 = 0; r0 < npad && ok; r0 += kRouterRows)
                         ok = ring_load(&tm_wr, true, 0, r0, (uint32_t)r_rows * 512);
             }
+            if (ok && prev >= 0) store_y(prev);
+            tma_store_wait0();
         }
     } else if (warp == 1) {
         // ============================ MMA issuer ==============================
-        // Order per tile: QKV_0; for h: [Q,K,V of h drained] S_h, QKV_{h+1},
-        // [P_h ready, O columns free] PV_h, every second head [pair ready] PO += ...
+        // Order per tile: QKV_0; for h: [Q,K,V of h drained] S_h, QKV_{h+1}, at h = 2, 4, 6
+        // [pair before ready] PO += ..., [P_h ready, O columns free] PV_h; after PV_7 the
+        // last pair's PO
         {
             const uint32_t id_qkv = idesc_f16(128, 96), id_s = idesc_f16(128, 128), id_pv = idesc_f16(128, 32) | (1u << 16) /* B = V MN-major */,
                            id_po = idesc_f16(128, 256);
@@ -276,9 +317,28 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 mma_commit_w(&bars->qkv_full);
             };
+            // ---- PO += O_pair . Wo[:, pair]^T for the pair po_pair(h): issued behind QKV_{h+1}
+            // rather than right after the pair's second PV, so the wait for the pair's
+            // attention output and the four N = 256 MMAs stay off the QKV -> S chain
+            auto issue_po = [&](int h) {
+                const int p = po_pair(h);
+                if (p < 0) return;
+                wait(&bars->ao_ready, c_aor.next());
+                if (p == 0 && !first_tile) {  // PO and the previous tile's logits drained
+                    wait(&bars->po_drained, c_pod.next());
+                    wait(&bars->lg_drained, c_lgd.next());
+                }
+                const uint32_t b = ring_wait();  // Wo[:, pair]: all 256 output rows, N = 256
+                if (ok) {
+#pragma unroll
+                    for (int k = 0; k < 4; ++k)
+                        mma_f16_ss_w(tmem + kTPO, sdesc(smem_u32(sAO) + k * 32, SW128), sdesc(b + k * 32, SW128),
+                                     id_po, (p > 0) || (k != 0));
+                    ring_release();
+                }
+                mma_commit_w(&bars->ao_free);
+            };
             for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
-                // logits of the previous tile live in the QKV/S/O columns
-                if (!first_tile) wait(&bars->lg_drained, c_lgd.next());
                 issue_qkv(true);
                 for (int h = 0; h < 8 && ok; ++h) {
                     const uint32_t vs = smem_u32(sV + (h & 1) * 8192);
@@ -289,6 +349,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                    id_s, k != 0);
                     mma_commit_w(&bars->s_full);
                     if (h < 7) issue_qkv(false);
+                    if (h < 7) issue_po(h);
                     wait(&bars->p_ready, c_pr.next());
                     // O columns free once the softmax group drained the previous head
                     if (h > 0 || !first_tile) wait(&bars->o_drained, c_od.next());
@@ -296,40 +357,32 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int k = 0; k < 8; ++k)
                         mma_f16_ts_w(tmem + kTO, tmem + kTS + k * 8, sdesc(vs + k * 1024, SW64), id_pv, k != 0);
                     mma_commit_w(&bars->o_full);
-                    if (h & 1) {
-                        // ---- PO += O_pair . Wo[:, pair]^T
-                        wait(&bars->ao_ready, c_aor.next());
-                        if (h == 1 && !first_tile) wait(&bars->po_drained, c_pod.next());
-                        const uint32_t b = ring_wait();  // Wo[:, pair]: all 256 output rows, N = 256
-                        if (ok) {
-#pragma unroll
-                            for (int k = 0; k < 4; ++k)
-                                mma_f16_ss_w(tmem + kTPO, sdesc(smem_u32(sAO) + k * 32, SW128), sdesc(b + k * 32, SW128),
-                                             id_po, (h > 1) || (k != 0));
-                            ring_release();
-                        }
-                        mma_commit_w(&bars->ao_free);
-                    }
+                    if (h == 7) issue_po(h);
                 }
                 mma_commit_w(&bars->po_full);
                 // ---- router logits = y . Wr^T, K-block by K-block as y lands; each X K-block
-                // is released (x_free, with the storer's arrival) after its last router MMA
+                // is released (x_free) after its last router MMA
                 if (router) {
                     const uint32_t ys = xs;  // y overwrote X
-                    // up to 96 expert rows per stage (K-block kc at +kc * r_rows rows);
-                    // their logits land in columns kTQKV + r0 ..
+                    int yw = 0;  // y K-blocks waited for
+                    auto need_y = [&](int kb) {
+                        for (; yw <= kb && yw < 4; ++yw) wait(&bars->y_ready[yw], c_yr[yw].next());
+                    };
+                    // up to 96 expert rows per stage (K-block kc at +kc * r_rows rows); their
+                    // logits land in PO columns r0 .., whose y K-blocks must have been drained
                     for (int r0 = 0; r0 < npad && ok; r0 += kRouterRows) {
                         const uint32_t b = ring_wait();
                         if (!ok) break;
                         const int n = npad - r0 < r_rows ? npad - r0 : r_rows;
                         const uint32_t id_r = idesc_f16(128, n);
                         const bool last_stage = r0 + kRouterRows >= npad;
+                        need_y((r0 + n - 1) >> 6);
 #pragma unroll
                         for (int kc = 0; kc < 4; ++kc) {
-                            if (r0 == 0) wait(&bars->y_ready[kc], c_yr[kc].next());
+                            need_y(kc);
 #pragma unroll
                             for (int k = 0; k < 4; ++k)
-                                mma_f16_ss_w(tmem + kTQKV + r0, sdesc(ys + kc * 16384 + k * 32, SW128),
+                                mma_f16_ss_w(tmem + kTPO + r0, sdesc(ys + kc * 16384 + k * 32, SW128),
                                              sdesc(b + kc * r_rows * 128 + k * 32, SW128), id_r, (kc | k) != 0);
                             if (last_stage) mma_commit_w(&bars->x_free[kc]);
                         }
@@ -462,12 +515,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
             if (!ok) break;
-            // ---- y, K-blocks 2 and 3 (column groups 4-7)
+            // ---- y: the odd 32-column chunk of every K-block
             wait(&bars->po_full, c_po.next());
             if (!ok) break;
-            for (int kb = 2; kb < 4; ++kb) {
-                y_groups(sX, tmem + lane_addr, r, a.bo, 2 * kb, 2 * kb + 2);
+            for (int kb = 0; kb < 4; ++kb) {
+                y_chunk(sX, tmem + lane_addr, r, bars->bo, 2 * kb + 1);
                 fence_async_shared();
+                tc_fence_before();
                 arrive(&bars->y_ready[kb]);
             }
             tc_fence_before();
@@ -481,10 +535,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int wnd = r >> 6;
         const int li = r & 63;
         const int ty = li >> 3, tx = li & 7;
-        Counter c_qkv, c_po, c_lg, c_ystore[4];
+        Counter c_qkv, c_po, c_lg;
         bool ok = true;
         bool first_tile = true;
-        const bool storer = (warp == 6 && lane == 0);
         auto wait = [&](uint64_t* bar, uint32_t par) {
             if (ok && !mbar_wait(bar, par, abort)) ok = false;
             tc_fence_after();
@@ -497,14 +550,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         auto drain_qkv = [&](int h) {
             wait(&bars->qkv_full, c_qkv.next());
             if (!ok) return;
-            const float* bq = a.bqkv + h * 96;
+            const float* bq = bars->bqkv + h * 96;
 #pragma unroll
             for (int part = 0; part < 3; ++part) {  // Q, K, V
-                float4 bb[8];
-#pragma unroll
-                for (int i = 0; i < 8; ++i) bb[i] = ldg_f4(bq + part * 32 + 4 * i);
                 uint32_t v[32];
                 tmem_ld32(tmem + lane_addr + kTQKV + part * 32, v);
+                float4 bb[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) bb[i] = *reinterpret_cast<const float4*>(bq + part * 32 + 4 * i);
                 tmem_ld_wait();
                 uint32_t pk[16];
 #pragma unroll
@@ -538,57 +591,40 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int h = 0; h < 8 && ok; ++h) drain_qkv(h);
             if (!ok) break;
 
-            // ---- y, K-blocks 0 and 1 (column groups 0-3; the softmax group writes 2 and 3)
+            // ---- y: the even 32-column chunk of every K-block (the producer stores y)
             wait(&bars->po_full, c_po.next());
             if (!ok) break;
-            for (int kb = 0; kb < 2; ++kb) {
-                y_groups(sX, tmem + lane_addr, r, a.bo, 2 * kb, 2 * kb + 2);
+            for (int kb = 0; kb < 4; ++kb) {
+                y_chunk(sX, tmem + lane_addr, r, bars->bo, 2 * kb);
                 fence_async_shared();
+                tc_fence_before();
                 arrive(&bars->y_ready[kb]);
             }
             tc_fence_before();
             arrive(&bars->po_drained);
-            // one thread stores both windows K-block by K-block as y lands, and hands each
-            // K-block of X back to the producer (x_free, with the router GEMM's commit) as
-            // soon as its store has read it
-            if (storer) {
-                for (int kb = 0; kb < 4; ++kb) {
-                    if (!mbar_wait(&bars->y_ready[kb], c_ystore[kb].next(), abort)) break;
-                    for (int half = 0; half < 2; ++half) {
-                        const int w2 = 2 * tile + half;
-                        if (w2 >= n_windows) continue;
-                        const int f2 = w2 / win_per_frame, wl2 = w2 % win_per_frame;
-                        tma_store_4d(&tm_y, smem_u32(sX + kb * 16384 + half * 8192), kb * 64, (wl2 % wx_n) * 8,
-                                     (wl2 / wx_n) * 8, f2);
-                    }
-                    tma_store_commit();
-                }
-                tma_store_wait_read<3>();
-                mbar_arrive(&bars->x_free[0]);
-                tma_store_wait_read<2>();
-                mbar_arrive(&bars->x_free[1]);
-                tma_store_wait_read<1>();
-                mbar_arrive(&bars->x_free[2]);
-                tma_store_wait_read<0>();
-                mbar_arrive(&bars->x_free[3]);
-            }
 
-            // ---- router: logits = fp16(y . Wr^T + br), first maximum
+            // ---- router: logits (PO columns [0, npad)) = fp16(y . Wr^T + br), first maximum
             wait(&bars->lg_full, c_lg.next());
             if (!ok) break;
             if (router) {
                 int best = 0;
                 float bv = 0.0f;
 #pragma unroll 1
-                for (int g = 0; g * 16 < npad; ++g) {
-                    uint32_t v[16];
-                    tmem_ld16(tmem + lane_addr + kTQKV + g * 16, v);
+                for (int g = 0; g < npad; g += 32) {
+                    uint32_t v[32];
+                    if (g + 32 <= npad) {
+                        tmem_ld32(tmem + lane_addr + kTPO + g, v);
+                    } else {  // npad is a multiple of 16: the last 16 columns
+                        tmem_ld16(tmem + lane_addr + kTPO + g, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
+#pragma unroll
+                        for (int j = 16; j < 32; ++j) v[j] = 0u;
+                    }
                     tmem_ld_wait();
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const int e = g * 16 + j;
+                    for (int j = 0; j < 32; ++j) {
+                        const int e = g + j;
                         if (e < a.n_experts) {
-                            const float l = rh(__fadd_rn(__uint_as_float(v[j]), a.br[e]));
+                            const float l = rh(__fadd_rn(__uint_as_float(v[j]), bars->br[e]));
                             if (e == 0 || l > bv) {
                                 bv = l;
                                 best = e;
@@ -605,7 +641,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             arrive(&bars->lg_drained);
             first_tile = false;
         }
-        if (storer) tma_store_wait0();
         // flush the CTA's routing histogram once every drain warp is done
         arrive(&bars->ep_done);
         if (mbar_wait(&bars->ep_done, 0, abort) && router)
