@@ -87,32 +87,48 @@ struct Counter {  // phase bookkeeping of one barrier as seen by one role
     PRISM_DEV uint32_t next_free() { return ((n++) & 1u) ^ 1u; }  // producer of a free slot
 };
 
-// y = fp16(fp16(PO + bo) + x) for the 32 columns [32g, 32g + 32) of tile row r, written
-// over X in its swizzled slot (bo staged in shared memory).  K-block kb is chunks 2kb (drain
-// group) and 2kb + 1 (softmax group), so the K-blocks complete in order.
-PRISM_DEV void y_chunk(unsigned char* sX, uint32_t row_taddr, int r, const float* bo, int g) {
-    {
-        uint32_t v[32];
-        tmem_ld32(row_taddr + kTPO + g * 32, v);
-        float4 bb[8];
+// y = fp16(fp16(PO + bo) + x) for the 32 columns [32g, 32g + 32) of tile row r (v = PO of
+// those columns), written over X in its swizzled slot (bo staged in shared memory).
+PRISM_DEV void y_chunk(unsigned char* sX, const uint32_t (&v)[32], int r, const float* bo, int g) {
+    unsigned char* xblk = sX + (g >> 1) * 16384;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) bb[i] = *reinterpret_cast<const float4*>(bo + g * 32 + 4 * i);
-        tmem_ld_wait();
-        unsigned char* xblk = sX + (g >> 1) * 16384;
+    for (int c = 0; c < 4; ++c) {
+        const int off = sw128_off(r, (g & 1) * 4 + c);
+        const uint4 x = *reinterpret_cast<const uint4*>(xblk + off);
+        const float4 b0 = *reinterpret_cast<const float4*>(bo + g * 32 + 8 * c);
+        const float4 b1 = *reinterpret_cast<const float4*>(bo + g * 32 + 8 * c + 4);
+        const float* fv = reinterpret_cast<const float*>(&v[8 * c]);
+        // y = h( h(PO + bo) + x ): the second rounding is the fp16 add of :76
+        uint4 y;
+        y.x = hadd2_u32(pack_h2(__fadd_rn(fv[0], b0.x), __fadd_rn(fv[1], b0.y)), x.x);
+        y.y = hadd2_u32(pack_h2(__fadd_rn(fv[2], b0.z), __fadd_rn(fv[3], b0.w)), x.y);
+        y.z = hadd2_u32(pack_h2(__fadd_rn(fv[4], b1.x), __fadd_rn(fv[5], b1.y)), x.z);
+        y.w = hadd2_u32(pack_h2(__fadd_rn(fv[6], b1.z), __fadd_rn(fv[7], b1.w)), x.w);
+        *reinterpret_cast<uint4*>(xblk + off) = y;
+    }
+}
+
+// One SIMT group's share of y: chunk 2kb + part of every K-block kb, in order, each K-block
+// announced on y_ready[kb] (with the other group's chunk it completes the K-block).  The
+// TMEM load of the next chunk is in flight while the current one is computed; the router
+// GEMM writes logits only over K-blocks already announced, so the load in flight is never
+// overwritten.
+PRISM_DEV void y_share(unsigned char* sX, uint32_t row_taddr, int r, const float* bo, int part, uint64_t* y_ready,
+                       int lane) {
+    uint32_t va[32], vb[32];
+    tmem_ld32(row_taddr + kTPO + part * 32, va);
+    tmem_ld_wait();
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            const int off = sw128_off(r, (g & 1) * 4 + c);
-            const uint4 x = *reinterpret_cast<const uint4*>(xblk + off);
-            const float4 b0 = bb[2 * c], b1 = bb[2 * c + 1];
-            const float* fv = reinterpret_cast<const float*>(&v[8 * c]);
-            // y = h( h(PO + bo) + x ): the second rounding is the fp16 add of :76
-            uint4 y;
-            y.x = hadd2_u32(pack_h2(__fadd_rn(fv[0], b0.x), __fadd_rn(fv[1], b0.y)), x.x);
-            y.y = hadd2_u32(pack_h2(__fadd_rn(fv[2], b0.z), __fadd_rn(fv[3], b0.w)), x.y);
-            y.z = hadd2_u32(pack_h2(__fadd_rn(fv[4], b1.x), __fadd_rn(fv[5], b1.y)), x.z);
-            y.w = hadd2_u32(pack_h2(__fadd_rn(fv[6], b1.z), __fadd_rn(fv[7], b1.w)), x.w);
-            *reinterpret_cast<uint4*>(xblk + off) = y;
-        }
+    for (int kb = 0; kb < 4; ++kb) {
+        uint32_t(&cur)[32] = (kb & 1) ? vb : va;
+        uint32_t(&nxt)[32] = (kb & 1) ? va : vb;
+        if (kb < 3) tmem_ld32(row_taddr + kTPO + (2 * (kb + 1) + part) * 32, nxt);
+        y_chunk(sX, cur, r, bo, 2 * kb + part);
+        fence_async_shared();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&y_ready[kb]);
+        if (kb < 3) tmem_ld_wait();
     }
 }
 
@@ -518,12 +534,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // ---- y: the odd 32-column chunk of every K-block
             wait(&bars->po_full, c_po.next());
             if (!ok) break;
-            for (int kb = 0; kb < 4; ++kb) {
-                y_chunk(sX, tmem + lane_addr, r, bars->bo, 2 * kb + 1);
-                fence_async_shared();
-                tc_fence_before();
-                arrive(&bars->y_ready[kb]);
-            }
+            y_share(sX, tmem + lane_addr, r, bars->bo, 1, bars->y_ready, lane);
             tc_fence_before();
             arrive(&bars->po_drained);
         }
@@ -594,12 +605,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // ---- y: the even 32-column chunk of every K-block (the producer stores y)
             wait(&bars->po_full, c_po.next());
             if (!ok) break;
-            for (int kb = 0; kb < 4; ++kb) {
-                y_chunk(sX, tmem + lane_addr, r, bars->bo, 2 * kb);
-                fence_async_shared();
-                tc_fence_before();
-                arrive(&bars->y_ready[kb]);
-            }
+            y_share(sX, tmem + lane_addr, r, bars->bo, 0, bars->y_ready, lane);
             tc_fence_before();
             arrive(&bars->po_drained);
 
