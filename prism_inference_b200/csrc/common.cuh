@@ -127,6 +127,10 @@ PRISM_DEV void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
                  : "memory");
 }
 
+// cp.async groups of this thread: close the current group / wait until all have landed
+PRISM_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+PRISM_DEV void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
 // generic-proxy shared-memory writes -> visible to the async proxy (TMA, tcgen05)
 PRISM_DEV void fence_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 

@@ -1,0 +1,355 @@
+// expert_tc.cu - grouped expert FFN of a Prism MoE block on the sm_100a tensor cores.
+//
+// For every row (token) routed to expert e (moe_expert_skip.comp.glsl:25-54):
+//     h   = fp16(gelu(fp16(W1_e x + b1_e)))        (GELU in fp32 on the fp16 value)
+//     out = fp16(fp16(W2_e h + b2_e) + x)          (the residual add is an fp16 add, :52)
+// The reference dispatches the expert shader once per expert with an early return for
+// tokens of other experts (prism_moe_bench.cpp:428-436); here the tiles of all experts run
+// in one launch: a tile holds up to 128 rows of one expert (the permutation and tile list
+// of route_kernels.cu), gathered from the token rows and scattered back.
+//
+// One persistent CTA per SM walks the tiles.  Per tile:
+//   GEMM1  acc1[128 x 256] = A . W1_e^T            A = gathered rows in smem, tcgen05 SS
+//   E1     h = gelu(...) packed as fp16 pairs over acc1 itself (TMEM): column part p
+//          (128 columns) keeps its H K-blocks in [128p, 128p + 64), each written over
+//          columns the same thread has already read
+//   GEMM2  acc2[128 x 256] = H . W2_e^T            A = H from TMEM (tcgen05 TS form)
+//   E2     out = fp16(fp16(acc2 + b2) + x), x (the same token rows) brought into a smem
+//          staging tile by cp.async while GEMM2 runs, stored row-contiguously
+// E1 and E2 are separate warp groups, so E2 of tile i runs while E1 works on tile i+1 (and
+// GEMM1 of tile i+1 runs while E2 of tile i finishes): acc1 and acc2 are each single
+// buffers and every hand-off is an mbarrier.  The MMA warp issues GEMM2(i) before
+// GEMM1(i+1), so GEMM2 has read H (in acc1) before GEMM1(i+1) overwrites it.
+//
+// Warp roles (608 threads):
+//   warp 0      producer: W1_e / W2_e K-chunks (TMA, 128B swizzle) through a 3-stage ring
+//   warp 1      TMEM owner + tcgen05.mma issuer (converged warp, elected lane)
+//   warp 2      row gather: TMA tile::gather4, four token rows per copy
+//   warps 3-10  E1: warp w reads TMEM lanes 32*(w%4).. and column part (w-3)/4
+//   warps 11-18 E2: likewise with part (w-11)/4
+// Every wait is bounded (common.cuh); on timeout the CTA sets the error word and winds
+// down.  No TMA multicast.
+#include "common.cuh"
+#include "tc_ffn.cuh"
+
+namespace prism {
+namespace {
+
+constexpr int kD = 256;                   // model / hidden width
+constexpr int kE1Base = 3, kE2Base = 11;  // first warp of each epilogue group
+constexpr int kThreads = 32 * 19;
+constexpr int kStage = 256 * 128;         // one W K-chunk: 256 rows x 64 columns fp16
+constexpr int kStages = 3;
+constexpr int kTile = 128 * kD * 2;       // a [128][256] fp16 tile as 4 K-major SW128 K-blocks
+constexpr int kOffA = 0;                  // gathered rows (GEMM1's A)
+constexpr int kOffO = kOffA + kTile;      // E2 staging: residual rows in, output rows out
+constexpr int kOffW = kOffO + kTile;
+constexpr int kOffBar = kOffW + kStages * kStage;
+constexpr uint32_t kAcc1 = 0, kAcc2 = 256;
+
+struct Bars {
+    uint64_t full[kStages], empty[kStages];
+    uint64_t a_full, a_empty, acc1_full, acc1_empty, h_full[4], acc2_full, acc2_empty, drain;
+    uint32_t tmem_base;
+    int abort;
+};
+constexpr int kSmem = kOffBar + (int)sizeof(Bars) + 1024;  // + alignment slack of the dynamic base
+static_assert(kSmem <= 232448, "shared memory budget");
+
+// GEMM2 consumes the H K-blocks in the order E1 completes them: part 0 writes K-blocks 0, 1
+// and part 1 K-blocks 2, 3, both parts at once
+PRISM_DEV constexpr int h_order(int i) { return (i & 1) * 2 + (i >> 1); }
+// TMEM column of H K-block kb (32 columns = 64 fp16 K values)
+PRISM_DEV constexpr uint32_t h_col(int kb) { return kAcc1 + 128u * (kb >> 1) + 32u * (kb & 1); }
+
+// staging-tile address of (tile row R, column col): K-major SW128 K-blocks of 64 columns
+PRISM_DEV unsigned char* oslot(unsigned char* sO, int R, int col) {
+    return sO + (col >> 6) * 16384 + sw128_off(R, (col & 63) >> 3);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    expert_tc_kernel(const FfnArgs a, const __grid_constant__ CUtensorMap tm_x,
+                     const __grid_constant__ CUtensorMap tm_w1, const __grid_constant__ CUtensorMap tm_w2) {
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    unsigned char* sA = smem + kOffA;
+    unsigned char* sO = smem + kOffO;
+    unsigned char* sW = smem + kOffW;
+    Bars* bars = reinterpret_cast<Bars*>(smem + kOffBar);
+    volatile int* abort = &bars->abort;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n_tiles = *a.n_tiles;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&bars->full[s], 1);
+            mbar_init(&bars->empty[s], 1);
+        }
+        mbar_init(&bars->a_full, 1);
+        mbar_init(&bars->a_empty, 1);     // GEMM1 has read A (commit)
+        mbar_init(&bars->acc1_full, 1);
+        mbar_init(&bars->acc1_empty, 8);  // E1 has read acc1 (its H stays for GEMM2, issued first)
+        for (int kb = 0; kb < 4; ++kb) mbar_init(&bars->h_full[kb], 4);  // the 4 row quads of a part
+        mbar_init(&bars->acc2_full, 1);
+        mbar_init(&bars->acc2_empty, 8);  // E2 has read acc2
+        mbar_init(&bars->drain, 1);
+        bars->abort = 0;
+        fence_barrier_init();
+        fence_async_shared();
+    }
+    if (warp == 1) tmem_alloc(&bars->tmem_base, 512);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = bars->tmem_base;
+
+    if (warp == 0) {
+        // ============================ producer ============================
+        if (lane == 0) {
+            prefetch_tmap(&tm_w1);
+            prefetch_tmap(&tm_w2);
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            auto load = [&](const CUtensorMap* map, int col, int row) {
+                if (!mbar_wait(&bars->empty[stage], phase ^ 1, abort)) return false;
+                mbar_expect_tx(&bars->full[stage], kStage);
+                tma_load_2d(smem_u32(sW + stage * kStage), map, &bars->full[stage], col, row);
+                if (++stage == kStages) {
+                    stage = 0;
+                    phase ^= 1;
+                }
+                return true;
+            };
+            for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
+                const int e = a.tiles[tile].expert;
+                for (int kc = 0; kc < 4 && ok; ++kc) ok = load(&tm_w1, kc * 64, e * kD);      // W1_e
+                for (int i = 0; i < 4 && ok; ++i) ok = load(&tm_w2, h_order(i) * 64, e * kD);  // W2_e
+            }
+        }
+    } else if (warp == 2) {
+        // ============================ row gather ============================
+        // lane l gathers tile rows 4l .. 4l+3; rows past the tile take row n_rows, outside
+        // the map, which the copy zero-fills
+        prefetch_tmap(&tm_x);
+        uint32_t it = 0;
+        const uint32_t a_base = smem_u32(sA);
+        for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
+            const ExpertTile t = a.tiles[tile];
+            int tok[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int r = 4 * lane + i;
+                tok[i] = r < t.rows ? a.perm[t.start + r] : a.n_rows;
+            }
+            if (!mbar_wait_w(&bars->a_empty, (it & 1) ^ 1, abort)) break;
+            if (lane == 0) mbar_expect_tx(&bars->a_full, kTile);
+            __syncwarp();
+#pragma unroll
+            for (int kb = 0; kb < 4; ++kb)
+                tma_gather4(a_base + kb * 16384 + lane * 512, &tm_x, &bars->a_full, kb * 64, tok[0], tok[1], tok[2],
+                            tok[3]);
+        }
+    } else if (warp == 1) {
+        // ============================ MMA issuer ============================
+        constexpr uint32_t idesc = idesc_f16(128, 256);
+        int stage = 0;
+        uint32_t phase = 0;
+        uint32_t it = 0;
+        bool ok = true;
+        auto wait = [&](uint64_t* bar, uint32_t par) {
+            if (ok && !mbar_wait_w(bar, par, abort)) ok = false;
+            tc_fence_after();
+        };
+        for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, ++it) {
+            // ---- GEMM1: acc1 = A . W1^T (E1 done with the previous tile's acc1)
+            wait(&bars->a_full, it & 1);
+            wait(&bars->acc1_empty, (it & 1) ^ 1);
+            for (int kc = 0; kc < 4 && ok; ++kc) {
+                wait(&bars->full[stage], phase);
+                if (!ok) break;
+                const uint32_t a0 = smem_u32(sA + kc * 16384), b0 = smem_u32(sW + stage * kStage);
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    mma_f16_ss_w(tmem + kAcc1, sdesc(a0 + k * 32, SW128), sdesc(b0 + k * 32, SW128), idesc,
+                                 (kc | k) != 0);
+                mma_commit_w(&bars->empty[stage]);
+                if (++stage == kStages) {
+                    stage = 0;
+                    phase ^= 1;
+                }
+            }
+            mma_commit_w(&bars->acc1_full);
+            mma_commit_w(&bars->a_empty);
+            // ---- GEMM2: acc2 = H . W2^T, H K-blocks from TMEM as E1 hands them over
+            // (E2 done with the previous tile's acc2)
+            wait(&bars->acc2_empty, (it & 1) ^ 1);
+            for (int i = 0; i < 4 && ok; ++i) {
+                const int kb = h_order(i);
+                wait(&bars->h_full[kb], it & 1);
+                wait(&bars->full[stage], phase);
+                if (!ok) break;
+                const uint32_t b0 = smem_u32(sW + stage * kStage);
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    mma_f16_ts_w(tmem + kAcc2, tmem + h_col(kb) + 8 * k, sdesc(b0 + k * 32, SW128), idesc,
+                                 (i | k) != 0);
+                mma_commit_w(&bars->empty[stage]);
+                if (++stage == kStages) {
+                    stage = 0;
+                    phase ^= 1;
+                }
+            }
+            mma_commit_w(&bars->acc2_full);
+        }
+        // every issued MMA has completed before TMEM is released
+        mma_commit_w(&bars->drain);
+        mbar_wait_w(&bars->drain, 0, abort);
+    } else if (warp < kE2Base) {
+        // ============================ E1: acc1 -> H ============================
+        const int quad = warp & 3;               // TMEM lanes 32*quad .. +31
+        const int part = (warp - kE1Base) >> 2;  // columns [128 part, 128 part + 128)
+        const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
+        uint32_t it = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, ++it) {
+            const int e = a.tiles[tile].expert;
+            // lane l holds bias columns 4l .. 4l+3 of the part, handed out by shuffles
+            const float4 bias = ldg_f4(a.b1 + (size_t)e * kD + part * 128 + 4 * lane);
+            if (!mbar_wait_w(&bars->acc1_full, it & 1, abort)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+#pragma unroll 1
+            for (int g = 0; g < 4; ++g) {
+                uint32_t r[32];
+                tmem_ld32(tmem + lane_addr + kAcc1 + part * 128 + g * 32, r);
+                tmem_ld_wait();
+                uint32_t packed[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    // columns 32g + 2j, +1 of the part live in lane 8g + j/2
+                    const float bx = __shfl_sync(0xffffffffu, (j & 1) ? bias.z : bias.x, g * 8 + (j >> 1));
+                    const float by = __shfl_sync(0xffffffffu, (j & 1) ? bias.w : bias.y, g * 8 + (j >> 1));
+                    // t = h(acc + b1): one rounding per coopVecMatMulAddNV result
+                    const uint32_t t = pack_h2(__fadd_rn(__uint_as_float(r[2 * j]), bx),
+                                               __fadd_rn(__uint_as_float(r[2 * j + 1]), by));
+                    packed[j] = pack_h2(gelu_f32(lo_h2f(t)), gelu_f32(hi_h2f(t)));
+                }
+                // H columns 32g .. 32g+31 of the part -> TMEM [128 part + 16g, +16), over
+                // fp32 columns this thread has already read
+                tmem_st16(tmem + lane_addr + kAcc1 + part * 128 + g * 16, packed);
+                if (g & 1) {  // H K-block 2 part + g/2 complete for this warp's rows
+                    tmem_st_wait();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&bars->h_full[2 * part + (g >> 1)]);
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->acc1_empty);
+        }
+    } else {
+        // ====================== E2: acc2 -> out (+ residual) ======================
+        const int quad = warp & 3;
+        const int part = (warp - kE2Base) >> 2;
+        const int row = quad * 32 + lane;  // tile row of this thread (= TMEM lane)
+        const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
+        // row-contiguous transfers: 16 lanes x 16 B cover a row's 128 columns of the part,
+        // two rows per warp instruction
+        const int sub_row = lane >> 4, sub_col = (lane & 15) * 8;
+        uint32_t it = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, ++it) {
+            const ExpertTile t = a.tiles[tile];
+            const bool row_valid = row < t.rows;
+            const int out_row = row_valid ? a.perm[t.start + row] : 0;
+            // the residual rows (the tile's input rows, L2-resident) into this warp's slice of
+            // the staging tile; invalid rows zero-filled
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const int lr = 2 * i + sub_row;
+                const int tk = __shfl_sync(0xffffffffu, out_row, lr);
+                const int vld = __shfl_sync(0xffffffffu, (int)row_valid, lr);
+                cp_async16(smem_u32(oslot(sO, quad * 32 + lr, part * 128 + sub_col)),
+                           a.x + (size_t)(vld ? tk : 0) * kD + part * 128 + sub_col, vld ? 16u : 0u);
+            }
+            cp_async_commit();
+            const float4 bias = ldg_f4(a.b2 + (size_t)t.expert * kD + part * 128 + 4 * lane);
+            if (!mbar_wait_w(&bars->acc2_full, it & 1, abort)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            cp_async_wait_all();
+            __syncwarp();
+#pragma unroll 1
+            for (int g = 0; g < 4; ++g) {
+                const int col0 = part * 128 + g * 32;
+                uint32_t r[32];
+                tmem_ld32(tmem + lane_addr + kAcc2 + col0, r);
+                tmem_ld_wait();
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    uint4* slot = reinterpret_cast<uint4*>(oslot(sO, row, col0 + 8 * q));
+                    const uint4 x = *slot;
+                    const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
+                    uint32_t z[4];
+#pragma unroll
+                    for (int jj = 0; jj < 4; ++jj) {
+                        const int j = 4 * q + jj;
+                        const float bx = __shfl_sync(0xffffffffu, (j & 1) ? bias.z : bias.x, g * 8 + (j >> 1));
+                        const float by = __shfl_sync(0xffffffffu, (j & 1) ? bias.w : bias.y, g * 8 + (j >> 1));
+                        // z = h(h(acc + b2) + x): the fp16 residual add of moe_expert_skip.comp.glsl:52
+                        z[jj] = hadd2_u32(pack_h2(__fadd_rn(__uint_as_float(r[2 * j]), bx),
+                                                  __fadd_rn(__uint_as_float(r[2 * j + 1]), by)),
+                                          xs[jj]);
+                    }
+                    *slot = make_uint4(z[0], z[1], z[2], z[3]);
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->acc2_empty);  // acc2 read: GEMM2 of the next tile may go
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const int lr = 2 * i + sub_row;
+                const int tk = __shfl_sync(0xffffffffu, out_row, lr);
+                const int vld = __shfl_sync(0xffffffffu, (int)row_valid, lr);
+                const uint4 v = *reinterpret_cast<const uint4*>(oslot(sO, quad * 32 + lr, part * 128 + sub_col));
+                if (vld) *reinterpret_cast<uint4*>(a.y + (size_t)tk * kD + part * 128 + sub_col) = v;
+            }
+            __syncwarp();  // the slice is free for the next tile's residual rows
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (bars->abort) {
+        if (threadIdx.x == 0) atomicOr(a.err, ERR_TIMEOUT);
+        // let any copy still in flight land before the CTA exits
+        const uint64_t t0 = globaltimer();
+        while (globaltimer() - t0 < 1000000ull) {
+        }
+    }
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_ffn_expert256(const FfnArgs& a, const CUtensorMap& x_rows, const CUtensorMap& w1,
+                                 const CUtensorMap& w2, int grid, cudaStream_t s) {
+    cudaError_t e = cudaFuncSetAttribute(expert_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    if (e != cudaSuccess) return e;
+    if (grid <= 0) return cudaSuccess;
+    expert_tc_kernel<<<grid, kThreads, kSmem, s>>>(a, x_rows, w1, w2);
+    return cudaGetLastError();
+}
+
+}  // namespace prism

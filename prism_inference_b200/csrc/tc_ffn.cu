@@ -477,10 +477,6 @@ cudaError_t launch_ffn(const FfnArgs& a, const CUtensorMap& tx, const CUtensorMa
 
 }  // namespace
 
-cudaError_t launch_ffn_expert256(const FfnArgs& a, const CUtensorMap& x_rows, const CUtensorMap& w1,
-                                 const CUtensorMap& w2, int grid, cudaStream_t s) {
-    return launch_ffn<FFN_EXPERT, 256, 256, 256>(a, x_rows, w1, w2, 1, grid, s);
-}
 cudaError_t launch_ffn_dense256(const FfnArgs& a, const CUtensorMap& x, const CUtensorMap& w1, const CUtensorMap& w2,
                                 int n_chunks, int grid, cudaStream_t s) {
     return launch_ffn<FFN_DENSE, 256, 256, 256>(a, x, w1, w2, n_chunks, grid, s);
