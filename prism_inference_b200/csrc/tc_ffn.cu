@@ -4,26 +4,21 @@
 //   GEMM1  acc1[128 x HID] = A[128 x KIN] . W1^T         (TMEM, fp32)
 //   epi1   h = act(fp16(acc1 + b1))  -> fp16 tile H in shared memory (K-major SW128)
 //   GEMM2  acc2[128 x NOUT] = H . W2^T                     (TMEM, fp32)   [two-GEMM modes]
-//   epi2   out = fp16(fp16(acc2 + b2) + x)  (expert)  or the chunked dense rule
+//   epi2   the chunked dense rule (fp16 sum of chunk outputs, residual add)
 // The rounding points are those of the reference shaders: every coopVecMatMulAddNV
 // result is rounded to fp16 once (acc + bias), GELU is evaluated in fp32 on that
 // fp16 value and rounded again, the residual add is an fp16 add.
 //
-// Warp roles (352 threads):
+// Modes: the 128<->256 adapters (one GEMM) and the dense FFN of a dense block (two GEMMs,
+// NCH chunks); the grouped expert FFN has its own kernel (expert_tc.cu).
+//
+// Warp roles (576 threads):
 //   warp 0     producer: A tile by TMA (contiguous rows) and the W1/W2 K-chunks (TMA,
 //              128B swizzle) through a STAGES-deep ring
-//   warp 18    expert mode: gathers the tile's token rows with TMA tile::gather4 (four
-//              rows per copy, one copy per lane and K-block), independently of the
-//              weight ring
 //   warp 1     TMEM allocation + single-thread tcgen05.mma issue
 //   warps 2-17 epilogue (four per SM sub-partition, to hide the latency of the per-element
 //              chains): warp w reads TMEM lanes 32*(w%4).. (its rows) and one quarter
 //              of the columns
-// Expert mode replaces the reference's per-expert early-return dispatch loop
-// (moe_expert_skip.comp.glsl:25-54 dispatched N times by prism_moe_bench.cpp:428-436):
-// the tiles of all experts run in one launch, each tile holding up to 128 tokens of
-// one expert (the permutation built by route_kernels.cu), and the epilogue scatters
-// the rows back to their token positions with the residual add fused.
 #include "common.cuh"
 #include "tc_ffn.cuh"
 
@@ -33,12 +28,12 @@ namespace {
 
 constexpr int kEpiWarps = 16;                 // epilogue: 4 per SM sub-partition
 constexpr int kParts = kEpiWarps / 4;          // column parts: warp 2 + 4p + q owns rows 32q.., part p
-constexpr int kGatherWarp = 2 + kEpiWarps;     // expert-row gather
-constexpr int kThreads = 32 * (kGatherWarp + 1);
+constexpr int kThreads = 32 * (2 + kEpiWarps);
 
 template <int MODE, int KIN, int HID, int NOUT>
 struct FfnCfg {
-    static constexpr bool kTwoGemm = (MODE == FFN_EXPERT || MODE == FFN_DENSE);
+    static_assert(MODE != FFN_EXPERT, "the expert FFN is expert_tc.cu");
+    static constexpr bool kTwoGemm = (MODE == FFN_DENSE);
     static constexpr int kA = KIN * 128 * 2;                    // A tile bytes
     static constexpr int kH = kTwoGemm ? HID * 128 * 2 : 0;     // H tile bytes
     static constexpr int kWRows = HID > NOUT ? HID : NOUT;      // rows of one W K-chunk
@@ -87,7 +82,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     volatile int* abort = &bars->abort;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n_tiles = MODE == FFN_EXPERT ? *a.n_tiles : (a.n_rows + 127) / 128;
+    const int n_tiles = (a.n_rows + 127) / 128;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < Cfg::kStages; ++s) {
@@ -124,24 +119,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t it = 0;
         bool ok = true;
         for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, ++it) {
-            int e = 0, start = 0, rows = 128;
-            if (MODE == FFN_EXPERT) {
-                const ExpertTile t = a.tiles[tile];
-                e = t.expert;
-                start = t.start;
-                rows = t.rows;
-            } else {
-                start = tile * 128;
-            }
-            // --- A rows by TMA (contiguous modes; the expert gather is the gather warp's job)
-            if (MODE != FFN_EXPERT) {
-                if (!mbar_wait(&bars->a_empty, (it & 1) ^ 1, abort)) { ok = false; break; }
-                if (lane == 0) {
-                    mbar_expect_tx(&bars->a_full, Cfg::kA);
+            const int start = tile * 128;
+            // --- A rows by TMA
+            if (!mbar_wait(&bars->a_empty, (it & 1) ^ 1, abort)) { ok = false; break; }
+            if (lane == 0) {
+                mbar_expect_tx(&bars->a_full, Cfg::kA);
 #pragma unroll
-                    for (int kb = 0; kb < KIN / 64; ++kb)
-                        tma_load_2d(smem_u32(sA + kb * 16384), &tm_x, &bars->a_full, kb * 64, start);
-                }
+                for (int kb = 0; kb < KIN / 64; ++kb)
+                    tma_load_2d(smem_u32(sA + kb * 16384), &tm_x, &bars->a_full, kb * 64, start);
             }
             // --- weight K-chunks, in the order the MMA warp consumes them
             for (int c = 0; c < n_chunks && ok; ++c) {
@@ -149,8 +134,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (!mbar_wait(&bars->empty[stage], phase ^ 1, abort)) { ok = false; break; }
                     if (lane == 0) {
                         mbar_expect_tx(&bars->full[stage], HID * 128);
-                        const int row = MODE == FFN_EXPERT ? e * HID : c * HID;
-                        tma_load_2d(smem_u32(sW + stage * Cfg::kStage), &tm_w1, &bars->full[stage], kc * 64, row);
+                        tma_load_2d(smem_u32(sW + stage * Cfg::kStage), &tm_w1, &bars->full[stage], kc * 64, c * HID);
                     }
                     if (++stage == Cfg::kStages) { stage = 0; phase ^= 1; }
                 }
@@ -160,39 +144,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (!mbar_wait(&bars->empty[stage], phase ^ 1, abort)) { ok = false; break; }
                     if (lane == 0) {
                         mbar_expect_tx(&bars->full[stage], NOUT * 128);
-                        const int col = (MODE == FFN_EXPERT ? 0 : c * HID) + kc * 64;
-                        const int row = MODE == FFN_EXPERT ? e * NOUT : 0;
-                        tma_load_2d(smem_u32(sW + stage * Cfg::kStage), &tm_w2, &bars->full[stage], col, row);
+                        tma_load_2d(smem_u32(sW + stage * Cfg::kStage), &tm_w2, &bars->full[stage], c * HID + kc * 64, 0);
                     }
                     if (++stage == Cfg::kStages) { stage = 0; phase ^= 1; }
                 }
             }
             __syncwarp();
-        }
-    } else if (warp == kGatherWarp) {
-        // ===================== expert-row gather =====================
-        if (MODE == FFN_EXPERT) {
-            uint32_t it = 0;
-            const uint32_t a_base = smem_u32(sA);
-            for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
-                const ExpertTile t = a.tiles[tile];
-                // lane l gathers tile rows 4l .. 4l+3 with TMA (tile::gather4): token rows of
-                // the attention output; rows past the tile take row n_rows, outside the map,
-                // which the copy zero-fills
-                int tok[4];
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const int r = 4 * lane + i;
-                    tok[i] = r < t.rows ? a.perm[t.start + r] : a.n_rows;
-                }
-                if (!mbar_wait(&bars->a_empty, (it & 1) ^ 1, abort)) break;
-                if (lane == 0) mbar_expect_tx(&bars->a_full, Cfg::kA);
-                __syncwarp();
-#pragma unroll
-                for (int kb = 0; kb < KIN / 64; ++kb)
-                    tma_gather4(a_base + kb * 16384 + lane * 512, &tm_x, &bars->a_full, kb * 64, tok[0], tok[1],
-                                tok[2], tok[3]);
-            }
         }
     } else if (warp == 1) {
         // ===================== MMA issuer =====================
@@ -267,18 +224,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t it = 0, chunk_it = 0;
         bool ok = true;
         for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, ++it) {
-            int e = 0, start = 0, rows = 128;
-            if (MODE == FFN_EXPERT) {
-                const ExpertTile t = a.tiles[tile];
-                e = t.expert;
-                start = t.start;
-                rows = t.rows;
-            } else {
-                start = tile * 128;
-                rows = min(128, a.n_rows - start);
-            }
+            const int e = 0;
+            const int start = tile * 128;
+            const int rows = min(128, a.n_rows - start);
             const bool row_valid = row < rows;
-            const int out_row = MODE == FFN_EXPERT ? (row_valid ? a.perm[start + row] : 0) : start + row;
+            const int out_row = start + row;
             // This warp's bias columns, lane l holding columns 4l .. 4l+3 of its part (HID / kParts and
             // NOUT / 2 are 128 here); loaded as the tile starts so the L2 latency hides behind the
             // GEMM, and handed to the column groups by shuffles.
@@ -311,7 +261,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         // t = h(acc + b1): one rounding per coopVecMatMulAddNV result
                         const uint32_t t = pack_h2(__fadd_rn(__uint_as_float(r[2 * j]), bx),
                                                    __fadd_rn(__uint_as_float(r[2 * j + 1]), by));
-                        if (MODE == FFN_EXPERT || MODE == FFN_DENSE) {
+                        if (MODE == FFN_DENSE) {
                             packed[j] = pack_h2(gelu_f32(lo_h2f(t)), gelu_f32(hi_h2f(t)));
                         } else if (MODE == FFN_PROJ_UP) {
                             const float v0 = lo_h2f(t), v1 = hi_h2f(t);
@@ -423,7 +373,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 z[j] = pack_h2(__fadd_rn(__fsub_rn(lo_h2f(acc), __fmul_rn(corr, bx)), lo_h2f(xs[j])),
                                                __fadd_rn(__fsub_rn(hi_h2f(acc), __fmul_rn(corr, by)), hi_h2f(xs[j])));
                             } else {
-                                // z = h(r + y), an fp16 add (moe_expert_skip.comp.glsl:52)
+                                // one chunk: z = h(r + y), an fp16 residual add
                                 z[j] = hadd2_u32(part[k], xs[j]);
                             }
                         }
