@@ -24,7 +24,8 @@
 // Warp roles (608 threads):
 //   warp 0      producer: W1_e / W2_e K-chunks (TMA, 128B swizzle) through a 3-stage ring
 //   warp 1      TMEM owner + tcgen05.mma issuer (converged warp, elected lane)
-//   warp 2      row gather: TMA tile::gather4, four token rows per copy
+//   warp 2      row gather: cp.async, one 512-byte token row per warp instruction (the
+//               TMA engine is left to the weight ring)
 //   warps 3-10  E1: warp w reads TMEM lanes 32*(w%4).. and column part (w-3)/4
 //   warps 11-18 E2: likewise with part (w-11)/4
 // Every wait is bounded (common.cuh); on timeout the CTA sets the error word and winds
@@ -86,7 +87,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&bars->full[s], 1);
             mbar_init(&bars->empty[s], 1);
         }
-        mbar_init(&bars->a_full, 1);
+        mbar_init(&bars->a_full, 32);     // the gather warp's lanes, once their cp.async landed
         mbar_init(&bars->a_empty, 1);     // GEMM1 has read A (commit)
         mbar_init(&bars->acc1_full, 1);
         mbar_init(&bars->acc1_empty, 8);  // E1 has read acc1 (its H stays for GEMM2, issued first)
@@ -130,26 +131,31 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp == 2) {
         // ============================ row gather ============================
-        // lane l gathers tile rows 4l .. 4l+3; rows past the tile take row n_rows, outside
-        // the map, which the copy zero-fills
-        prefetch_tmap(&tm_x);
+        // lane l copies 16-byte chunk l of every row into its swizzled slot; rows past the
+        // tile are zero-filled.  Each lane arrives on a_full once its copies have landed.
         uint32_t it = 0;
         const uint32_t a_base = smem_u32(sA);
+        const uint32_t dst_lane = a_base + (lane >> 3) * 16384;
         for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
             const ExpertTile t = a.tiles[tile];
-            int tok[4];
+            int tok[4];  // token of row 32j + lane
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int r = 4 * lane + i;
-                tok[i] = r < t.rows ? a.perm[t.start + r] : a.n_rows;
+            for (int j = 0; j < 4; ++j) {
+                const int r = 32 * j + lane;
+                tok[j] = r < t.rows ? a.perm[t.start + r] : -1;
             }
             if (!mbar_wait_w(&bars->a_empty, (it & 1) ^ 1, abort)) break;
-            if (lane == 0) mbar_expect_tx(&bars->a_full, kTile);
-            __syncwarp();
 #pragma unroll
-            for (int kb = 0; kb < 4; ++kb)
-                tma_gather4(a_base + kb * 16384 + lane * 512, &tm_x, &bars->a_full, kb * 64, tok[0], tok[1], tok[2],
-                            tok[3]);
+            for (int j = 0; j < 4; ++j) {
+#pragma unroll 8
+                for (int i = 0; i < 32; ++i) {
+                    const int tk = __shfl_sync(0xffffffffu, tok[j], i);
+                    const int r = 32 * j + i;
+                    cp_async16(dst_lane + sw128_off(r, lane & 7), a.x + (size_t)(tk < 0 ? 0 : tk) * kD + lane * 8,
+                               tk < 0 ? 0u : 16u);
+                }
+            }
+            cp_async_mbar_arrive(&bars->a_full);
         }
     } else if (warp == 1) {
         // ============================ MMA issuer ============================
@@ -165,6 +171,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, ++it) {
             // ---- GEMM1: acc1 = A . W1^T (E1 done with the previous tile's acc1)
             wait(&bars->a_full, it & 1);
+            fence_async_shared();  // the gathered rows (cp.async) are read by the tensor cores
             wait(&bars->acc1_empty, (it & 1) ^ 1);
             for (int kc = 0; kc < 4 && ok; ++kc) {
                 wait(&bars->full[stage], phase);
