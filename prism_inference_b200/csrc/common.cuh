@@ -70,6 +70,40 @@ PRISM_DEV float gelu_f32(float x) {
     return fmaf(hx, t, hx);
 }
 
+// ---- packed fp32 pairs (sm_100 f32x2 arithmetic: one instruction for two values, each
+// rounded exactly as the scalar instruction would) -----------------------------------------
+PRISM_DEV uint64_t f2_pack(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+PRISM_DEV void f2_unpack(uint64_t v, float& lo, float& hi) { asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v)); }
+PRISM_DEV uint64_t f2_add(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+PRISM_DEV uint64_t f2_mul(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+PRISM_DEV uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+// gelu_f32 of two values (the same operations in the same order, so the same results)
+PRISM_DEV uint64_t gelu_f32x2(uint64_t x) {
+    const uint64_t x2 = f2_mul(x, x);
+    const uint64_t inner = f2_mul(x, f2_fma(f2_pack(0.035677408f, 0.035677408f), x2, f2_pack(0.7978846f, 0.7978846f)));
+    float i0, i1;
+    f2_unpack(inner, i0, i1);
+    const uint64_t t = f2_pack(tanh_approx(i0), tanh_approx(i1));
+    const uint64_t hx = f2_mul(f2_pack(0.5f, 0.5f), x);
+    return f2_fma(hx, t, hx);
+}
+
 // ---- mbarrier -------------------------------------------------------------------
 PRISM_DEV void mbar_init(uint64_t* bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));

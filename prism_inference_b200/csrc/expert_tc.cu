@@ -240,10 +240,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                     // columns 32g + 2j, +1 of the part live in lane 8g + j/2
                     const float bx = __shfl_sync(0xffffffffu, (j & 1) ? bias.z : bias.x, g * 8 + (j >> 1));
                     const float by = __shfl_sync(0xffffffffu, (j & 1) ? bias.w : bias.y, g * 8 + (j >> 1));
-                    // t = h(acc + b1): one rounding per coopVecMatMulAddNV result
-                    const uint32_t t = pack_h2(__fadd_rn(__uint_as_float(r[2 * j]), bx),
-                                               __fadd_rn(__uint_as_float(r[2 * j + 1]), by));
-                    packed[j] = pack_h2(gelu_f32(lo_h2f(t)), gelu_f32(hi_h2f(t)));
+                    // t = h(acc + b1): one rounding per coopVecMatMulAddNV result; both columns
+                    // of the pair in one f32x2 instruction per step
+                    float s0, s1;
+                    f2_unpack(f2_add(f2_pack(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1])), f2_pack(bx, by)),
+                              s0, s1);
+                    const uint32_t t = pack_h2(s0, s1);
+                    float g0, g1;
+                    f2_unpack(gelu_f32x2(f2_pack(lo_h2f(t), hi_h2f(t))), g0, g1);
+                    packed[j] = pack_h2(g0, g1);
                 }
                 // H columns 32g .. 32g+31 of the part -> TMEM [128 part + 16g, +16), over
                 // fp32 columns this thread has already read
