@@ -194,6 +194,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = bars->tmem_base;
+    grid_dep_wait();  // x and the routing counters come from the previous kernels
 
     if (warp == 0) {
         // ============================ TMA producer ============================
@@ -676,8 +677,7 @@ cudaError_t launch_attn_tc(const AttnTcArgs& a, const CUtensorMap& x, const CUte
                            const CUtensorMap& wo, const CUtensorMap& wr, int grid, cudaStream_t s) {
     cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
     if (e != cudaSuccess) return e;
-    attn_tc_kernel<<<grid, kThreads, kSmem, s>>>(a, x, y, wqkv, wo, wr);
-    return cudaGetLastError();
+    return launch_pdl(attn_tc_kernel, dim3(grid), dim3(kThreads), kSmem, s, a, x, y, wqkv, wo, wr);
 }
 
 }  // namespace prism

@@ -7,6 +7,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "../../include/prism_moe.h"
 
 #define PRISM_DEV __device__ __forceinline__
@@ -164,6 +166,29 @@ PRISM_DEV void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
 // cp.async groups of this thread: close the current group / wait until all have landed
 PRISM_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 PRISM_DEV void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+// ---- programmatic dependent launch ------------------------------------------------------
+// The stack's kernels are launched so that each may start (and run its prologue: barrier
+// init, TMEM allocation, tensor-map prefetch, weight staging) while the previous kernel of
+// the stream finishes; every one of them executes grid_dep_wait() before touching anything
+// the previous kernels wrote, which returns once those kernels have completed and their
+// memory is visible.
+PRISM_DEV void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // generic-proxy shared-memory writes -> visible to the async proxy (TMA, tcgen05)
 PRISM_DEV void fence_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }

@@ -80,7 +80,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     volatile int* abort = &bars->abort;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n_tiles = *a.n_tiles;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -104,6 +103,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = bars->tmem_base;
+    grid_dep_wait();  // tile list, permutation and rows come from the previous kernels
+    const int n_tiles = *a.n_tiles;
 
     if (warp == 0) {
         // ============================ producer ============================
@@ -360,8 +361,7 @@ cudaError_t launch_ffn_expert256(const FfnArgs& a, const CUtensorMap& x_rows, co
     cudaError_t e = cudaFuncSetAttribute(expert_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
     if (e != cudaSuccess) return e;
     if (grid <= 0) return cudaSuccess;
-    expert_tc_kernel<<<grid, kThreads, kSmem, s>>>(a, x_rows, w1, w2);
-    return cudaGetLastError();
+    return launch_pdl(expert_tc_kernel, dim3(grid), dim3(kThreads), kSmem, s, a, x_rows, w1, w2);
 }
 
 }  // namespace prism

@@ -21,6 +21,7 @@ namespace prism {
 
 __global__ void __launch_bounds__(256) route_plan_kernel(RoutePlanArgs a) {
     __shared__ int s_off[256], s_toff[256];
+    grid_dep_wait();  // the counts come from the attention kernel
     const int e = threadIdx.x;
     const int n = a.n_experts;
     const int c = e < n ? a.counts[e] : 0;
@@ -77,6 +78,7 @@ __global__ void __launch_bounds__(256) route_scatter_kernel(RouteScatterArgs a) 
     constexpr int kPer = kScatterChunk / 256;
     const int t0 = blockIdx.x * kScatterChunk;
     s_cnt[threadIdx.x] = 0;
+    grid_dep_wait();  // assignments (attention) and segment offsets (route_plan)
     __syncthreads();
     int ex[kPer], rk[kPer];
 #pragma unroll
@@ -100,11 +102,12 @@ __global__ void __launch_bounds__(256) route_scatter_kernel(RouteScatterArgs a) 
 }
 
 cudaError_t launch_route(const RoutePlanArgs& p, const RouteScatterArgs& s, cudaStream_t st) {
-    route_plan_kernel<<<1, 256, 0, st>>>(p);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_pdl(route_plan_kernel, dim3(1), dim3(256), 0, st, p);
     if (e != cudaSuccess) return e;
-    if (s.n_tokens > 0) route_scatter_kernel<<<(s.n_tokens + kScatterChunk - 1) / kScatterChunk, 256, 0, st>>>(s);
-    return cudaGetLastError();
+    if (s.n_tokens > 0)
+        e = launch_pdl(route_scatter_kernel, dim3((s.n_tokens + kScatterChunk - 1) / kScatterChunk), dim3(256), 0, st,
+                       s);
+    return e;
 }
 
 }  // namespace prism

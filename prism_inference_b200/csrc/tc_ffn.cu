@@ -106,6 +106,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = bars->tmem_base;
+    grid_dep_wait();  // the input rows come from the previous kernel
 
     if (warp == 0) {
         // ===================== producer =====================
@@ -421,8 +422,7 @@ cudaError_t launch_ffn(const FfnArgs& a, const CUtensorMap& tx, const CUtensorMa
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
     if (e != cudaSuccess) return e;
     if (grid <= 0) return cudaSuccess;
-    k<<<grid, kThreads, Cfg::kSmem, s>>>(a, tx, t1, t2, n_chunks);
-    return cudaGetLastError();
+    return launch_pdl(k, dim3(grid), dim3(kThreads), Cfg::kSmem, s, a, tx, t1, t2, n_chunks);
 }
 
 }  // namespace
