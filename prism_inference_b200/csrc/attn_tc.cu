@@ -100,10 +100,10 @@ PRISM_DEV void y_chunk(unsigned char* sX, const uint32_t (&v)[32], int r, const 
         const float* fv = reinterpret_cast<const float*>(&v[8 * c]);
         // y = h( h(PO + bo) + x ): the second rounding is the fp16 add of :76
         uint4 y;
-        y.x = hadd2_u32(pack_h2(__fadd_rn(fv[0], b0.x), __fadd_rn(fv[1], b0.y)), x.x);
-        y.y = hadd2_u32(pack_h2(__fadd_rn(fv[2], b0.z), __fadd_rn(fv[3], b0.w)), x.y);
-        y.z = hadd2_u32(pack_h2(__fadd_rn(fv[4], b1.x), __fadd_rn(fv[5], b1.y)), x.z);
-        y.w = hadd2_u32(pack_h2(__fadd_rn(fv[6], b1.z), __fadd_rn(fv[7], b1.w)), x.w);
+        y.x = hadd2_u32(add_pack_h2(fv[0], fv[1], b0.x, b0.y), x.x);
+        y.y = hadd2_u32(add_pack_h2(fv[2], fv[3], b0.z, b0.w), x.y);
+        y.z = hadd2_u32(add_pack_h2(fv[4], fv[5], b1.x, b1.y), x.z);
+        y.w = hadd2_u32(add_pack_h2(fv[6], fv[7], b1.z, b1.w), x.w);
         *reinterpret_cast<uint4*>(xblk + off) = y;
     }
 }
@@ -460,20 +460,24 @@ __global__ void __launch_bounds__(kThreads, 1)
                         m3 = fmaxf(m3, __uint_as_float(sv[j + 3]));
                     }
                     const float mc = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3)) * c2;
-                    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+                    // the per-key fma(s, scale log2 e, -max) and the four running sums as
+                    // f32x2 pairs (the same operations per element)
+                    const uint64_t c22 = f2_pack(c2, c2), nmc = f2_pack(-mc, -mc);
+                    uint64_t s01 = f2_pack(0.f, 0.f), s23 = f2_pack(0.f, 0.f);
 #pragma unroll
                     for (int j = 0; j < 64; j += 4) {
-                        const float p0 = ex2_approx(fmaf(__uint_as_float(sv[j]), c2, -mc));
-                        const float p1 = ex2_approx(fmaf(__uint_as_float(sv[j + 1]), c2, -mc));
-                        const float p2 = ex2_approx(fmaf(__uint_as_float(sv[j + 2]), c2, -mc));
-                        const float p3 = ex2_approx(fmaf(__uint_as_float(sv[j + 3]), c2, -mc));
-                        s0 += p0;
-                        s1 += p1;
-                        s2 += p2;
-                        s3 += p3;
+                        float a0, a1, a2, a3;
+                        f2_unpack(f2_fma(f2_pack(__uint_as_float(sv[j]), __uint_as_float(sv[j + 1])), c22, nmc), a0, a1);
+                        f2_unpack(f2_fma(f2_pack(__uint_as_float(sv[j + 2]), __uint_as_float(sv[j + 3])), c22, nmc), a2, a3);
+                        const float p0 = ex2_approx(a0), p1 = ex2_approx(a1), p2 = ex2_approx(a2), p3 = ex2_approx(a3);
+                        s01 = f2_add(s01, f2_pack(p0, p1));
+                        s23 = f2_add(s23, f2_pack(p2, p3));
                         pk[j >> 1] = pack_h2(p0, p1);
                         pk[(j >> 1) + 1] = pack_h2(p2, p3);
                     }
+                    float s0, s1, s2, s3;
+                    f2_unpack(s01, s0, s1);
+                    f2_unpack(s23, s2, s3);
                     se = (s0 + s1) + (s2 + s3);
                 } else {
                     // frames of fewer than 64 tokens: keys are the first n_keys slots (:33)
@@ -516,8 +520,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tmem_ld_wait();
                     uint32_t po[16];
 #pragma unroll
-                    for (int j = 0; j < 16; ++j)
-                        po[j] = pack_h2(__fmul_rn(__uint_as_float(v[2 * j]), inv), __fmul_rn(__uint_as_float(v[2 * j + 1]), inv));
+                    for (int j = 0; j < 16; ++j) {  // O / sum, as f32x2 pairs
+                        float o0, o1;
+                        f2_unpack(f2_mul(f2_pack(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1])), f2_pack(inv, inv)),
+                                  o0, o1);
+                        po[j] = pack_h2(o0, o1);
+                    }
 #pragma unroll
                     for (int c = 0; c < 4; ++c)
                         *reinterpret_cast<uint4*>(sAO + sw128_off(r, (h & 1) * 4 + c)) =
@@ -574,10 +582,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 uint32_t pk[16];
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
-                    pk[2 * i] = pack_h2(__fadd_rn(__uint_as_float(v[4 * i]), bb[i].x),
-                                        __fadd_rn(__uint_as_float(v[4 * i + 1]), bb[i].y));
-                    pk[2 * i + 1] = pack_h2(__fadd_rn(__uint_as_float(v[4 * i + 2]), bb[i].z),
-                                            __fadd_rn(__uint_as_float(v[4 * i + 3]), bb[i].w));
+                    pk[2 * i] = add_pack_h2(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]), bb[i].x, bb[i].y);
+                    pk[2 * i + 1] = add_pack_h2(__uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]), bb[i].z, bb[i].w);
                 }
                 // Q, K and V rows alike: row r, 32 fp16 = four 16-byte chunks, SW64 (V is the
                 // MN-major B operand of PV, which has exactly this layout)

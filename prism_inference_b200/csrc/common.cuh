@@ -95,6 +95,12 @@ PRISM_DEV uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
     asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
     return r;
 }
+// h(a0 + b0), h(a1 + b1) packed as f16x2 (lo = pair 0), the adds as one f32x2 instruction
+PRISM_DEV uint32_t add_pack_h2(float a0, float a1, float b0, float b1) {
+    float s0, s1;
+    f2_unpack(f2_add(f2_pack(a0, a1), f2_pack(b0, b1)), s0, s1);
+    return pack_h2(s0, s1);
+}
 // gelu_f32 of two values (the same operations in the same order, so the same results)
 PRISM_DEV uint64_t gelu_f32x2(uint64_t x) {
     const uint64_t x2 = f2_mul(x, x);
