@@ -21,11 +21,12 @@
 // buffers and every hand-off is an mbarrier.  The MMA warp issues GEMM2(i) before
 // GEMM1(i+1), so GEMM2 has read H (in acc1) before GEMM1(i+1) overwrites it.
 //
-// Warp roles (608 threads):
+// Warp roles (640 threads):
 //   warp 0      producer: W1_e / W2_e K-chunks (TMA, 128B swizzle) through a 3-stage ring
 //   warp 1      TMEM owner + tcgen05.mma issuer (converged warp, elected lane)
-//   warp 2      row gather: cp.async, one 512-byte token row per warp instruction (the
-//               TMA engine is left to the weight ring)
+//   warps 2, 19 row gather: cp.async, one 512-byte token row per warp instruction, 64 rows
+//               each (two warps keep twice the row loads in flight; the TMA engine is left
+//               to the weight ring)
 //   warps 3-10  E1: warp w reads TMEM lanes 32*(w%4).. and column part (w-3)/4
 //   warps 11-18 E2: likewise with part (w-11)/4
 // Every wait is bounded (common.cuh); on timeout the CTA sets the error word and winds
@@ -38,7 +39,8 @@ namespace {
 
 constexpr int kD = 256;                   // model / hidden width
 constexpr int kE1Base = 3, kE2Base = 11;  // first warp of each epilogue group
-constexpr int kThreads = 32 * 19;
+constexpr int kGather2 = 19;              // the second row-gather warp
+constexpr int kThreads = 32 * 20;
 constexpr int kStage = 256 * 128;         // one W K-chunk: 256 rows x 64 columns fp16
 constexpr int kStages = 3;
 constexpr int kTile = 128 * kD * 2;       // a [128][256] fp16 tile as 4 K-major SW128 K-blocks
@@ -86,7 +88,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&bars->full[s], 1);
             mbar_init(&bars->empty[s], 1);
         }
-        mbar_init(&bars->a_full, 32);     // the gather warp's lanes, once their cp.async landed
+        mbar_init(&bars->a_full, 64);     // the gather warps' lanes, once their cp.async landed
         mbar_init(&bars->a_empty, 1);     // GEMM1 has read A (commit)
         mbar_init(&bars->acc1_full, 1);
         mbar_init(&bars->acc1_empty, 8);  // E1 has read acc1 (its H stays for GEMM2, issued first)
@@ -130,24 +132,27 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int i = 0; i < 4 && ok; ++i) ok = load(&tm_w2, h_order(i) * 64, e * kD);  // W2_e
             }
         }
-    } else if (warp == 2) {
+    } else if (warp == 2 || warp == kGather2) {
         // ============================ row gather ============================
-        // lane l copies 16-byte chunk l of every row into its swizzled slot; rows past the
-        // tile are zero-filled.  Each lane arrives on a_full once its copies have landed.
+        // warp 2 takes tile rows 0-63, the second warp rows 64-127; lane l copies 16-byte
+        // chunk l of each row into its swizzled slot, rows past the tile are zero-filled.
+        // Each lane arrives on a_full once its copies have landed.
         uint32_t it = 0;
         const uint32_t a_base = smem_u32(sA);
         const uint32_t dst_lane = a_base + (lane >> 3) * 16384;
         for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
             const ExpertTile t = a.tiles[tile];
-            int tok[4];  // token of row 32j + lane
+            const int j0 = warp == 2 ? 0 : 2;  // this warp's row blocks: j0, j0 + 1 (32 rows each)
+            int tok[4];                        // token of row 32j + lane (own blocks only)
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 const int r = 32 * j + lane;
-                tok[j] = r < t.rows ? a.perm[t.start + r] : -1;
+                tok[j] = (j >> 1) == (j0 >> 1) && r < t.rows ? a.perm[t.start + r] : -1;
             }
             if (!mbar_wait_w(&bars->a_empty, (it & 1) ^ 1, abort)) break;
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
+                if ((j >> 1) != (j0 >> 1)) continue;
 #pragma unroll 8
                 for (int i = 0; i < 32; ++i) {
                     const int tk = __shfl_sync(0xffffffffu, tok[j], i);
