@@ -32,8 +32,8 @@ struct FfnArgs {
     uint32_t* err;             // device error word
 };
 
-// x_rows: 2-D [n_rows][256] map of a.x with box {64, 1} (one row) for the tile::gather4 row gather;
-// a.n_rows = its row count.
+// Grouped expert FFN (expert_tc.cu): w1, w2 = 2-D [E*256][256] maps with box {64, 256}; the token
+// rows are gathered from a.x with cp.async (x_rows, a map of a.x, is not read); a.n_rows = rows of a.x.
 cudaError_t launch_ffn_expert256(const FfnArgs& a, const CUtensorMap& x_rows, const CUtensorMap& w1,
                                  const CUtensorMap& w2, int grid, cudaStream_t s);
 cudaError_t launch_ffn_dense256(const FfnArgs& a, const CUtensorMap& x, const CUtensorMap& w1, const CUtensorMap& w2,
