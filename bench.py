@@ -261,7 +261,19 @@ def run_ours(args):
     if ws > 1:
         torch.cuda.set_device(local)
         from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+        # NCCL may print a version banner on stdout while the communicator comes up; send it to
+        # stderr so that stdout carries only the JSON line
+        sys.stdout.flush()
+        saved = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+            dist.barrier()
+            torch.cuda.synchronize()
+        finally:
+            sys.stdout.flush()
+            os.dup2(saved, 1)
+            os.close(saved)
     dev = torch.cuda.current_device()
     cfg = configs.get(args.config)
     L = cfg.layout
