@@ -107,6 +107,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem = bars->tmem_base;
     grid_dep_wait();  // tile list, permutation and rows come from the previous kernels
     const int n_tiles = *a.n_tiles;
+    // the routing kernel is done with the counts and cursors: clear them for the next block's
+    // router (which starts only after this kernel completes)
+    if (blockIdx.x == 0 && a.route_counts)
+        for (int i = threadIdx.x; i < a.n_route; i += blockDim.x) {
+            a.route_counts[i] = 0;
+            a.route_cursor[i] = 0;
+        }
 
     if (warp == 0) {
         // ============================ producer ============================

@@ -376,7 +376,7 @@ struct prism_stack {
     CUtensorMap tm_act_y_rows;  // act_y with a one-row box: the expert kernel's tile::gather4 row gather
     std::vector<FastBlock> blocks;
     __half *act_a = nullptr, *act_b = nullptr, *act_y = nullptr;
-    int32_t *assign_ws = nullptr, *counts = nullptr, *offsets = nullptr, *cursor = nullptr, *perm = nullptr,
+    int32_t *assign_ws = nullptr, *counts = nullptr, *cursor = nullptr, *perm = nullptr,
             *n_tiles = nullptr;
     ExpertTile* tiles = nullptr;
     uint32_t* err = nullptr;
@@ -636,12 +636,13 @@ extern "C" int prism_stack_create(prism_ctx* ctx, const prism_stack_desc* desc, 
     // workspace
     if ((rc = dev_alloc(st, &st->act_a, rows * D)) || (rc = dev_alloc(st, &st->act_b, rows * D)) ||
         (rc = dev_alloc(st, &st->act_y, rows * D)) || (rc = dev_alloc(st, &st->assign_ws, rows)) ||
-        (rc = dev_alloc(st, &st->counts, 256)) || (rc = dev_alloc(st, &st->offsets, 256)) ||
+        (rc = dev_alloc(st, &st->counts, 256)) ||
         (rc = dev_alloc(st, &st->cursor, 256)) || (rc = dev_alloc(st, &st->perm, rows)) ||
         (rc = dev_alloc(st, &st->n_tiles, 1)) || (rc = dev_alloc(st, &st->tiles, rows / 128 + 256 + 1)) ||
         (rc = dev_alloc(st, &st->err, 1)))
         return fail_cleanup(rc);
-    if (cudaMemset(st->counts, 0, 256 * 4) != cudaSuccess || cudaMemset(st->err, 0, 4) != cudaSuccess)
+    if (cudaMemset(st->counts, 0, 256 * 4) != cudaSuccess || cudaMemset(st->cursor, 0, 256 * 4) != cudaSuccess ||
+        cudaMemset(st->err, 0, 4) != cudaSuccess)
         return fail_cleanup(fail(PRISM_E_CUDA, "workspace memset failed"));
     if (st->tc) {
         if ((rc = make_map_2d(&st->tm_act_a, st->act_a, rows, D, 128)) ||
@@ -669,7 +670,8 @@ extern "C" int prism_stack_tokens_per_frame(const prism_stack* st) { return st ?
 extern "C" int prism_stack_launch_count(const prism_stack* st, int frames) {
     if (!st || frames <= 0) return 0;
     int n = (st->desc.up_w >= 0 ? 1 : 0) + (st->desc.down_w >= 0 ? 1 : 0);
-    for (const auto& b : st->blocks) n += b.d.kind == PRISM_BLOCK_MOE ? 4 : 2;
+    // MoE: attention (+ router on the CUDA-core path), routing, experts; dense: attention, FFN
+    for (const auto& b : st->blocks) n += b.d.kind == PRISM_BLOCK_MOE ? (st->tc ? 3 : 4) : 2;
     if (st->desc.down_w < 0 && st->blocks.empty()) n += 1;  // plain copy
     return n;
 }
@@ -762,27 +764,20 @@ extern "C" int prism_stack_forward(prism_stack* st, const void* in, void* out, i
                 CUDA_TRY(launch_attn_tc(ta, tm_x, tm_y, b.tm_wqkv, b.tm_wo, b.tm_wr, std::min(grid, (n_win + 1) / 2), s));
             }
             if (b.d.kind == PRISM_BLOCK_MOE) {
-                RoutePlanArgs rp;
-                rp.counts = st->counts;
-                rp.counts_out = nullptr;
-                rp.offsets = st->offsets;
-                rp.cursor = st->cursor;
-                rp.tiles = st->tiles;
-                rp.n_tiles = st->n_tiles;
-                rp.n_experts = b.d.n_experts;
-                rp.n_tokens = rows;
-                rp.err = st->err;
-                RouteScatterArgs rs;
-                rs.assign = asg;
-                rs.offsets = st->offsets;
-                rs.cursor = st->cursor;
-                rs.perm = st->perm;
-                rs.n_experts = b.d.n_experts;
-                rs.n_tokens = rows;
-                rs.err = st->err;
+                RouteArgs ra_;
+                ra_.counts = st->counts;
+                ra_.counts_out = nullptr;
+                ra_.cursor = st->cursor;
+                ra_.assign = asg;
+                ra_.perm = st->perm;
+                ra_.tiles = st->tiles;
+                ra_.n_tiles = st->n_tiles;
+                ra_.n_experts = b.d.n_experts;
+                ra_.n_tokens = rows;
+                ra_.err = st->err;
                 {
                     KernelTimer kt(st, s, PRISM_K_ROUTE);
-                    CUDA_TRY(launch_route(rp, rs, s));
+                    CUDA_TRY(launch_route(ra_, s));
                 }
                 FfnArgs fa{};
                 fa.x = st->act_y;
@@ -793,6 +788,9 @@ extern "C" int prism_stack_forward(prism_stack* st, const void* in, void* out, i
                 fa.b1 = b.b1;
                 fa.b2 = b.b2;
                 fa.err = st->err;
+                fa.route_counts = st->counts;
+                fa.route_cursor = st->cursor;
+                fa.n_route = b.d.n_experts;
                 KernelTimer kt(st, s, PRISM_K_EXPERT);
                 fa.n_rows = (int)rows;
                 CUDA_TRY(launch_ffn_expert256(fa, st->tm_act_y_rows, b.tm_w1, b.tm_w2,
@@ -847,27 +845,20 @@ extern "C" int prism_stack_forward(prism_stack* st, const void* in, void* out, i
                 KernelTimer kt(st, s, PRISM_K_ROUTER);
                 CUDA_TRY(launch_router(ra, D, s));
             }
-            RoutePlanArgs rp;
-            rp.counts = st->counts;
-            rp.counts_out = nullptr;
-            rp.offsets = st->offsets;
-            rp.cursor = st->cursor;
-            rp.tiles = st->tiles;
-            rp.n_tiles = st->n_tiles;
-            rp.n_experts = b.d.n_experts;
-            rp.n_tokens = rows;
-            rp.err = st->err;
-            RouteScatterArgs rs;
-            rs.assign = asg;
-            rs.offsets = st->offsets;
-            rs.cursor = st->cursor;
-            rs.perm = st->perm;
-            rs.n_experts = b.d.n_experts;
-            rs.n_tokens = rows;
-            rs.err = st->err;
+            RouteArgs ra_;
+            ra_.counts = st->counts;
+            ra_.counts_out = nullptr;
+            ra_.cursor = st->cursor;
+            ra_.assign = asg;
+            ra_.perm = st->perm;
+            ra_.tiles = st->tiles;
+            ra_.n_tiles = st->n_tiles;
+            ra_.n_experts = b.d.n_experts;
+            ra_.n_tokens = rows;
+            ra_.err = st->err;
             {
                 KernelTimer kt(st, s, PRISM_K_ROUTE);
-                CUDA_TRY(launch_route(rp, rs, s));
+                CUDA_TRY(launch_route(ra_, s));
             }
             FfnArgs fa{};
             fa.x = st->act_y;
@@ -878,6 +869,9 @@ extern "C" int prism_stack_forward(prism_stack* st, const void* in, void* out, i
             fa.b1 = b.b1;
             fa.b2 = b.b2;
             fa.err = st->err;
+            fa.route_counts = st->counts;
+            fa.route_cursor = st->cursor;
+            fa.n_route = b.d.n_experts;
             KernelTimer kt(st, s, PRISM_K_EXPERT);
             fa.n_rows = (int)rows;
             CUDA_TRY(launch_ffn_expert256(fa, st->tm_act_y_rows, b.tm_w1, b.tm_w2,

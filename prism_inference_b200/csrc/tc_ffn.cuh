@@ -30,6 +30,9 @@ struct FfnArgs {
     const float* b1;           // fp32 biases [experts][HID*NCH]
     const float* b2;           // fp32 biases [experts][NOUT]
     uint32_t* err;             // device error word
+    int32_t* route_counts;     // FFN_EXPERT: the router's counts and the scatter cursors, cleared by
+    int32_t* route_cursor;     //   the expert kernel for the next MoE block (nullable)
+    int n_route;               // FFN_EXPERT: entries of route_counts / route_cursor
 };
 
 // Grouped expert FFN (expert_tc.cu): w1, w2 = 2-D [E*256][256] maps with box {64, 256}; the token
