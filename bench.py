@@ -14,8 +14,9 @@ neither).  The activations (267 MB per buffer) are larger than the 126 MB L2.
 
 value: tokens/s over all ranks, inputs resident in HBM, device time (CUDA events,
 max over ranks).  e2e: the same metric through the same public call with pinned host
-buffers, the host->device copy of the frames and the device->host copy of the output
-inside the timed region.  roofline: the kernel kind with the largest share of the
+buffers, the host->device copy of every step's frames and the device->host copy of every
+step's output inside the timed region, overlapped across neighbouring steps as a serving
+loop would (copy-in and copy-out streams, double-buffered device buffers).  roofline: the kernel kind with the largest share of the
 timed region, its algorithmic FLOPs per launch / its mean event-timed duration,
 against the sustained cuBLAS bf16 figure of MEASURED_PEAKS.json.
 
@@ -327,25 +328,58 @@ def run_ours(args):
     st.status()
     launches = st.launch_count(B) * args.steps
 
-    # ---- end to end: pinned host frames in, host output back, every step
+    # ---- end to end: pinned host frames in, host output back, every step.  As a serving loop
+    # would, the copies of neighbouring steps overlap the compute: step i's frames go in on a
+    # copy stream while step i-1 computes and step i-2's output comes back on another, with
+    # double-buffered device input/output and events guarding each buffer's reuse.
+    ref_out = out.clone()  # the device-resident result of the same frames
     xh = torch.from_numpy(x_host.view(np.int16)).view(torch.float16).pin_memory()
-    oh = torch.empty((B, T, L.out_dim), dtype=torch.float16).pin_memory()
-    xd = torch.empty_like(x)
-    for _ in range(2):
-        xd.copy_(xh, non_blocking=True)
-        st.forward(xd, out)
-        oh.copy_(out, non_blocking=True)
+    oh = [torch.empty((B, T, L.out_dim), dtype=torch.float16).pin_memory() for _ in range(2)]
+    xd = [torch.empty_like(x) for _ in range(2)]
+    od = [out, torch.empty_like(out)]
+    s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+    ev = lambda: torch.cuda.Event()
+    in_ready, in_free, out_ready, out_free = ([ev(), ev()] for _ in range(4))
+
+    def e2e_steps(n, start_ev=None):
+        if start_ev is not None:
+            s_in.wait_event(start_ev)
+            s_out.wait_event(start_ev)
+        for i in range(n):
+            b = i & 1
+            with torch.cuda.stream(s_in):
+                if i >= 2:
+                    s_in.wait_event(in_free[b])  # step i-2 has read xd[b]
+                xd[b].copy_(xh, non_blocking=True)
+                in_ready[b].record(s_in)
+            stream.wait_event(in_ready[b])
+            if i >= 2:
+                stream.wait_event(out_free[b])  # step i-2's output has left od[b]
+            st.forward(xd[b], od[b])
+            in_free[b].record(stream)
+            out_ready[b].record(stream)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(out_ready[b])
+                oh[b].copy_(od[b], non_blocking=True)
+                out_free[b].record(s_out)
+        stream.wait_event(out_free[(n - 1) & 1])  # the last output is on the host
+        if n >= 2:
+            stream.wait_event(out_free[(n - 2) & 1])
+
+    e2e_steps(2)
     torch.cuda.synchronize()
     barrier()
     e0.record(stream)
-    for _ in range(args.steps):
-        xd.copy_(xh, non_blocking=True)
-        st.forward(xd, out)
-        oh.copy_(out, non_blocking=True)
+    e2e_steps(args.steps, e0)
     e1.record(stream)
     torch.cuda.synchronize()
     barrier()
     ms_e2e = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    last = oh[(args.steps - 1) & 1]
+    if not torch.equal(last.view(torch.int16), ref_out.cpu().view(torch.int16)):
+        raise SystemExit("bench: the end-to-end output differs from the device-resident output")
+    del ref_out
+    oh = last
 
     # ---- batch-1 latency (one frame through the whole stack)
     x1, o1 = x[:1], out[:1]
@@ -434,7 +468,9 @@ def run_ours(args):
                            "tflops_effective": flops_step / (ms / 1e3) / 1e12,
                            "kernel_ms_per_step": kernel_ms},
                 "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": int(xh.numel() * 2),
-                        "d2h_bytes_per_step": int(oh.numel() * 2), "ms_per_step": ms_e2e},
+                        "d2h_bytes_per_step": int(oh.numel() * 2), "ms_per_step": ms_e2e,
+                        "overlap": "copy-in, compute and copy-out of neighbouring steps on three streams, "
+                                   "double-buffered device input/output"},
                 "gpu_launches": launches, "roofline": roof, "cpu_baseline": cpu, "clocks": clk}
         print(json.dumps(line))
     st.close()
