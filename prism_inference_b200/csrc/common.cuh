@@ -180,6 +180,9 @@ PRISM_DEV void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "
 // the previous kernels wrote, which returns once those kernels have completed and their
 // memory is visible.
 PRISM_DEV void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// This CTA no longer needs to delay the next kernel's launch (its remaining work is an epilogue);
+// the next kernel still waits for this one to complete before reading its results.
+PRISM_DEV void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
                               Args&&... args) {

@@ -31,6 +31,7 @@ __global__ void __launch_bounds__(256) route_kernel(RouteArgs a) {
     const int n = a.n_experts;
     s_cnt[e] = 0;
     grid_dep_wait();  // counts and assignments come from the router
+    grid_dep_launch();  // short kernel: the expert kernel may launch (it waits for this one)
     // inclusive Hillis-Steele scans of the counts and of the tile counts
     const int c = e < n ? a.counts[e] : 0;
     s_off[e] = c;

@@ -214,6 +214,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
         // every issued MMA has completed before TMEM is released
+        grid_dep_launch();  // every MMA of this CTA is issued
         mma_commit_w(&bars->drain);
         mbar_wait_w(&bars->drain, 0, abort);
     } else if (warp >= 2 && warp < 2 + kEpiWarps) {
