@@ -113,6 +113,43 @@ def test_frames_are_independent_and_deterministic(prism_ctx):
     assert (a4[:, 2 * T:3 * T] == a1).all()
 
 
+def test_stack_graph_replay_matches_eager(prism_ctx):
+    """prism_stack_forward captured in a CUDA graph (its kernels chained by programmatic
+    dependent launch) gives the eager call's bits on every replay, also for routing."""
+    import torch
+    cfg = configs.get("moe64x16", n_blocks=3)
+    L = cfg.layout
+    blob = synth.make_blob(L)
+    x = synth.make_frames(L, 2)
+    st = Stack(prism_ctx, L, blob, 2)
+    xd = torch.from_numpy(x.view(np.int16)).cuda().view(torch.float16)
+    eager = torch.empty((2, L.tokens, L.out_dim), dtype=torch.float16, device="cuda")
+    asg_e = torch.empty((L.n_moe_blocks, 2 * L.tokens), dtype=torch.int32, device="cuda")
+    st.forward(xd, eager, asg_e)
+    torch.cuda.synchronize()
+    out = torch.empty_like(eager)
+    asg = torch.empty_like(asg_e)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):  # warm the capture stream, as torch recommends
+        st.forward(xd, out, asg)
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        st.forward(xd, out, asg)
+    for _ in range(2):
+        out.zero_()
+        asg.fill_(-1)
+        g.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out.view(torch.int16), eager.view(torch.int16))
+        assert torch.equal(asg, asg_e)
+    st.status()
+    del g
+    st.close()
+
+
 def test_routing_histogram_and_skew(prism_ctx):
     cfg = configs.get("moe32x22skew", n_blocks=2)
     blob = synth.make_blob(cfg.layout, router_skew=cfg.router_skew, skew_bias=cfg.skew_bias)
