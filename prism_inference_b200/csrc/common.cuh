@@ -217,16 +217,6 @@ PRISM_DEV void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint64_t* bar, 
         "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
         : "memory");
 }
-// Four rows r0..r3 (any order, out-of-range rows zero-filled) of a 2-D map whose box is
-// {64, 1}: 4 x 128 B land at dst, dst + 128, ... with the map's swizzle.  Not multicast.
-PRISM_DEV void tma_gather4(uint32_t dst, const CUtensorMap* map, uint64_t* bar, int c0, int r0, int r1, int r2,
-                           int r3) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(dst),
-        "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(r0), "r"(r1), "r"(r2), "r"(r3)
-        : "memory");
-}
 PRISM_DEV void tma_load_4d(uint32_t dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2,
                            int c3) {
     asm volatile(
@@ -243,7 +233,6 @@ PRISM_DEV void tma_store_4d(const CUtensorMap* map, uint32_t src, int c0, int c1
                  : "memory");
 }
 PRISM_DEV void tma_store_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-PRISM_DEV void tma_store_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 // until at most N of this thread's committed bulk store groups still read shared memory
 template <int N>
 PRISM_DEV void tma_store_wait_read() {

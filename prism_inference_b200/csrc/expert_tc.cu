@@ -71,8 +71,8 @@ PRISM_DEV unsigned char* oslot(unsigned char* sO, int R, int col) {
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
-    expert_tc_kernel(const FfnArgs a, const __grid_constant__ CUtensorMap tm_x,
-                     const __grid_constant__ CUtensorMap tm_w1, const __grid_constant__ CUtensorMap tm_w2) {
+    expert_tc_kernel(const FfnArgs a, const __grid_constant__ CUtensorMap tm_w1,
+                     const __grid_constant__ CUtensorMap tm_w2) {
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     unsigned char* sA = smem + kOffA;
@@ -368,12 +368,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 }  // namespace
 
-cudaError_t launch_ffn_expert256(const FfnArgs& a, const CUtensorMap& x_rows, const CUtensorMap& w1,
-                                 const CUtensorMap& w2, int grid, cudaStream_t s) {
+cudaError_t launch_ffn_expert256(const FfnArgs& a, const CUtensorMap& w1, const CUtensorMap& w2, int grid,
+                                 cudaStream_t s) {
     cudaError_t e = cudaFuncSetAttribute(expert_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
     if (e != cudaSuccess) return e;
     if (grid <= 0) return cudaSuccess;
-    return launch_pdl(expert_tc_kernel, dim3(grid), dim3(kThreads), kSmem, s, a, x_rows, w1, w2);
+    return launch_pdl(expert_tc_kernel, dim3(grid), dim3(kThreads), kSmem, s, a, w1, w2);
 }
 
 }  // namespace prism

@@ -373,7 +373,6 @@ struct prism_stack {
     __half *up_w = nullptr, *dn_w = nullptr;
     float *up_b = nullptr, *dn_b = nullptr;
     CUtensorMap tm_up, tm_dn, tm_act_a, tm_act_b, tm_act_y;
-    CUtensorMap tm_act_y_rows;  // act_y with a one-row box: the expert kernel's tile::gather4 row gather
     std::vector<FastBlock> blocks;
     __half *act_a = nullptr, *act_b = nullptr, *act_y = nullptr;
     int32_t *assign_ws = nullptr, *counts = nullptr, *cursor = nullptr, *perm = nullptr,
@@ -647,8 +646,7 @@ extern "C" int prism_stack_create(prism_ctx* ctx, const prism_stack_desc* desc, 
     if (st->tc) {
         if ((rc = make_map_2d(&st->tm_act_a, st->act_a, rows, D, 128)) ||
             (rc = make_map_2d(&st->tm_act_b, st->act_b, rows, D, 128)) ||
-            (rc = make_map_2d(&st->tm_act_y, st->act_y, rows, D, 128)) ||
-            (rc = make_map_2d(&st->tm_act_y_rows, st->act_y, rows, D, 1)))
+            (rc = make_map_2d(&st->tm_act_y, st->act_y, rows, D, 128)))
             return fail_cleanup(rc);
     }
     if (cudaDeviceSynchronize() != cudaSuccess) return fail_cleanup(fail(PRISM_E_CUDA, "stack upload failed"));
@@ -793,7 +791,7 @@ extern "C" int prism_stack_forward(prism_stack* st, const void* in, void* out, i
                 fa.n_route = b.d.n_experts;
                 KernelTimer kt(st, s, PRISM_K_EXPERT);
                 fa.n_rows = (int)rows;
-                CUDA_TRY(launch_ffn_expert256(fa, st->tm_act_y_rows, b.tm_w1, b.tm_w2,
+                CUDA_TRY(launch_ffn_expert256(fa, b.tm_w1, b.tm_w2,
                                               std::min(grid, rows / 128 + b.d.n_experts), s));
             } else {
                 FfnArgs fa{};
@@ -874,7 +872,7 @@ extern "C" int prism_stack_forward(prism_stack* st, const void* in, void* out, i
             fa.n_route = b.d.n_experts;
             KernelTimer kt(st, s, PRISM_K_EXPERT);
             fa.n_rows = (int)rows;
-            CUDA_TRY(launch_ffn_expert256(fa, st->tm_act_y_rows, b.tm_w1, b.tm_w2,
+            CUDA_TRY(launch_ffn_expert256(fa, b.tm_w1, b.tm_w2,
                                           std::min(grid, rows / 128 + b.d.n_experts), s));
         } else if (st->tc) {
             FfnArgs fa{};

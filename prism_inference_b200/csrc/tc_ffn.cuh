@@ -36,9 +36,9 @@ struct FfnArgs {
 };
 
 // Grouped expert FFN (expert_tc.cu): w1, w2 = 2-D [E*256][256] maps with box {64, 256}; the token
-// rows are gathered from a.x with cp.async (x_rows, a map of a.x, is not read); a.n_rows = rows of a.x.
-cudaError_t launch_ffn_expert256(const FfnArgs& a, const CUtensorMap& x_rows, const CUtensorMap& w1,
-                                 const CUtensorMap& w2, int grid, cudaStream_t s);
+// rows are gathered from a.x with cp.async; a.n_rows = rows of a.x.
+cudaError_t launch_ffn_expert256(const FfnArgs& a, const CUtensorMap& w1, const CUtensorMap& w2, int grid,
+                                 cudaStream_t s);
 cudaError_t launch_ffn_dense256(const FfnArgs& a, const CUtensorMap& x, const CUtensorMap& w1, const CUtensorMap& w2,
                                 int n_chunks, int grid, cudaStream_t s);
 cudaError_t launch_ffn_proj_up(const FfnArgs& a, const CUtensorMap& x, const CUtensorMap& w, int grid,
