@@ -164,3 +164,62 @@ def stack_from_json(js: dict, dim: int, n_heads: int, n_experts: int, n_blocks: 
         b.out_w, b.out_b = o["weight_offset_fp16"], o["bias_offset_fp16"]
         L.blocks.append(b)
     return L
+
+
+# ---- weight files ------------------------------------------------------------------------
+# Shapes of the named layers, in the reference's row-major [out][in] convention (each output
+# row contiguous, as the shaders index W[row * dim + k]): blk{i}.qkv is [3*D][D] with the q, k
+# and v matrices stacked, blk{i}.out [D][D], blk{i}.router [N][D], blk{i}.expert{e}.w1 / .w2
+# [D][D], blk{i}.ffn_w1 [H][D], blk{i}.ffn_w2 [D][H], proj_up [256][128], proj_down [128][256].
+
+
+def pack_weights(L: StackLayout, tensors) -> "np.ndarray":
+    """The flat fp16 blob of layout L from named (weight, bias) arrays.
+
+    tensors maps every layer name of L.layers to (weight, bias); each array is converted to
+    fp16 and must hold exactly weight_count / bias_count values (the shapes above, or flat).
+    Raises KeyError for a missing layer and ValueError for a size mismatch."""
+    import numpy as np
+
+    blob = np.zeros(L.total, dtype=np.float16)
+    for l in L.layers:
+        w, b = tensors[l["name"]]
+        w = np.asarray(w, dtype=np.float16).reshape(-1)
+        b = np.asarray(b, dtype=np.float16).reshape(-1)
+        if w.size != l["weight_count"] or b.size != l["bias_count"]:
+            raise ValueError(f"{l['name']}: {w.size} weights / {b.size} biases, the layout wants "
+                             f"{l['weight_count']} / {l['bias_count']}")
+        wo, bo = l["weight_offset_fp16"], l["bias_offset_fp16"]
+        blob[wo:wo + w.size] = w
+        blob[bo:bo + b.size] = b
+    return blob
+
+
+def write_weights(path: str, L: StackLayout, blob) -> str:
+    """Write blob as a raw fp16 .weights file and L's table as the .json beside it (the pair
+    export_weights.py writes); returns the .json path."""
+    import numpy as np
+
+    if not path.endswith(".weights"):
+        raise ValueError("the weight file name must end in .weights")
+    blob = np.asarray(blob, dtype=np.float16)
+    if blob.size != L.total:
+        raise ValueError(f"blob holds {blob.size} values, the layout {L.total}")
+    blob.tofile(path)
+    js = path[: -len(".weights")] + ".json"
+    with open(js, "w") as f:
+        f.write(L.to_json())
+    return js
+
+
+def read_weights(path: str):
+    """(blob, table) from a .weights / .json pair; the blob is checked against the table's
+    total_fp16_values."""
+    import numpy as np
+
+    with open(path[: -len(".weights")] + ".json") as f:
+        table = json.load(f)
+    blob = np.fromfile(path, dtype=np.float16)
+    if blob.size != table["total_fp16_values"]:
+        raise ValueError(f"{path}: {blob.size} fp16 values, the table says {table['total_fp16_values']}")
+    return blob, table

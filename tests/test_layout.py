@@ -2,6 +2,7 @@
 import json
 
 import numpy as np
+import pytest
 
 from prism_inference_b200 import configs, layout, synth
 
@@ -34,6 +35,42 @@ def test_export_weights_json_schema_roundtrip():
     for a, b in zip(L.blocks, L2.blocks):
         assert a == b
     assert (L2.up_w, L2.down_w, L2.in_dim, L2.out_dim) == (L.up_w, L.down_w, 128, 128)
+
+
+def test_pack_write_read_weights(tmp_path):
+    """Named (weight, bias) arrays -> flat blob at the layout's offsets -> .weights/.json pair
+    -> the same blob and a table that rebuilds the same layout."""
+    L = layout.build_stack(256, 2, n_experts=3, up_adapter=True, down_adapter=True)
+    rng = np.random.default_rng(7)
+    shapes = {"proj_up": (256, 128), "proj_down": (128, 256)}
+    for i in range(2):
+        shapes[f"blk{i}.qkv"] = (768, 256)
+        shapes[f"blk{i}.out"] = (256, 256)
+        shapes[f"blk{i}.router"] = (3, 256)
+        for e in range(3):
+            shapes[f"blk{i}.expert{e}.w1"] = (256, 256)
+            shapes[f"blk{i}.expert{e}.w2"] = (256, 256)
+    tensors = {n: (rng.standard_normal(s).astype(np.float32), rng.standard_normal(s[0]).astype(np.float32))
+               for n, s in shapes.items()}
+    blob = layout.pack_weights(L, tensors)
+    b = L.blocks[1]
+    w, bias = tensors["blk1.qkv"]
+    assert np.array_equal(blob[b.qkv_w:b.qkv_w + w.size], w.astype(np.float16).reshape(-1))
+    assert np.array_equal(blob[b.qkv_b:b.qkv_b + 768], bias.astype(np.float16))
+    e2 = b.expert_w1 + 2 * b.expert_stride  # expert 2 of block 1 through the stride
+    assert np.array_equal(blob[e2:e2 + 65536], tensors["blk1.expert2.w1"][0].astype(np.float16).reshape(-1))
+    path = str(tmp_path / "stack.weights")
+    js_path = layout.write_weights(path, L, blob)
+    blob2, table = layout.read_weights(path)
+    assert js_path.endswith("stack.json") and np.array_equal(blob, blob2)
+    L2 = layout.stack_from_json(table, 256, 8, 3, 2)
+    assert L2.blocks == L.blocks
+    bad = dict(tensors)
+    bad["blk0.out"] = (np.zeros((256, 255), np.float32), tensors["blk0.out"][1])
+    with pytest.raises(ValueError):
+        layout.pack_weights(L, bad)
+    with pytest.raises(KeyError):
+        layout.pack_weights(L, {k: v for k, v in tensors.items() if k != "proj_up"})
 
 
 def test_synthetic_data_is_seeded_per_frame():
