@@ -230,8 +230,9 @@ int prism_stack_destroy(prism_stack* st);
 
 /* in: device [frames][spatial_h*spatial_w][in_dim] fp16; out: device
  * [frames][T][out_dim] fp16 (must not alias in).  assign (nullable): device int32
- * [n_moe_blocks][frames*T] receives each MoE block's routing.  Stream-ordered,
- * no host synchronisation, no allocation: CUDA-graph capturable. */
+ * [n_moe_blocks][frames*T] receives each MoE block's routing.  frames == 0 is a
+ * no-op (in and out may then be NULL).  Stream-ordered, no host synchronisation,
+ * no allocation: CUDA-graph capturable. */
 int prism_stack_forward(prism_stack* st, const void* in, void* out, int frames,
                         int32_t* assign, void* stream);
 

@@ -689,10 +689,11 @@ extern "C" int prism_stack_status(prism_stack* st, void* stream) {
 
 extern "C" int prism_stack_forward(prism_stack* st, const void* in, void* out, int frames, int32_t* assign,
                                    void* stream) {
-    if (!st || !in || !out) return fail(PRISM_E_ARG, "prism_stack_forward: NULL argument");
+    if (!st) return fail(PRISM_E_ARG, "prism_stack_forward: NULL stack");
     if (frames < 0 || frames > st->max_frames)
         return fail(PRISM_E_RANGE, "prism_stack_forward: frames %d (max %d)", frames, st->max_frames);
-    if (frames == 0) return PRISM_OK;
+    if (frames == 0) return PRISM_OK;  // an empty batch: nothing to read or write
+    if (!in || !out) return fail(PRISM_E_ARG, "prism_stack_forward: NULL argument");
     if (in == out) return fail(PRISM_E_ARG, "prism_stack_forward: out aliases in");
     DeviceGuard g(st->ctx->device);
     cudaStream_t s = as_stream(stream);

@@ -162,6 +162,25 @@ def test_routing_histogram_and_skew(prism_ctx):
         assert 0.3 < frac < 0.7, f"skewed experts take {frac:.2f} of the tokens"
 
 
+def test_stack_zero_frames_is_a_no_op(prism_ctx):
+    """An empty batch launches nothing and leaves the output untouched; the next full call
+    is unaffected (routing counters stay clean)."""
+    import torch
+    cfg = configs.get("moe16x1")
+    blob = synth.make_blob(cfg.layout)
+    st = Stack(prism_ctx, cfg.layout, blob, 1)
+    x = torch.zeros((1, cfg.layout.tokens, cfg.layout.in_dim), dtype=torch.float16, device="cuda")
+    out = torch.full((1, cfg.layout.tokens, cfg.layout.out_dim), 7.0, dtype=torch.float16, device="cuda")
+    st.forward(x[:0], out[:0])  # frames = 0 (valid pointers)
+    torch.cuda.synchronize()
+    st.status()
+    assert bool((out == 7.0).all())
+    st.close()
+    o1, a1 = _run(prism_ctx, cfg.layout, blob, synth.make_frames(cfg.layout, 1))
+    o2, a2 = _run(prism_ctx, cfg.layout, blob, synth.make_frames(cfg.layout, 1))
+    assert (o1.view(np.uint16) == o2.view(np.uint16)).all() and (a1 == a2).all()
+
+
 def test_stack_argument_errors(prism_ctx):
     import torch
     from prism_inference_b200.abi import PrismError
