@@ -681,6 +681,10 @@ extern "C" int prism_stack_status(prism_stack* st, void* stream) {
     CUDA_TRY(cudaMemcpyAsync(&e, st->err, 4, cudaMemcpyDeviceToHost, as_stream(stream)));
     CUDA_TRY(cudaStreamSynchronize(as_stream(stream)));
     CUDA_TRY(cudaMemsetAsync(st->err, 0, 4, as_stream(stream)));
+    if (e) {  // a forward that gave up may have left routing counts behind: start the next one clean
+        CUDA_TRY(cudaMemsetAsync(st->counts, 0, 256 * 4, as_stream(stream)));
+        CUDA_TRY(cudaMemsetAsync(st->cursor, 0, 256 * 4, as_stream(stream)));
+    }
     CUDA_TRY(cudaStreamSynchronize(as_stream(stream)));
     if (e & ERR_TIMEOUT) return fail(PRISM_E_TIMEOUT, "a device-side wait timed out (error word 0x%x)", e);
     if (e & ERR_ROUTE) return fail(PRISM_E_RANGE, "routing invariant failed (error word 0x%x)", e);
