@@ -240,6 +240,16 @@ int prism_stack_forward(prism_stack* st, const void* in, void* out, int frames,
  * bounded wait gives up (PRISM_E_TIMEOUT) or an invariant fails; clears it. */
 int prism_stack_status(prism_stack* st, void* stream);
 
+/* Diagnostic for the failure path (no counterpart in the reference, whose waits are
+ * vkWaitForFences with an infinite timeout, prism_moe_bench.cpp:196-206): launches one
+ * kernel that leaves expert 0's routing count one token high, as a forward cut short
+ * leaves it, and then waits on a device barrier that nothing releases.  The wait gives up
+ * after the library's wait limit (2 s) and sets the error word, so the next
+ * prism_stack_status returns PRISM_E_TIMEOUT and resets the routing state.  A forward
+ * issued in between finds the counts inconsistent, plans no expert work and reports
+ * PRISM_E_TIMEOUT/PRISM_E_RANGE through the same status call.  Stream-ordered. */
+int prism_stack_inject_stall(prism_stack* st, void* stream);
+
 /* Per-kernel timing (no counterpart in the reference, whose benches time a whole
  * command buffer with timestamp queries, prism_moe_bench.cpp:183-209).  While
  * enabled, prism_stack_forward brackets every launch with CUDA events on the

@@ -123,6 +123,11 @@ class Stack:
     def status(self, stream=None):
         check(self.lib, self.lib.prism_stack_status(self.h, _stream(stream)))
 
+    def inject_stall(self, stream=None):
+        """Diagnostic (prism_stack_inject_stall): a device wait that nothing releases; the
+        next status() raises PRISM_E_TIMEOUT after the library's wait limit."""
+        check(self.lib, self.lib.prism_stack_inject_stall(self.h, _stream(stream)))
+
     def profile(self, enable: bool = True):
         check(self.lib, self.lib.prism_stack_profile(self.h, int(enable)))
 

@@ -86,7 +86,7 @@ EXPORTS = ("prism_create", "prism_destroy", "prism_last_error_string", "prism_ab
            "prism_proj_down", "prism_dense_block", "prism_stack_create", "prism_stack_destroy",
            "prism_stack_forward", "prism_stack_status", "prism_stack_launch_count",
            "prism_stack_tokens_per_frame", "prism_stack_profile", "prism_stack_profile_read",
-           "prism_expert_all_static")
+           "prism_expert_all_static", "prism_stack_inject_stall")
 STATIC_MAX_TOKENS = 65536  # PRISM_STATIC_MAX_TOKENS
 KERNEL_KINDS = ("proj_up", "attn", "router", "route", "expert", "dense_ffn", "proj_down", "copy")
 
@@ -120,6 +120,7 @@ def load(path: os.PathLike | None = None) -> C.CDLL:
         "prism_stack_destroy": (i32, [vp]),
         "prism_stack_forward": (i32, [vp, vp, vp, i32, vp, vp]),
         "prism_stack_status": (i32, [vp, vp]),
+        "prism_stack_inject_stall": (i32, [vp, vp]),
         "prism_stack_launch_count": (i32, [vp, i32]),
         "prism_stack_tokens_per_frame": (i32, [vp]),
         "prism_stack_profile": (i32, [vp, i32]),

@@ -45,6 +45,16 @@ __global__ void __launch_bounds__(256) route_kernel(RouteArgs a) {
         s_toff[e] += v1;
         __syncthreads();
     }
+    // Counts that do not add up to the token count (left behind by a forward that gave up)
+    // would place rows outside the permutation and tile arrays: flag it, plan no tiles and
+    // scatter nothing.  The expert kernel that follows then has no work and clears the counts.
+    if (s_off[255] != a.n_tokens) {
+        if (blockIdx.x == 0 && e == 0) {
+            *a.n_tiles = 0;
+            atomicOr(a.err, ERR_ROUTE);
+        }
+        return;
+    }
     if (blockIdx.x == 0) {
         if (e < n && a.counts_out) a.counts_out[e] = c;
         // tile i belongs to the first expert whose inclusive tile count exceeds i; every
@@ -66,10 +76,7 @@ __global__ void __launch_bounds__(256) route_kernel(RouteArgs a) {
             t.pad = 0;
             a.tiles[i] = t;
         }
-        if (e == 255) {
-            *a.n_tiles = n_tiles;
-            if (s_off[255] != a.n_tokens) atomicOr(a.err, ERR_ROUTE);  // every token routed exactly once
-        }
+        if (e == 255) *a.n_tiles = n_tiles;
     }
     // ---- this CTA's chunk of tokens
     constexpr int kPer = kScatterChunk / 256;

@@ -691,6 +691,31 @@ extern "C" int prism_stack_status(prism_stack* st, void* stream) {
     return PRISM_OK;
 }
 
+// Diagnostic stall: one warp adds a token to expert 0's routing count, as a router cut short
+// in mid-block leaves it, then waits through the library's bounded mbarrier wait on a barrier
+// that nothing arrives at.  The wait gives up after kWaitLimitNs and the kernel records
+// ERR_TIMEOUT in the stack's error word, as a stack kernel whose wait ran out does.
+__global__ void __launch_bounds__(32) stall_kernel(int32_t* counts, uint32_t* err) {
+    __shared__ uint64_t bar;
+    __shared__ int gave_up;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        gave_up = 0;
+        fence_barrier_init();
+        atomicAdd(&counts[0], 1);
+    }
+    __syncwarp();
+    if (!mbar_wait_w(&bar, 0, &gave_up) && threadIdx.x == 0) atomicOr(err, ERR_TIMEOUT);
+}
+
+extern "C" int prism_stack_inject_stall(prism_stack* st, void* stream) {
+    if (!st) return fail(PRISM_E_ARG, "prism_stack_inject_stall: NULL");
+    DeviceGuard g(st->ctx->device);
+    stall_kernel<<<1, 32, 0, as_stream(stream)>>>(st->counts, st->err);
+    CUDA_TRY(cudaGetLastError());
+    return PRISM_OK;
+}
+
 extern "C" int prism_stack_forward(prism_stack* st, const void* in, void* out, int frames, int32_t* assign,
                                    void* stream) {
     if (!st) return fail(PRISM_E_ARG, "prism_stack_forward: NULL stack");

@@ -181,6 +181,53 @@ def test_stack_zero_frames_is_a_no_op(prism_ctx):
     assert (o1.view(np.uint16) == o2.view(np.uint16)).all() and (a1 == a2).all()
 
 
+def test_device_wait_timeout_is_reported_and_recovered(prism_ctx):
+    """A device wait that nothing releases gives up after the library's wait limit (2 s)
+    instead of hanging: prism_stack_status raises PRISM_E_TIMEOUT once, resets the routing
+    state the stalled kernel left behind, and the next forward gives a clean run's bits.  A
+    forward issued between the stall and the status call finds the routing counts
+    inconsistent, plans no expert work, and is reported through the same status call."""
+    import time
+
+    import torch
+    from prism_inference_b200.abi import PrismError
+    cfg = configs.get("moe64x16", n_blocks=2)
+    L = cfg.layout
+    blob = synth.make_blob(L)
+    x = synth.make_frames(L, 2)
+    st = Stack(prism_ctx, L, blob, 2)
+    xd = torch.from_numpy(x.view(np.int16)).cuda().view(torch.float16)
+    ref = torch.empty((2, L.tokens, L.out_dim), dtype=torch.float16, device="cuda")
+    st.forward(xd, ref)
+    torch.cuda.synchronize()
+    st.status()
+    out = torch.empty_like(ref)
+
+    t0 = time.perf_counter()
+    st.inject_stall()
+    with pytest.raises(PrismError, match="TIMEOUT"):
+        st.status()
+    waited = time.perf_counter() - t0
+    assert 1.5 < waited < 60, f"the stalled wait ended after {waited:.2f} s"
+    st.status()  # the error word was cleared
+    out.zero_()
+    st.forward(xd, out)
+    torch.cuda.synchronize()
+    st.status()
+    assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
+
+    st.inject_stall()
+    st.forward(xd, out)  # counts one token high: routing must refuse, not scatter out of range
+    with pytest.raises(PrismError, match="TIMEOUT"):
+        st.status()
+    out.zero_()
+    st.forward(xd, out)
+    torch.cuda.synchronize()
+    st.status()
+    assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
+    st.close()
+
+
 def test_stack_argument_errors(prism_ctx):
     import torch
     from prism_inference_b200.abi import PrismError
