@@ -98,6 +98,47 @@ def test_headline_stack_full_depth(prism_ctx, oracle):
     _check(prism_ctx, oracle, cfg.layout, blob, x, "moe64x16-full")
 
 
+def test_skewed_config_full_depth(prism_ctx, oracle):
+    """Config 5 at its full depth: 32 experts x 22 blocks + adapters, about half of the
+    tokens routed to 4 experts (long expert segments, many full tiles of one expert)."""
+    cfg = configs.get("moe32x22skew")
+    blob = synth.make_blob(cfg.layout, router_skew=cfg.router_skew, skew_bias=cfg.skew_bias)
+    x = synth.make_frames(cfg.layout, 2)
+    _check(prism_ctx, oracle, cfg.layout, blob, x, "moe32x22skew-full")
+
+
+def test_bench_workload_frames(prism_ctx, oracle):
+    """The benchmarked workload itself (config 4, 64 frames, 16 blocks): sampled frames of
+    the batch equal single-frame runs bit for bit (tiles and expert segments mix frames and
+    hold up to 64x a single frame's rows), and the last frame matches the oracle."""
+    import torch
+    cfg = configs.get("moe64x16")
+    L = cfg.layout
+    T = L.tokens
+    blob = synth.make_blob(L)
+    x = synth.make_frames(L, 64)
+    st = Stack(prism_ctx, L, blob, 64)
+    xd = torch.from_numpy(x.view(np.int16)).cuda().view(torch.float16)
+    out = torch.empty((64, T, L.out_dim), dtype=torch.float16, device="cuda")
+    asg = torch.empty((L.n_moe_blocks, 64 * T), dtype=torch.int32, device="cuda")
+    st.forward(xd, out, asg)
+    one = torch.empty((1, T, L.out_dim), dtype=torch.float16, device="cuda")
+    asg1 = torch.empty((L.n_moe_blocks, T), dtype=torch.int32, device="cuda")
+    for f in (0, 37, 63):
+        st.forward(xd[f:f + 1], one, asg1)
+        assert torch.equal(one[0].view(torch.int16), out[f].view(torch.int16)), f
+        assert torch.equal(asg1, asg[:, f * T:(f + 1) * T]), f
+    torch.cuda.synchronize()
+    st.status()
+    o = out[63:].view(torch.int16).cpu().numpy().view(np.float16)
+    a = asg[:, 63 * T:].cpu().numpy()
+    st.close()
+    ref, _, stats = oracle.stack(L, blob, x[63:], forced=a, tie_thr=TIE_MARGIN)
+    assert stats[2] == 0, f"{stats[2]} hard routing mismatches"
+    m = assert_close(o, ref, "moe64x16 frame 63 of 64")
+    print(f"frame 63 of 64: max_abs {m[0]:.3g} rel_l2 {m[1]:.3g}; followed at ties {stats[1]}")
+
+
 def test_frames_are_independent_and_deterministic(prism_ctx):
     """Frame f gives the same bits alone and inside a batch (tiles mix frames), and
     two runs give the same bits."""
