@@ -13,10 +13,11 @@ Data: seeded synthetic frames ~N(0,1) and weights ~N(0,0.02) (the reference ship
 neither).  The activations (267 MB per buffer) are larger than the 126 MB L2.
 
 value: tokens/s over all ranks, inputs resident in HBM, device time (CUDA events,
-max over ranks).  e2e: the same metric through the same public call with pinned host
-buffers, the host->device copy of every step's frames and the device->host copy of every
-step's output inside the timed region, overlapped across neighbouring steps as a serving
-loop would (copy-in and copy-out streams, double-buffered device buffers).  roofline: the kernel kind with the largest share of the
+max over ranks).  e2e: the same metric through the C ABI's host-buffer call
+(prism_stack_submit / prism_stack_wait) from page-locked host memory: the host->device copy
+of every step's frames and the device->host copy of every step's output are inside the timed
+region, overlapped across neighbouring steps by the library's two staging slots as a serving
+loop runs.  roofline: the kernel kind with the largest share of the
 timed region, its algorithmic FLOPs per launch / its mean event-timed duration,
 against the sustained cuBLAS bf16 figure of MEASURED_PEAKS.json.
 
@@ -69,7 +70,8 @@ def dist_env():
 
 # ---------------------------------------------------------------- clocks ----
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    """nvidia-smi clocks / throttle reasons sampled every 100 ms; the figures reported are
+    the samples taken between mark() and stop() (the timed regions)."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -82,12 +84,21 @@ class ClockSampler:
     def start(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
         except OSError:
             self.proc = None
+
+    def wait_first(self, timeout=15.0):
+        """Block until the first sample has arrived (nvidia-smi can take a while to start)."""
+        t0 = time.time()
+        while self.proc and not self.rows and time.time() - t0 < timeout:
+            time.sleep(0.05)
+
+    def mark(self) -> int:
+        return len(self.rows)
 
     def _read(self):
         for line in self.proc.stdout:
@@ -95,7 +106,7 @@ class ClockSampler:
             if len(parts) == 9:
                 self.rows.append(parts)
 
-    def stop(self):
+    def stop(self, first: int = 0):
         if not self.proc:
             return None
         self.proc.terminate()
@@ -107,7 +118,11 @@ class ClockSampler:
         reasons = set()
         sm = []
         smax = None
-        for r in self.rows:
+        rows = self.rows[first:]
+        in_region = len(rows)
+        if not rows:  # a region shorter than the sampling period: the nearest sample after it
+            rows = self.rows[-1:]
+        for r in rows:
             try:
                 sm.append(float(r[1]))
                 smax = float(r[2])
@@ -119,7 +134,7 @@ class ClockSampler:
         if not sm:
             return None
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": in_region}
 
 
 # ---------------------------------------------------------------- flops ------
@@ -309,11 +324,12 @@ def run_ours(args):
     # ---- timed region (device-resident inputs); per-kernel events on the same stream
     clocks = ClockSampler(dev)
     clocks.start()
-    time.sleep(0.3)
+    clocks.wait_first()
     st.profile(True)
     barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clock_mark = clocks.mark()
     e0.record(stream)
     for _ in range(args.steps):
         st.forward(x, out)
@@ -323,63 +339,41 @@ def run_ours(args):
     ms = e0.elapsed_time(e1) / args.steps
     prof = st.profile_read()
     st.profile(False)
-    clk = clocks.stop()
     ms = max_over_ranks(ms)
     st.status()
     launches = st.launch_count(B) * args.steps
 
-    # ---- end to end: pinned host frames in, host output back, every step.  As a serving loop
-    # would, the copies of neighbouring steps overlap the compute: step i's frames go in on a
-    # copy stream while step i-1 computes and step i-2's output comes back on another, with
-    # double-buffered device input/output and events guarding each buffer's reuse.
-    ref_out = out.clone()  # the device-resident result of the same frames
+    # ---- end to end through the C ABI with host buffers: every step, prism_stack_submit
+    # uploads the step's frames from page-locked host memory, runs the stack on `stream` and
+    # downloads the output into host memory.  The library's two staging slots overlap step i's
+    # upload and step i-1's download with the forward in between, as a serving loop runs;
+    # prism_stack_wait makes `stream` wait on the device for the last download.
+    ref_out = out.cpu()  # the device-resident result of the same frames
     xh = torch.from_numpy(x_host.view(np.int16)).view(torch.float16).pin_memory()
     oh = [torch.empty((B, T, L.out_dim), dtype=torch.float16).pin_memory() for _ in range(2)]
-    xd = [torch.empty_like(x) for _ in range(2)]
-    od = [out, torch.empty_like(out)]
-    s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
-    ev = lambda: torch.cuda.Event()
-    in_ready, in_free, out_ready, out_free = ([ev(), ev()] for _ in range(4))
 
-    def e2e_steps(n, start_ev=None):
-        if start_ev is not None:
-            s_in.wait_event(start_ev)
-            s_out.wait_event(start_ev)
+    def e2e_steps(n):
+        t = None
         for i in range(n):
-            b = i & 1
-            with torch.cuda.stream(s_in):
-                if i >= 2:
-                    s_in.wait_event(in_free[b])  # step i-2 has read xd[b]
-                xd[b].copy_(xh, non_blocking=True)
-                in_ready[b].record(s_in)
-            stream.wait_event(in_ready[b])
-            if i >= 2:
-                stream.wait_event(out_free[b])  # step i-2's output has left od[b]
-            st.forward(xd[b], od[b])
-            in_free[b].record(stream)
-            out_ready[b].record(stream)
-            with torch.cuda.stream(s_out):
-                s_out.wait_event(out_ready[b])
-                oh[b].copy_(od[b], non_blocking=True)
-                out_free[b].record(s_out)
-        stream.wait_event(out_free[(n - 1) & 1])  # the last output is on the host
-        if n >= 2:
-            stream.wait_event(out_free[(n - 2) & 1])
+            t = st.submit(xh, oh[i & 1], stream)
+        st.wait(t, stream, host=False)
 
     e2e_steps(2)
     torch.cuda.synchronize()
     barrier()
     e0.record(stream)
-    e2e_steps(args.steps, e0)
+    e0.synchronize()  # the start is stamped before the first upload is queued
+    e2e_steps(args.steps)
     e1.record(stream)
     torch.cuda.synchronize()
     barrier()
     ms_e2e = max_over_ranks(e0.elapsed_time(e1) / args.steps)
-    last = oh[(args.steps - 1) & 1]
-    if not torch.equal(last.view(torch.int16), ref_out.cpu().view(torch.int16)):
+    clk = clocks.stop(clock_mark)  # samples over both timed regions
+    st.status()
+    oh = oh[(args.steps - 1) & 1]
+    if not torch.equal(oh.view(torch.int16), ref_out.view(torch.int16)):
         raise SystemExit("bench: the end-to-end output differs from the device-resident output")
     del ref_out
-    oh = last
 
     # ---- batch-1 latency (one frame through the whole stack)
     x1, o1 = x[:1], out[:1]
@@ -469,8 +463,9 @@ def run_ours(args):
                            "kernel_ms_per_step": kernel_ms},
                 "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": int(xh.numel() * 2),
                         "d2h_bytes_per_step": int(oh.numel() * 2), "ms_per_step": ms_e2e,
-                        "overlap": "copy-in, compute and copy-out of neighbouring steps on three streams, "
-                                   "double-buffered device input/output"},
+                        "api": "prism_stack_submit / prism_stack_wait (C ABI, host buffers)",
+                        "overlap": "upload, forward and download of neighbouring steps on three streams, "
+                                   "two device staging slots inside the library"},
                 "gpu_launches": launches, "roofline": roof, "cpu_baseline": cpu, "clocks": clk}
         print(json.dumps(line))
     st.close()

@@ -236,6 +236,33 @@ int prism_stack_destroy(prism_stack* st);
 int prism_stack_forward(prism_stack* st, const void* in, void* out, int frames,
                         int32_t* assign, void* stream);
 
+/* Host-buffer inference, the counterpart of PrismVulkan::Infer (prism_vulkan.h:90-91,
+ * prism_vulkan.cpp:1007-1040: upload, run, wait, download, return the GPU time).
+ * host_in: host [frames][T][in_dim] fp16; host_out: host [frames][T][out_dim] fp16, or
+ * NULL to skip the download (as the reference allows).  Synchronous: returns once host_out
+ * is written, with the device error word checked as prism_stack_status does.  *gpu_ms
+ * (nullable) receives the device time of the forward alone, as the reference returns the
+ * inference time without the copies.  Page-locked host memory (cudaHostAlloc,
+ * cudaHostRegister) is copied by DMA; pageable memory goes through the driver's staging.
+ * The first host-buffer call allocates two device staging slots (input and output for
+ * max_frames each) and three internal streams. */
+int prism_stack_infer(prism_stack* st, const void* host_in, void* host_out, int frames,
+                      float* gpu_ms);
+
+/* Pipelined host-buffer inference for serving loops.  prism_stack_submit enqueues the
+ * upload of host_in on an internal copy stream, the forward on `stream` and the download
+ * into host_out (nullable) on a second copy stream, and returns at once with a ticket.
+ * Submissions alternate between the two staging slots, so the upload of one and the
+ * download of the one before overlap the forward in between; ordering between slot uses is
+ * kept on the device (events), never by blocking the host.  host_in and host_out must stay
+ * untouched until the ticket completes.  prism_stack_wait: with stream == NULL the host
+ * blocks until the ticket's download has landed; otherwise `stream` waits for it on the
+ * device (pass cudaStreamLegacy for the legacy default stream).  Waiting on a ticket also
+ * covers every earlier one.  Same threading rule as prism_stack_forward. */
+int prism_stack_submit(prism_stack* st, const void* host_in, void* host_out, int frames,
+                       void* stream, int64_t* ticket);
+int prism_stack_wait(prism_stack* st, int64_t ticket, void* stream);
+
 /* Host-synchronising check of the device error word the kernels set when a
  * bounded wait gives up (PRISM_E_TIMEOUT) or an invariant fails; clears it. */
 int prism_stack_status(prism_stack* st, void* stream);

@@ -29,6 +29,19 @@ def _ptr(t) -> int:
     return t.data_ptr()
 
 
+def _host_ptr(a) -> int | None:
+    """Address of a host array (CPU tensor or numpy array); None passes through."""
+    if a is None:
+        return None
+    if hasattr(a, "data_ptr"):
+        if a.is_cuda or not a.is_contiguous():
+            raise ValueError("expected a contiguous host tensor")
+        return a.data_ptr()
+    if not a.flags["C_CONTIGUOUS"]:
+        raise ValueError("expected a C-contiguous array")
+    return a.ctypes.data
+
+
 def _stream(stream) -> int | None:
     if stream is None:
         import torch
@@ -119,6 +132,26 @@ class Stack:
                                                      _ptr(assign) if assign is not None else None,
                                                      _stream(stream)))
         return out
+
+    def infer(self, host_in, host_out=None) -> float:
+        """prism_stack_infer: host_in [F, T, in_dim] / host_out [F, T, out_dim] fp16 host
+        arrays (CPU tensors, page-locked for DMA, or numpy arrays); synchronous.  Returns
+        the forward's device time in ms."""
+        ms = C.c_float()
+        check(self.lib, self.lib.prism_stack_infer(self.h, _host_ptr(host_in), _host_ptr(host_out),
+                                                   host_in.shape[0], C.byref(ms)))
+        return ms.value
+
+    def submit(self, host_in, host_out=None, stream=None) -> int:
+        """prism_stack_submit: enqueue upload, forward and download; returns the ticket."""
+        t = C.c_int64()
+        check(self.lib, self.lib.prism_stack_submit(self.h, _host_ptr(host_in), _host_ptr(host_out),
+                                                    host_in.shape[0], _stream(stream), C.byref(t)))
+        return t.value
+
+    def wait(self, ticket: int, stream=None, host: bool = True):
+        """prism_stack_wait: block the host (default) or make `stream` wait on the device."""
+        check(self.lib, self.lib.prism_stack_wait(self.h, ticket, None if host else _stream(stream)))
 
     def status(self, stream=None):
         check(self.lib, self.lib.prism_stack_status(self.h, _stream(stream)))

@@ -380,6 +380,15 @@ struct prism_stack {
     ExpertTile* tiles = nullptr;
     uint32_t* err = nullptr;
     std::vector<void*> allocs;
+    // host-buffer inference (prism_stack_infer / _submit / _wait): two device staging slots,
+    // an upload and a download stream, created on first use
+    struct Staging {
+        bool ready = false;
+        __half *in[2] = {}, *out[2] = {};
+        cudaStream_t s_in = nullptr, s_out = nullptr, s_fwd = nullptr;
+        cudaEvent_t in_ready[2] = {}, out_done[2] = {}, t0[2] = {}, t1[2] = {};
+        int64_t next = 0;  // ticket of the next submission; slot = ticket & 1
+    } stg;
     // per-kernel profiling (prism_stack_profile)
     bool profiling = false;
     std::vector<cudaEvent_t> ev_pool;
@@ -399,7 +408,21 @@ int dev_alloc(prism_stack* st, T** p, size_t count) {
     return PRISM_OK;
 }
 
+void free_staging(prism_stack* st) {
+    auto& q = st->stg;
+    for (int i = 0; i < 2; ++i) {
+        for (cudaEvent_t* e : {&q.in_ready[i], &q.out_done[i], &q.t0[i], &q.t1[i]})
+            if (*e) cudaEventDestroy(*e), *e = nullptr;
+        if (q.in[i]) cudaFree(q.in[i]), q.in[i] = nullptr;
+        if (q.out[i]) cudaFree(q.out[i]), q.out[i] = nullptr;
+    }
+    for (cudaStream_t* s : {&q.s_in, &q.s_out, &q.s_fwd})
+        if (*s) cudaStreamDestroy(*s), *s = nullptr;
+    q.ready = false;
+}
+
 void free_stack(prism_stack* st) {
+    free_staging(st);
     for (void* p : st->allocs) cudaFree(p);
     st->allocs.clear();
     for (cudaEvent_t e : st->ev_pool) cudaEventDestroy(e);
@@ -952,6 +975,105 @@ extern "C" int prism_stack_forward(prism_stack* st, const void* in, void* out, i
         CUDA_TRY(cudaMemcpyAsync(out, cur, (size_t)rows * D * 2, cudaMemcpyDeviceToDevice, s));
     }
     return PRISM_OK;
+}
+
+// ---- host-buffer inference -------------------------------------------------------------
+// The reference's Infer uploads the frame through a staging buffer, runs the recorded
+// command buffer, waits on a fence and downloads the result (prism_vulkan.cpp:1007-1040).
+// Here two device staging slots let one submission's upload and the previous one's download
+// run on their own streams while the forward in between computes: per slot, the upload waits
+// for the forward that last read the slot, the forward waits for the upload and for the
+// download that last read its output slot, and the download waits for the forward.
+
+namespace {
+
+int staging_init(prism_stack* st) {
+    auto& q = st->stg;
+    if (q.ready) return PRISM_OK;
+    const size_t rows = (size_t)st->T * st->max_frames;
+    bool ok = true;
+    for (int i = 0; i < 2 && ok; ++i) {
+        ok = cudaMalloc(&q.in[i], rows * st->desc.in_dim * 2) == cudaSuccess &&
+             cudaMalloc(&q.out[i], rows * st->desc.out_dim * 2) == cudaSuccess &&
+             cudaEventCreateWithFlags(&q.in_ready[i], cudaEventDisableTiming) == cudaSuccess &&
+             cudaEventCreateWithFlags(&q.out_done[i], cudaEventDisableTiming) == cudaSuccess &&
+             cudaEventCreate(&q.t0[i]) == cudaSuccess && cudaEventCreate(&q.t1[i]) == cudaSuccess;
+    }
+    for (cudaStream_t* s : {&q.s_in, &q.s_out, &q.s_fwd})
+        ok = ok && cudaStreamCreateWithFlags(s, cudaStreamNonBlocking) == cudaSuccess;
+    if (!ok) {
+        cudaGetLastError();
+        free_staging(st);
+        return fail(PRISM_E_NOMEM, "host-buffer staging: allocation of 2 x %zu frames' buffers failed",
+                    (size_t)st->max_frames);
+    }
+    q.ready = true;
+    return PRISM_OK;
+}
+
+}  // namespace
+
+extern "C" int prism_stack_submit(prism_stack* st, const void* host_in, void* host_out, int frames, void* stream,
+                                  int64_t* ticket) {
+    if (!st) return fail(PRISM_E_ARG, "prism_stack_submit: NULL stack");
+    if (frames < 0 || frames > st->max_frames)
+        return fail(PRISM_E_RANGE, "prism_stack_submit: frames %d (max %d)", frames, st->max_frames);
+    if (frames > 0 && !host_in) return fail(PRISM_E_ARG, "prism_stack_submit: NULL host_in");
+    DeviceGuard g(st->ctx->device);
+    int rc = staging_init(st);
+    if (rc) return rc;
+    auto& q = st->stg;
+    const int64_t k = q.next;
+    const int p = (int)(k & 1);
+    cudaStream_t s = as_stream(stream);
+    const size_t rows = (size_t)st->T * frames;
+    const size_t in_bytes = rows * st->desc.in_dim * 2, out_bytes = rows * st->desc.out_dim * 2;
+    // upload, once the forward that last read this slot is done (t1 of the slot)
+    CUDA_TRY(cudaStreamWaitEvent(q.s_in, q.t1[p], 0));
+    if (in_bytes) CUDA_TRY(cudaMemcpyAsync(q.in[p], host_in, in_bytes, cudaMemcpyHostToDevice, q.s_in));
+    CUDA_TRY(cudaEventRecord(q.in_ready[p], q.s_in));
+    // forward, once the upload has landed and the slot's previous output has been downloaded
+    CUDA_TRY(cudaStreamWaitEvent(s, q.in_ready[p], 0));
+    CUDA_TRY(cudaStreamWaitEvent(s, q.out_done[p], 0));
+    CUDA_TRY(cudaEventRecord(q.t0[p], s));
+    if ((rc = prism_stack_forward(st, q.in[p], q.out[p], frames, nullptr, stream))) return rc;
+    CUDA_TRY(cudaEventRecord(q.t1[p], s));
+    // download
+    if (host_out && out_bytes) {
+        CUDA_TRY(cudaStreamWaitEvent(q.s_out, q.t1[p], 0));
+        CUDA_TRY(cudaMemcpyAsync(host_out, q.out[p], out_bytes, cudaMemcpyDeviceToHost, q.s_out));
+        CUDA_TRY(cudaEventRecord(q.out_done[p], q.s_out));
+    } else {
+        CUDA_TRY(cudaEventRecord(q.out_done[p], s));
+    }
+    q.next = k + 1;
+    if (ticket) *ticket = k;
+    return PRISM_OK;
+}
+
+extern "C" int prism_stack_wait(prism_stack* st, int64_t ticket, void* stream) {
+    if (!st) return fail(PRISM_E_ARG, "prism_stack_wait: NULL stack");
+    if (ticket < 0 || ticket >= st->stg.next)
+        return fail(PRISM_E_RANGE, "prism_stack_wait: ticket %lld was not submitted", (long long)ticket);
+    DeviceGuard g(st->ctx->device);
+    // a later submission to the same slot completes after this one, so its event covers it
+    cudaEvent_t e = st->stg.out_done[ticket & 1];
+    if (stream) CUDA_TRY(cudaStreamWaitEvent(as_stream(stream), e, 0));
+    else CUDA_TRY(cudaEventSynchronize(e));
+    return PRISM_OK;
+}
+
+extern "C" int prism_stack_infer(prism_stack* st, const void* host_in, void* host_out, int frames, float* gpu_ms) {
+    if (!st) return fail(PRISM_E_ARG, "prism_stack_infer: NULL stack");
+    DeviceGuard g(st->ctx->device);
+    int rc = staging_init(st);
+    if (rc) return rc;
+    int64_t k = 0;
+    if ((rc = prism_stack_submit(st, host_in, host_out, frames, st->stg.s_fwd, &k))) return rc;
+    const int p = (int)(k & 1);
+    CUDA_TRY(cudaEventSynchronize(st->stg.out_done[p]));
+    if (gpu_ms) CUDA_TRY(cudaEventElapsedTime(gpu_ms, st->stg.t0[p], st->stg.t1[p]));
+    return prism_stack_status(st, st->stg.s_fwd);
 }
 
 extern "C" int prism_stack_profile(prism_stack* st, int enable) {

@@ -222,6 +222,55 @@ def test_stack_zero_frames_is_a_no_op(prism_ctx):
     assert (o1.view(np.uint16) == o2.view(np.uint16)).all() and (a1 == a2).all()
 
 
+def test_host_buffer_infer_and_pipelined_submit(prism_ctx):
+    """prism_stack_infer (the reference's Infer: host in, host out, GPU ms) and the pipelined
+    prism_stack_submit / prism_stack_wait give prism_stack_forward's bits: pageable numpy and
+    page-locked tensor buffers, five submissions of different sizes through the two staging
+    slots (one empty), a submission without download, host and device-side waits."""
+    import torch
+    from prism_inference_b200.abi import PrismError
+    cfg = configs.get("moe64x16", n_blocks=2)
+    L = cfg.layout
+    T = L.tokens
+    blob = synth.make_blob(L)
+    x = synth.make_frames(L, 3)
+    st = Stack(prism_ctx, L, blob, 3)
+    xd = torch.from_numpy(x.view(np.int16)).cuda().view(torch.float16)
+    ref = torch.empty((3, T, L.out_dim), dtype=torch.float16, device="cuda")
+    st.forward(xd, ref)
+    torch.cuda.synchronize()
+    st.status()
+    ref_h = ref.view(torch.int16).cpu().numpy()
+
+    out_np = np.zeros((3, T, L.out_dim), np.float16)
+    ms = st.infer(x, out_np)
+    assert ms > 0.0
+    assert (out_np.view(np.int16) == ref_h).all()
+
+    xin = torch.from_numpy(x.view(np.int16)).pin_memory()
+    sizes = [3, 1, 2, 0, 3]
+    outs = [torch.zeros((3, T, L.out_dim), dtype=torch.int16).pin_memory() for _ in sizes]
+    tickets = [st.submit(xin[:n], outs[i][:n]) for i, n in enumerate(sizes)]
+    assert tickets == list(range(tickets[0], tickets[0] + len(sizes)))
+    st.wait(tickets[-1])  # covers every earlier ticket
+    for i, n in enumerate(sizes):
+        assert (outs[i][:n].numpy() == ref_h[:n]).all(), i
+        assert not outs[i][n:].any(), i  # nothing written past the submitted frames
+
+    t = st.submit(xin, None)  # forward without download
+    outs[0].zero_()
+    t = st.submit(xin, outs[0])
+    st.wait(t, host=False)  # the current stream waits on the device for the download
+    ev = torch.cuda.Event()
+    ev.record()
+    ev.synchronize()  # the current stream only: done once the download has landed
+    assert (outs[0].numpy() == ref_h).all()
+    st.status()
+    with pytest.raises(PrismError, match="RANGE"):
+        st.wait(t + 1)
+    st.close()
+
+
 def test_device_wait_timeout_is_reported_and_recovered(prism_ctx):
     """A device wait that nothing releases gives up after the library's wait limit (2 s)
     instead of hanging: prism_stack_status raises PRISM_E_TIMEOUT once, resets the routing
