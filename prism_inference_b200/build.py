@@ -5,7 +5,9 @@
 Every .cu file under csrc/ is compiled for sm_100a only
 (-gencode arch=compute_100a,code=sm_100a) and linked with the static CUDA runtime;
 the driver API (cuTensorMapEncodeTiled) is resolved at run time through
-cudaGetDriverEntryPoint, so nothing links against libcuda.
+cudaGetDriverEntryPoint, so nothing links against libcuda.  csrc/prism_bench.cpp, a C++
+caller that uses only include/prism_moe.h, is linked against the library as
+prism_inference_b200/prism_bench.
 """
 from __future__ import annotations
 
@@ -18,6 +20,7 @@ from pathlib import Path
 PKG = Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
 OUT = PKG / "libprism_moe.so"
+BENCH = PKG / "prism_bench"
 BUILD = PKG / "_build"
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
@@ -51,6 +54,14 @@ def build(force: bool = False) -> Path:
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+    src = CSRC / "prism_bench.cpp"
+    deps = [src, OUT, PKG.parent / "include" / "prism_moe.h"]
+    if force or not BENCH.exists() or BENCH.stat().st_mtime < max(d.stat().st_mtime for d in deps):
+        cmd = [NVCC, "-O2", "-std=c++17", "-I", str(PKG.parent / "include"), str(src), "-L", str(PKG),
+               "-lprism_moe", "-Xlinker", "-rpath,$ORIGIN", "-o", str(BENCH)]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"prism_bench build failed:\n{r.stdout}\n{r.stderr}")
     return OUT
 
 
