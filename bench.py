@@ -156,6 +156,26 @@ def kind_flops_per_frame(L, kind):
     return 0.0
 
 
+def batch1_bytes(L, experts_touched):
+    """Algorithmic DRAM bytes of one frame through the stack: every weight and bias the frame
+    touches once (attention, router and adapter weights; of the experts, those that received
+    at least one token, per MoE block) plus the frame in and the result out, fp16."""
+    D, T = L.dim, L.tokens
+    n = 0
+    if L.up_w >= 0:
+        n += 256 * 128 + 256
+    if L.down_w >= 0:
+        n += 128 * 256 + 128
+    moe = iter(experts_touched)
+    for b in L.blocks:
+        n += 3 * D * D + 3 * D + D * D + D
+        if b.kind == "moe":
+            n += b.n_experts * D + b.n_experts + next(moe) * (2 * D * D + 2 * D)
+        else:
+            n += 2 * D * b.ffn_hidden + b.ffn_hidden + D
+    return 2 * (n + T * L.in_dim + T * L.out_dim)
+
+
 def load_peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -405,6 +425,13 @@ def run_ours(args):
     ms_b1_graph = max_over_ranks(e0.elapsed_time(e1) / n1)
     del g
     st.status()
+    # batch 1 is bound by streaming the weights the frame touches from HBM
+    asg1 = torch.empty((max(1, L.n_moe_blocks), T), dtype=torch.int32, device="cuda")
+    st.forward(x1, o1, asg1 if L.n_moe_blocks else None)
+    torch.cuda.synchronize()
+    touched = [int(np.unique(a).size) for a in asg1.cpu().numpy()[:L.n_moe_blocks]]
+    b1_bytes = batch1_bytes(L, touched)
+    b1_gbs = b1_bytes / (ms_b1_graph / 1e3) / 1e9
 
     # ---- N > 1: the sharded output collected on rank 0 (NCCL over NVLink), timed apart
     # from the compute (the frames are independent: this is the only exchange)
@@ -430,6 +457,10 @@ def run_ours(args):
 
     # ---- roofline of the dominant kernel kind
     peak_tf, peak_gbs, peak_src = load_peaks()
+    b1_roof = {"bound": "hbm", "achieved": b1_gbs, "peak": peak_gbs, "unit": "GB/s", "frac": b1_gbs / peak_gbs,
+               "peak_source": f"{peak_src} hbm_gbs", "bytes_per_frame": b1_bytes,
+               "experts_touched_per_block": statistics.mean(touched) if touched else 0,
+               "time": "batch1_graph_ms"}
     roof = None
     if prof:
         kind = max(prof, key=lambda k: prof[k][0])
@@ -458,6 +489,7 @@ def run_ours(args):
                            "parallelism": f"frame-sharded x{ws}, weights replicated",
                            "l2": "inputs/activations larger than L2 (134 MB in, 267 MB per activation buffer)",
                            "frames_per_s": B * ws / (ms / 1e3), "batch1_ms": ms_b1, "batch1_graph_ms": ms_b1_graph,
+                           "batch1_roofline": b1_roof,
                            "output_gather": gather,
                            "tflops_effective": flops_step / (ms / 1e3) / 1e12,
                            "kernel_ms_per_step": kernel_ms},
