@@ -691,8 +691,8 @@ extern "C" int prism_stack_tokens_per_frame(const prism_stack* st) { return st ?
 extern "C" int prism_stack_launch_count(const prism_stack* st, int frames) {
     if (!st || frames <= 0) return 0;
     int n = (st->desc.up_w >= 0 ? 1 : 0) + (st->desc.down_w >= 0 ? 1 : 0);
-    // MoE: attention (+ router on the CUDA-core path), routing, experts; dense: attention, FFN
-    for (const auto& b : st->blocks) n += b.d.kind == PRISM_BLOCK_MOE ? (st->tc ? 3 : 4) : 2;
+    // MoE (dim 256): attention with the fused router, routing, experts; dense: attention, FFN
+    for (const auto& b : st->blocks) n += b.d.kind == PRISM_BLOCK_MOE ? 3 : 2;
     if (st->desc.down_w < 0 && st->blocks.empty()) n += 1;  // plain copy
     return n;
 }
@@ -862,12 +862,12 @@ extern "C" int prism_stack_forward(prism_stack* st, const void* in, void* out, i
             cur_map = nxt_map;
             continue;
         }
-        // dim 128: CUDA-core attention + dense FFN
+        // dim 128 (dense blocks only: MoE blocks need dim 256): CUDA-core attention into the
+        // next buffer, then the CUDA-core dense FFN in place on it
         AttnArgs at;
         at.weights = st->blob;
         at.x = cur;
-        // dim 128 runs the CUDA-core dense FFN in place on the block output
-        at.y = (b.d.kind == PRISM_BLOCK_DENSE && !st->tc) ? nxt : st->act_y;
+        at.y = nxt;
         at.frame_stride = (int64_t)T * D;
         at.qkv_w = b.d.qkv_w;
         at.qkv_b = b.d.qkv_b;
@@ -881,74 +881,17 @@ extern "C" int prism_stack_forward(prism_stack* st, const void* in, void* out, i
             KernelTimer kt(st, s, PRISM_K_ATTN);
             CUDA_TRY(launch_attn_window(at, D, frames, s));
         }
-        if (b.d.kind == PRISM_BLOCK_MOE) {
-            int32_t* asg = assign ? assign + (size_t)b.moe_index * rows : st->assign_ws;
-            RouterArgs ra;
-            ra.weights = st->blob;
-            ra.x = st->act_y;
-            ra.assign = asg;
-            ra.counts = st->counts;
-            ra.router_w = b.d.router_w;
-            ra.router_b = b.d.router_b;
-            ra.n_experts = b.d.n_experts;
-            ra.n_tokens = rows;
-            {
-                KernelTimer kt(st, s, PRISM_K_ROUTER);
-                CUDA_TRY(launch_router(ra, D, s));
-            }
-            RouteArgs ra_;
-            ra_.counts = st->counts;
-            ra_.counts_out = nullptr;
-            ra_.cursor = st->cursor;
-            ra_.assign = asg;
-            ra_.perm = st->perm;
-            ra_.tiles = st->tiles;
-            ra_.n_tiles = st->n_tiles;
-            ra_.n_experts = b.d.n_experts;
-            ra_.n_tokens = rows;
-            ra_.err = st->err;
-            {
-                KernelTimer kt(st, s, PRISM_K_ROUTE);
-                CUDA_TRY(launch_route(ra_, s));
-            }
-            FfnArgs fa{};
-            fa.x = st->act_y;
-            fa.y = nxt;
-            fa.perm = st->perm;
-            fa.tiles = st->tiles;
-            fa.n_tiles = st->n_tiles;
-            fa.b1 = b.b1;
-            fa.b2 = b.b2;
-            fa.err = st->err;
-            fa.route_counts = st->counts;
-            fa.route_cursor = st->cursor;
-            fa.n_route = b.d.n_experts;
-            KernelTimer kt(st, s, PRISM_K_EXPERT);
-            fa.n_rows = (int)rows;
-            CUDA_TRY(launch_ffn_expert256(fa, b.tm_w1, b.tm_w2,
-                                          std::min(grid, rows / 128 + b.d.n_experts), s));
-        } else if (st->tc) {
-            FfnArgs fa{};
-            fa.x = st->act_y;
-            fa.y = nxt;
-            fa.n_rows = rows;
-            fa.b1 = b.b1;
-            fa.b2 = b.b2;
-            fa.err = st->err;
-            KernelTimer kt(st, s, PRISM_K_DENSE_FFN);
-            CUDA_TRY(launch_ffn_dense256(fa, st->tm_act_y, b.tm_w1, b.tm_w2, b.d.ffn_hidden / 256,
-                                         std::min(grid, (rows + 127) / 128), s));
-        } else {
-            DenseFfnArgs f;
-            f.weights = st->blob;
-            f.io = nxt;
-            f.w1 = b.d.ffn_w1;
-            f.b1 = b.d.ffn_b1;
-            f.w2 = b.d.ffn_w2;
-            f.b2 = b.d.ffn_b2;
-            f.hidden = b.d.ffn_hidden;
-            f.chunk = b.d.ffn_chunk;
-            f.n_tokens = rows;
+        DenseFfnArgs f;
+        f.weights = st->blob;
+        f.io = nxt;
+        f.w1 = b.d.ffn_w1;
+        f.b1 = b.d.ffn_b1;
+        f.w2 = b.d.ffn_w2;
+        f.b2 = b.d.ffn_b2;
+        f.hidden = b.d.ffn_hidden;
+        f.chunk = b.d.ffn_chunk;
+        f.n_tokens = rows;
+        {
             KernelTimer kt(st, s, PRISM_K_DENSE_FFN);
             CUDA_TRY(launch_dense_ffn(f, D, s));
         }
