@@ -236,6 +236,19 @@ int prism_stack_destroy(prism_stack* st);
 int prism_stack_forward(prism_stack* st, const void* in, void* out, int frames,
                         int32_t* assign, void* stream);
 
+/* Fast path of one MoE block on the caller's arenas: the reference's per-block dispatch
+ * sequence attn (ci -> f_attn), router (f_attn), experts (f_attn -> co)
+ * (prism_moe_bench.cpp:414-438) as the fused tcgen05 kernels of prism_stack_forward.  blk is a
+ * stack of exactly one MoE block without adapters (prism_stack_create holds its repacked
+ * weights), else PRISM_E_ARG.  features_in / features_out: device [frames][T][dim] fp16,
+ * typically the caller's feature arena at the pass's input and output offsets (must not
+ * overlap).  assign (nullable): device int32 [frames*T], the routing (the router's
+ * assignment_offset); counts (nullable): device int32 [n_experts], the tokens each expert
+ * received (the router's count_offset; overwritten, where the reference's atomics add to
+ * whatever the arena held).  Stream-ordered, no host synchronisation, graph capturable. */
+int prism_moe_block(prism_stack* blk, const void* features_in, void* features_out, int frames,
+                    int32_t* assign, int32_t* counts, void* stream);
+
 /* Host-buffer inference, the counterpart of PrismVulkan::Infer (prism_vulkan.h:90-91,
  * prism_vulkan.cpp:1007-1040: upload, run, wait, download, return the GPU time).
  * host_in: host [frames][T][in_dim] fp16; host_out: host [frames][T][out_dim] fp16, or

@@ -133,6 +133,16 @@ class Stack:
                                                      _stream(stream)))
         return out
 
+    def moe_block(self, x, out, assign=None, counts=None, stream=None):
+        """prism_moe_block (a stack of one MoE block, no adapters): x / out CUDA fp16
+        [F, T, dim] (views into a feature arena work), assign CUDA int32 [F*T] and counts
+        CUDA int32 [n_experts], both optional."""
+        check(self.lib, self.lib.prism_moe_block(self.h, _ptr(x), _ptr(out), x.shape[0],
+                                                 _ptr(assign) if assign is not None else None,
+                                                 _ptr(counts) if counts is not None else None,
+                                                 _stream(stream)))
+        return out
+
     def infer(self, host_in, host_out=None) -> float:
         """prism_stack_infer: host_in [F, T, in_dim] / host_out [F, T, out_dim] fp16 host
         arrays (CPU tensors, page-locked for DMA, or numpy arrays); synchronous.  Returns

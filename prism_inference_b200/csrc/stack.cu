@@ -739,8 +739,12 @@ extern "C" int prism_stack_inject_stall(prism_stack* st, void* stream) {
     return PRISM_OK;
 }
 
-extern "C" int prism_stack_forward(prism_stack* st, const void* in, void* out, int frames, int32_t* assign,
-                                   void* stream) {
+namespace {
+
+// The whole stack; counts_out (nullable, one-MoE-block stacks) receives the block's per-expert
+// token counts as the routing kernel reads them.
+int stack_forward(prism_stack* st, const void* in, void* out, int frames, int32_t* assign, int32_t* counts_out,
+                  void* stream) {
     if (!st) return fail(PRISM_E_ARG, "prism_stack_forward: NULL stack");
     if (frames < 0 || frames > st->max_frames)
         return fail(PRISM_E_RANGE, "prism_stack_forward: frames %d (max %d)", frames, st->max_frames);
@@ -817,7 +821,7 @@ extern "C" int prism_stack_forward(prism_stack* st, const void* in, void* out, i
             if (b.d.kind == PRISM_BLOCK_MOE) {
                 RouteArgs ra_;
                 ra_.counts = st->counts;
-                ra_.counts_out = nullptr;
+                ra_.counts_out = counts_out;
                 ra_.cursor = st->cursor;
                 ra_.assign = asg;
                 ra_.perm = st->perm;
@@ -918,6 +922,22 @@ extern "C" int prism_stack_forward(prism_stack* st, const void* in, void* out, i
         CUDA_TRY(cudaMemcpyAsync(out, cur, (size_t)rows * D * 2, cudaMemcpyDeviceToDevice, s));
     }
     return PRISM_OK;
+}
+
+}  // namespace
+
+extern "C" int prism_stack_forward(prism_stack* st, const void* in, void* out, int frames, int32_t* assign,
+                                   void* stream) {
+    return stack_forward(st, in, out, frames, assign, nullptr, stream);
+}
+
+extern "C" int prism_moe_block(prism_stack* blk, const void* features_in, void* features_out, int frames,
+                               int32_t* assign, int32_t* counts, void* stream) {
+    if (!blk) return fail(PRISM_E_ARG, "prism_moe_block: NULL block");
+    if (blk->desc.n_blocks != 1 || blk->desc.blocks[0].kind != PRISM_BLOCK_MOE || blk->desc.up_w >= 0 ||
+        blk->desc.down_w >= 0)
+        return fail(PRISM_E_ARG, "prism_moe_block: the handle must hold exactly one MoE block and no adapters");
+    return stack_forward(blk, features_in, features_out, frames, assign, counts, stream);
 }
 
 // ---- host-buffer inference -------------------------------------------------------------

@@ -222,6 +222,43 @@ def test_stack_zero_frames_is_a_no_op(prism_ctx):
     assert (o1.view(np.uint16) == o2.view(np.uint16)).all() and (a1 == a2).all()
 
 
+def test_moe_block_on_caller_arenas(prism_ctx, oracle):
+    """prism_moe_block on views into one feature arena and one aux arena at the reference's
+    pass offsets (input, output, assignments, counts): the block's output matches the oracle,
+    the counts are the histogram of the assignments, and the arena outside the output is
+    untouched.  A handle with adapters or more blocks is refused."""
+    import torch
+    from prism_inference_b200.abi import PrismError
+    cfg = configs.get("moe16x1")
+    L = cfg.layout
+    T = L.tokens
+    blob = synth.make_blob(L)
+    x = synth.make_frames(L, 1)
+    blk = Stack(prism_ctx, L, blob, 1)
+    arena = torch.full((3 * T * 256,), 5.0, dtype=torch.float16, device="cuda")
+    arena[:T * 256] = torch.from_numpy(x.reshape(-1).view(np.int16)).cuda().view(torch.float16)
+    aux = torch.full((T + 64,), -7, dtype=torch.int32, device="cuda")
+    xin = arena[:T * 256].view(1, T, 256)
+    xout = arena[2 * T * 256:].view(1, T, 256)
+    blk.moe_block(xin, xout, aux[:T], aux[T:T + 16])
+    torch.cuda.synchronize()
+    blk.status()
+    a = aux[:T].cpu().numpy()
+    counts = aux[T:T + 16].cpu().numpy()
+    assert (counts == np.bincount(a, minlength=16)).all()
+    assert (aux[T + 16:] == -7).all() and (arena[T * 256:2 * T * 256] == 5.0).all()
+    o = xout.view(torch.int16).cpu().numpy().view(np.float16)
+    ref, _, stats = oracle.stack(L, blob, x, forced=a[None], tie_thr=TIE_MARGIN)
+    assert stats[2] == 0
+    assert_close(o, ref, "prism_moe_block")
+    blk.close()
+    L2 = layout.build_stack(256, 1, n_experts=16, up_adapter=True, down_adapter=True)
+    st = Stack(prism_ctx, L2, synth.make_blob(L2), 1)
+    with pytest.raises(PrismError, match="ARG"):
+        st.moe_block(xin, xout)
+    st.close()
+
+
 def test_host_buffer_infer_and_pipelined_submit(prism_ctx):
     """prism_stack_infer (the reference's Infer: host in, host out, GPU ms) and the pipelined
     prism_stack_submit / prism_stack_wait give prism_stack_forward's bits: pageable numpy and
