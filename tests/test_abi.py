@@ -87,3 +87,25 @@ def test_null_arguments_rejected(lib):
     assert rc == abi.PRISM_E_ARG
     assert b"NULL" in lib.prism_last_error_string()
     assert lib.prism_stack_forward(None, None, None, 1, None, None) == abi.PRISM_E_ARG
+
+
+def test_null_handles_rejected_by_every_stack_call(lib):
+    """Each stack entry point answers a NULL handle with PRISM_E_ARG (and a message) instead of
+    touching it; none needs a GPU to do so."""
+    f = C.c_float()
+    t = C.c_int64()
+    calls = {
+        "prism_stack_status": lambda: lib.prism_stack_status(None, None),
+        "prism_stack_inject_stall": lambda: lib.prism_stack_inject_stall(None, None),
+        "prism_moe_block": lambda: lib.prism_moe_block(None, None, None, 1, None, None, None),
+        "prism_stack_infer": lambda: lib.prism_stack_infer(None, None, None, 1, C.byref(f)),
+        "prism_stack_submit": lambda: lib.prism_stack_submit(None, None, None, 1, None, C.byref(t)),
+        "prism_stack_wait": lambda: lib.prism_stack_wait(None, 0, None),
+        "prism_stack_profile": lambda: lib.prism_stack_profile(None, 1),
+    }
+    for name, call in calls.items():
+        assert call() == abi.PRISM_E_ARG, name
+        assert lib.prism_last_error_string(), name
+    assert lib.prism_stack_destroy(None) == abi.PRISM_OK  # like free(NULL)
+    assert lib.prism_stack_launch_count(None, 4) == 0
+    assert lib.prism_stack_tokens_per_frame(None) == 0
