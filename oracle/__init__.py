@@ -26,7 +26,16 @@ LIB = ORACLE_DIR / "liboracle.so"
 REF_LIB = ORACLE_DIR / "_ref" / "libglsl_ref.so"
 REF_SHADERS = ("split2_qkv_attn_d256", "moe_router", "moe_expert_skip", "moe_ffn_16exp",
                "pw_project_128to256", "pw_project_256to128", "attention_windowed_d256",
-               "attention_windowed")
+               "attention_windowed",
+               # the encoder / decoder around the stack (prism_moe_bench.cpp:386-471)
+               "conv3x3_coopvec_9ch", "strided_conv_coopvec_32ch", "strided_conv_split_64ch",
+               "strided_conv_split_128ch", "dec3_fused", "dec2_fused", "dec1_fused",
+               "pw_conv_coopvec_32to12", "pixelshuffle_sigmoid")
+
+# order of enum oracle_codec_kind (prism_oracle.h)
+CODEC_KINDS = ("conv3x3_coopvec_9ch", "strided_conv_coopvec_32ch", "strided_conv_split_64ch",
+               "strided_conv_split_128ch", "dec3_fused", "dec2_fused", "dec1_fused",
+               "pw_conv_coopvec_32to12", "pixelshuffle_sigmoid")
 
 _u16p = np.ctypeslib.ndpointer(dtype=np.uint16, flags="C_CONTIGUOUS")
 _i32p = np.ctypeslib.ndpointer(dtype=np.int32, flags="C_CONTIGUOUS")
@@ -55,6 +64,8 @@ class Oracle:
         L.oracle_f2h.argtypes, L.oracle_f2h.restype = [C.c_float], C.c_uint16
         L.oracle_h2f.argtypes, L.oracle_h2f.restype = [C.c_uint16], C.c_float
         L.oracle_gelu_h.argtypes, L.oracle_gelu_h.restype = [C.c_float], C.c_float
+        L.oracle_codec_pass.argtypes = [C.c_int, _i32p, C.c_int, _u16p, _u16p, C.c_void_p]
+        L.oracle_codec_pass.restype = C.c_int
         L.oracle_num_threads.restype = C.c_int
         L.oracle_set_num_threads.argtypes = [C.c_int]
         self.lib = L
@@ -101,6 +112,15 @@ class Oracle:
             raise RuntimeError("oracle_stack_forward: invalid descriptor")
         return out, assign, stats
 
+    def codec_pass(self, shader: str, push, weights, features, rgb=None):
+        """One encoder / decoder pass (CODEC_KINDS) with the shader's push constants, on the
+        feature arena in place; rgb receives pixelshuffle_sigmoid's output."""
+        pc = np.ascontiguousarray(np.asarray(push, dtype=np.int32))
+        rc = self.lib.oracle_codec_pass(CODEC_KINDS.index(shader), pc, pc.size, _u16(weights), _u16(features),
+                                        _u16(rgb).ctypes.data if rgb is not None else None)
+        if rc != 0:
+            raise ValueError(f"oracle_codec_pass({shader}): bad push constants")
+
     def f2h(self, x):
         return self.lib.oracle_f2h(x)
 
@@ -134,16 +154,27 @@ class GlslRef:
             n.restype = C.c_int
             ls = getattr(L, f"glslref_{s}_local_size")
             ls.restype = C.c_int
-            self.fns[s] = (f, n(), ls())
+            ly = getattr(L, f"glslref_{s}_local_size_y")
+            ly.restype = C.c_int
+            if ly() > 1:  # 2-D workgroups: the _2d entry takes the group grid
+                f = getattr(L, f"glslref_{s}_2d")
+                f.argtypes = [_i32p, C.c_int, _u16p, _u16p, C.c_void_p, C.c_int, C.c_int]
+                f.restype = C.c_int
+            self.fns[s] = (f, n(), ls(), ly())
         self.lib = L
 
-    def dispatch(self, shader: str, push, weights, features, aux=None, n_groups: int = 1):
-        f, n_push, _ = self.fns[shader]
+    def dispatch(self, shader: str, push, weights, features, aux=None, n_groups=1):
+        """n_groups: an int, or (groups_x, groups_y) for a shader with 2-D workgroups.  aux is
+        binding 2 (int32 for the router / experts, fp16 for pixelshuffle's RGB output)."""
+        f, n_push, _, ly = self.fns[shader]
         pc = np.ascontiguousarray(np.asarray(push, dtype=np.int32))
         if pc.size != n_push:
             raise ValueError(f"{shader}: {n_push} push constants expected, got {pc.size}")
+        grid = tuple(n_groups) if isinstance(n_groups, (tuple, list)) else (n_groups,)
+        if (len(grid) == 2) != (ly > 1):
+            raise ValueError(f"{shader}: workgroup grid {grid} does not match its workgroup shape")
         rc = f(pc, pc.size, _u16(weights), _u16(features),
-               aux.ctypes.data if aux is not None else None, n_groups)
+               aux.ctypes.data if aux is not None else None, *grid)
         if rc != 0:
             raise RuntimeError(f"{shader}: dispatch failed")
 

@@ -161,6 +161,22 @@ inline void run_group(unsigned g, unsigned L, bool uses_barrier, void (*fn)()) {
     }
 }
 
+// 2-D workgroups (no barrier): group (gx, gy) of a groups_x x groups_y grid, invocation
+// (ix, iy) of an Lx x Ly workgroup.
+inline void run_groups_2d(int groups_x, int groups_y, int Lx, int Ly, void (*fn)()) {
+#pragma omp parallel for schedule(dynamic, 1)
+    for (int g = 0; g < groups_x * groups_y; ++g) {
+        const unsigned gx = (unsigned)(g % groups_x), gy = (unsigned)(g / groups_x);
+        for (unsigned iy = 0; iy < (unsigned)Ly; ++iy)
+            for (unsigned ix = 0; ix < (unsigned)Lx; ++ix) {
+                gl_WorkGroupID = {gx, gy, 0};
+                gl_LocalInvocationID = {ix, iy, 0};
+                gl_GlobalInvocationID = {gx * Lx + ix, gy * Ly + iy, 0};
+                fn();
+            }
+    }
+}
+
 inline void run_groups(int n_groups, int L, bool uses_barrier, void (*fn)()) {
 #pragma omp parallel for schedule(dynamic, 1)
     for (int g = 0; g < n_groups; ++g) run_group((unsigned)g, (unsigned)L, uses_barrier, fn);

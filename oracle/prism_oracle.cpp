@@ -425,4 +425,142 @@ int oracle_stack_forward(const prism_stack_desc* d, const uint16_t* blob, size_t
     return 0;
 }
 
+// ---- encoder / decoder passes (CHW feature maps) ---------------------------------------
+// Each follows its shader line by line; MV() is the coopVecMatMulAddNV model above, on one
+// gathered input vector.  The shaders fix their channel counts in the code (loop bounds and
+// coopvec sizes); their in/out/up/skip-channel push constants are not read, so neither are
+// they here.
+
+namespace {
+
+// h( sum_k W[r*ld + k] * v[k] + b[r] ) for r < M, fp32 accumulator in k order, bias last.
+void mv_vec(const uint16_t* W, int ld, const uint16_t* b, int M, int K, const float* v, uint16_t* out) {
+    for (int r = 0; r < M; ++r) {
+        const uint16_t* wr = W + (size_t)r * ld;
+        float acc = 0.0f;
+        for (int k = 0; k < K; ++k) acc += h2f(wr[k]) * v[k];
+        out[r] = f2h(acc + h2f(b[r]));
+    }
+}
+
+// 3x3 patch of channels [c0, c0 + nc) around (cy, cx), zero outside the map, in the order
+// the shaders gather it: channel, then ky, then kx (e.g. strided_conv_split_64ch.comp.glsl:43-55).
+void gather3x3(const uint16_t* F, int in_off, int c0, int nc, int in_w, int in_h, int cy, int cx, float* v) {
+    const size_t in_px = (size_t)in_w * in_h;
+    int p = 0;
+    for (int ic = c0; ic < c0 + nc; ++ic)
+        for (int ky = -1; ky <= 1; ++ky)
+            for (int kx = -1; kx <= 1; ++kx) {
+                const int iy = cy + ky, ix = cx + kx;
+                v[p++] = (iy >= 0 && iy < in_h && ix >= 0 && ix < in_w)
+                             ? h2f(F[in_off + ic * in_px + (size_t)iy * in_w + ix])
+                             : 0.0f;
+            }
+}
+
+inline uint16_t relu_h(uint16_t v) { return h2f(v) < 0.0f ? f2h(0.0f) : v; }  // `if (v < 0) v = 0` on fp16
+
+}  // namespace
+
+int oracle_codec_pass(int kind, const int32_t* push, int n_push, const uint16_t* W, uint16_t* F, uint16_t* rgb) {
+    static const int kPush[9] = {9, 10, 10, 10, 10, 11, 11, 9, 7};
+    if (kind < 0 || kind > 8 || n_push != kPush[kind]) return -1;
+    const int* q = push;
+    if (kind == ORACLE_CONV3X3_9CH || kind == ORACLE_PW_32TO12) {
+        // conv3x3_coopvec_9ch.comp.glsl:27-59 (3x3, stride 1) / pw_conv_coopvec_32to12.comp.glsl:24-45
+        const int w = q[2], h = q[3], wo = q[4], bo = q[5], in_off = q[6], out_off = q[7], relu = q[8];
+        const bool conv = kind == ORACLE_CONV3X3_9CH;
+        const int in_ch = conv ? 9 : 32, out_ch = conv ? 32 : 12;
+        const int px = w * h, K = conv ? in_ch * 9 : in_ch;
+#pragma omp parallel for schedule(static)
+        for (int idx = 0; idx < px; ++idx) {
+            std::vector<float> v(K);
+            std::vector<uint16_t> o(out_ch);
+            if (kind == ORACLE_CONV3X3_9CH) gather3x3(F, in_off, 0, in_ch, w, h, idx / w, idx % w, v.data());
+            else
+                for (int c = 0; c < in_ch; ++c) v[c] = h2f(F[in_off + (size_t)c * px + idx]);
+            mv_vec(W + wo, K, W + bo, out_ch, K, v.data(), o.data());
+            for (int c = 0; c < out_ch; ++c)
+                F[out_off + (size_t)c * px + idx] = relu == 1 ? relu_h(o[c]) : o[c];
+        }
+        return 0;
+    }
+    if (kind <= ORACLE_STRIDED_SPLIT_128CH) {
+        // stride-2 3x3 convs over 32-channel groups of the input
+        const int in_w = q[2], in_h = q[3], out_w = q[4], out_h = q[5], wo = q[6], bo = q[7], in_off = q[8],
+                  out_off = q[9];
+        // 32 -> 64 in one product; 64 -> 128 and 128 -> 128 in 32-channel groups
+        const int in_ch = kind == ORACLE_STRIDED_CONV_32CH ? 32 : kind == ORACLE_STRIDED_SPLIT_64CH ? 64 : 128;
+        const int out_ch = kind == ORACLE_STRIDED_CONV_32CH ? 64 : 128;
+        const int out_px = out_w * out_h;
+        const int groups = kind == ORACLE_STRIDED_CONV_32CH ? 1 : in_ch / 32;
+        const int Kg = (in_ch / groups) * 9, ld = in_ch * 9;
+#pragma omp parallel for schedule(static)
+        for (int idx = 0; idx < out_px; ++idx) {
+            const int cy = (idx / out_w) * 2, cx = (idx % out_w) * 2;
+            std::vector<float> v(Kg);
+            std::vector<uint16_t> part(out_ch), acc(out_ch);
+            std::vector<float> sum2(out_ch);
+            for (int g = 0; g < groups; ++g) {
+                gather3x3(F, in_off, g * (in_ch / groups), in_ch / groups, in_w, in_h, cy, cx, v.data());
+                mv_vec(W + wo + g * Kg, ld, W + bo, out_ch, Kg, v.data(), part.data());
+                for (int c = 0; c < out_ch; ++c) {
+                    if (kind == ORACLE_STRIDED_SPLIT_128CH) {
+                        // strided_conv_split_128ch.comp.glsl:81-86: fp16 running sum, bias removed per group
+                        acc[c] = g == 0 ? part[c] : f2h(h2f(acc[c]) + h2f(part[c]) - h2f(W[bo + c]));
+                    } else if (kind == ORACLE_STRIDED_SPLIT_64CH) {
+                        // strided_conv_split_64ch.comp.glsl:87-91: fp32 sum of the two products - bias
+                        if (g == 0) sum2[c] = h2f(part[c]);
+                        else sum2[c] = sum2[c] + h2f(part[c]) - h2f(W[bo + c]);
+                    } else {
+                        acc[c] = part[c];  // strided_conv_coopvec_32ch.comp.glsl: one product
+                    }
+                }
+            }
+            for (int c = 0; c < out_ch; ++c) {
+                uint16_t r;
+                if (kind == ORACLE_STRIDED_SPLIT_64CH) r = f2h(sum2[c] < 0.0f ? 0.0f : sum2[c]);
+                else r = relu_h(acc[c]);
+                F[out_off + (size_t)c * out_px + idx] = r;
+            }
+        }
+        return 0;
+    }
+    if (kind <= ORACLE_DEC1) {
+        // dec*_fused.comp.glsl: nearest-neighbour 2x upsample (clamped to the input map) of the
+        // deeper map, concatenated with the skip map, then a pointwise product and ReLU
+        // up + skip -> out channels: dec3 128 + 128 -> 128, dec2 128 + 64 -> 64, dec1 64 + 32 -> 32
+        const int up_ch = kind == ORACLE_DEC1 ? 64 : 128;
+        const int skip_ch = kind == ORACLE_DEC3 ? 128 : kind == ORACLE_DEC2 ? 64 : 32, out_ch = skip_ch;
+        const int out_w = q[0], out_h = q[1], in_w = q[2], in_h = q[3];
+        const int* r = kind == ORACLE_DEC3 ? q + 5 : q + 6;  // dec3 has no up_channels constant
+        const int wo = r[0], bo = r[1], in_off = r[2], skip_off = r[3], out_off = r[4];
+        const int out_px = out_w * out_h, in_px = in_w * in_h, K = up_ch + skip_ch;
+#pragma omp parallel for schedule(static)
+        for (int idx = 0; idx < out_px; ++idx) {
+            const int iy = std::min((idx / out_w) / 2, in_h - 1), ix = std::min((idx % out_w) / 2, in_w - 1);
+            std::vector<float> v(K);
+            std::vector<uint16_t> o(out_ch);
+            for (int c = 0; c < up_ch; ++c) v[c] = h2f(F[in_off + (size_t)c * in_px + iy * in_w + ix]);
+            for (int c = 0; c < skip_ch; ++c) v[up_ch + c] = h2f(F[skip_off + (size_t)c * out_px + idx]);
+            mv_vec(W + wo, K, W + bo, out_ch, K, v.data(), o.data());
+            for (int c = 0; c < out_ch; ++c) F[out_off + (size_t)c * out_px + idx] = relu_h(o[c]);
+        }
+        return 0;
+    }
+    // pixelshuffle_sigmoid.comp.glsl:26-56: display pixel (ox, oy) takes channel
+    // c*s*s + (oy%s)*s + ox%s of render pixel (ox/s, oy/s), through 1/(1+exp(-v)) in fp32
+    const int rw = q[0], rh_ = q[1], dw = q[2], dh = q[3], sc = q[4], in_off = q[5], out_off = q[6];
+    const size_t rpx = (size_t)rw * rh_;
+#pragma omp parallel for schedule(static)
+    for (int oy = 0; oy < dh; ++oy)
+        for (int ox = 0; ox < dw; ++ox)
+            for (int c = 0; c < 3; ++c) {
+                const int src_ch = c * sc * sc + (oy % sc) * sc + ox % sc;
+                const float v = h2f(F[in_off + src_ch * rpx + (size_t)(oy / sc) * rw + ox / sc]);
+                rgb[out_off + (size_t)c * dw * dh + (size_t)oy * dw + ox] = f2h(1.0f / (1.0f + expf(-v)));
+            }
+    return 0;
+}
+
 }  // extern "C"

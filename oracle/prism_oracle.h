@@ -66,6 +66,25 @@ int oracle_stack_forward(const prism_stack_desc* d, const uint16_t* blob, size_t
                          int32_t* assign_out, const int32_t* forced, float tie_thr,
                          int64_t* stats);
 
+/* The encoder / decoder around the stack (prism_moe_bench.cpp:386-471): one pass of the
+ * named shader on CHW feature maps, with the shader's push constants in declaration order
+ * (n_push of them) and its bindings: weights (binding 0), features (binding 1) and, for
+ * ORACLE_PIXELSHUFFLE only, the fp16 RGB output (binding 2).  Returns 0, or -1 for an
+ * unknown kind or a push-constant count that does not match the shader. */
+enum oracle_codec_kind {
+    ORACLE_CONV3X3_9CH = 0,        /* conv3x3_coopvec_9ch.comp.glsl       */
+    ORACLE_STRIDED_CONV_32CH = 1,  /* strided_conv_coopvec_32ch.comp.glsl */
+    ORACLE_STRIDED_SPLIT_64CH = 2, /* strided_conv_split_64ch.comp.glsl   */
+    ORACLE_STRIDED_SPLIT_128CH = 3,/* strided_conv_split_128ch.comp.glsl  */
+    ORACLE_DEC3 = 4,               /* dec3_fused.comp.glsl                */
+    ORACLE_DEC2 = 5,               /* dec2_fused.comp.glsl                */
+    ORACLE_DEC1 = 6,               /* dec1_fused.comp.glsl                */
+    ORACLE_PW_32TO12 = 7,          /* pw_conv_coopvec_32to12.comp.glsl    */
+    ORACLE_PIXELSHUFFLE = 8        /* pixelshuffle_sigmoid.comp.glsl      */
+};
+int oracle_codec_pass(int kind, const int32_t* push, int n_push, const uint16_t* weights,
+                      uint16_t* features, uint16_t* rgb);
+
 /* helpers exposed for tests */
 uint16_t oracle_f2h(float x);
 float oracle_h2f(uint16_t h);

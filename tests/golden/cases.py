@@ -1,4 +1,5 @@
-"""Golden cases: small seeded inputs for every reference shader on the hot path.
+"""Golden cases: small seeded inputs for every reference shader on the hot path, and for
+the encoder / decoder shaders around it (CODEC_CASES).
 
 Each case builds (shader, push constants, weight blob, feature arena, aux arena,
 workgroup count) deterministically from numpy PCG64 seeds, so the inputs are rebuilt
@@ -108,11 +109,97 @@ def build(name):
         return dict(shader="pw_project_256to128", push=[T, L.down_w, L.down_b, 0, T * 256], blob=blob,
                     feat=_arena(T * (256 + 128), x), aux=None, groups=(T + 255) // 256,
                     out=("feat", slice(T * 256, T * 384)))
+    if name in CODEC_CASES:
+        return _codec(name)
     raise KeyError(name)
 
 
+# ---- the encoder / decoder around the stack (prism_moe_bench.cpp:386-471), CHW feature maps.
+# A 24x14 frame and its stride-2 pyramid 12x7, 6x4, 3x2 (odd heights round up, as 135 -> 68
+# does in the reference).  Every case is one dispatch on its own seeded inputs.
+R = ((24, 14), (12, 7), (6, 4), (3, 2))
+P = tuple(w * h for w, h in R)
+
+
+def _codec_weights(rows, cols, seed):
+    """[rows][cols] row-major weights ~ N(0, 1/cols) followed by [rows] biases ~ N(0, 0.1)."""
+    rng = np.random.Generator(np.random.PCG64(seed))
+    w = (rng.standard_normal(rows * cols, dtype=np.float32) / np.float32(np.sqrt(cols))).astype(np.float16)
+    b = (rng.standard_normal(rows, dtype=np.float32) * np.float32(0.1)).astype(np.float16)
+    return np.concatenate([w, b]), 0, rows * cols
+
+
+def _codec_features(sizes, seed):
+    rng = np.random.Generator(np.random.PCG64(seed))
+    return [rng.standard_normal(n, dtype=np.float32).astype(np.float16) for n in sizes]
+
+
+def _codec(name):
+    (w0, h0), (w1, h1), (w2, h2), (w3, h3) = R
+    p0, p1, p2, p3 = P
+    g = lambda n: (n + 255) // 256  # noqa: E731
+    if name == "enc_ic":  # conv3x3_coopvec_9ch: 9 -> 32, ReLU
+        blob, wo, bo = _codec_weights(32, 81, 21)
+        (x,) = _codec_features([9 * p0], 31)
+        return dict(shader="conv3x3_coopvec_9ch", push=[9, 32, w0, h0, wo, bo, 0, 9 * p0, 1], blob=blob,
+                    feat=_arena(9 * p0 + 32 * p0, x), aux=None, groups=g(p0), out=("feat", slice(9 * p0, 41 * p0)))
+    if name == "enc1":  # strided_conv_coopvec_32ch: 32 -> 64, stride 2
+        blob, wo, bo = _codec_weights(64, 288, 22)
+        (x,) = _codec_features([32 * p0], 32)
+        return dict(shader="strided_conv_coopvec_32ch", push=[32, 64, w0, h0, w1, h1, wo, bo, 0, 32 * p0],
+                    blob=blob, feat=_arena(32 * p0 + 64 * p1, x), aux=None, groups=g(p1),
+                    out=("feat", slice(32 * p0, 32 * p0 + 64 * p1)))
+    if name == "enc2":  # strided_conv_split_64ch: 64 -> 128, two 32-channel groups
+        blob, wo, bo = _codec_weights(128, 576, 23)
+        (x,) = _codec_features([64 * p1], 33)
+        return dict(shader="strided_conv_split_64ch", push=[64, 128, w1, h1, w2, h2, wo, bo, 0, 64 * p1],
+                    blob=blob, feat=_arena(64 * p1 + 128 * p2, x), aux=None, groups=g(p2),
+                    out=("feat", slice(64 * p1, 64 * p1 + 128 * p2)))
+    if name == "enc3":  # strided_conv_split_128ch: 128 -> 128, four groups, fp16 running sum
+        blob, wo, bo = _codec_weights(128, 1152, 24)
+        (x,) = _codec_features([128 * p2], 34)
+        return dict(shader="strided_conv_split_128ch", push=[128, 128, w2, h2, w3, h3, wo, bo, 0, 128 * p2],
+                    blob=blob, feat=_arena(128 * p2 + 128 * p3, x), aux=None, groups=g(p3),
+                    out=("feat", slice(128 * p2, 128 * p2 + 128 * p3)))
+    if name == "dec3":  # upsample 128 @ r3 + skip 128 @ r2 -> PW 256 -> 128, ReLU
+        blob, wo, bo = _codec_weights(128, 256, 25)
+        up, skip = _codec_features([128 * p3, 128 * p2], 35)
+        o = 128 * p3 + 128 * p2
+        return dict(shader="dec3_fused", push=[w2, h2, w3, h3, 128, wo, bo, 0, 128 * p3, o], blob=blob,
+                    feat=_arena(o + 128 * p2, np.concatenate([up, skip])), aux=None, groups=g(p2),
+                    out=("feat", slice(o, o + 128 * p2)))
+    if name == "dec2":  # upsample 128 @ r2 + skip 64 @ r1 -> PW 192 -> 64, ReLU
+        blob, wo, bo = _codec_weights(64, 192, 26)
+        up, skip = _codec_features([128 * p2, 64 * p1], 36)
+        o = 128 * p2 + 64 * p1
+        return dict(shader="dec2_fused", push=[w1, h1, w2, h2, 128, 64, wo, bo, 0, 128 * p2, o], blob=blob,
+                    feat=_arena(o + 64 * p1, np.concatenate([up, skip])), aux=None, groups=g(p1),
+                    out=("feat", slice(o, o + 64 * p1)))
+    if name == "dec1":  # upsample 64 @ r1 + skip 32 @ r0 -> PW 96 -> 32, ReLU
+        blob, wo, bo = _codec_weights(32, 96, 27)
+        up, skip = _codec_features([64 * p1, 32 * p0], 37)
+        o = 64 * p1 + 32 * p0
+        return dict(shader="dec1_fused", push=[w0, h0, w1, h1, 64, 32, wo, bo, 0, 64 * p1, o], blob=blob,
+                    feat=_arena(o + 32 * p0, np.concatenate([up, skip])), aux=None, groups=g(p0),
+                    out=("feat", slice(o, o + 32 * p0)))
+    if name == "out12":  # pw_conv_coopvec_32to12, no activation
+        blob, wo, bo = _codec_weights(12, 32, 28)
+        (x,) = _codec_features([32 * p0], 38)
+        return dict(shader="pw_conv_coopvec_32to12", push=[32, 12, w0, h0, wo, bo, 0, 32 * p0, 0], blob=blob,
+                    feat=_arena(32 * p0 + 12 * p0, x), aux=None, groups=g(p0),
+                    out=("feat", slice(32 * p0, 44 * p0)))
+    if name == "pixelshuffle":  # 12 channels @ r0 -> RGB @ 2x, sigmoid; output in binding 2 (fp16)
+        (x,) = _codec_features([12 * p0], 39)
+        rgb = np.zeros(3 * 4 * p0, np.float16)
+        return dict(shader="pixelshuffle_sigmoid", push=[w0, h0, 2 * w0, 2 * h0, 2, 0, 0],
+                    blob=np.zeros(8, np.float16), feat=_arena(12 * p0, x), aux=rgb,
+                    groups=((2 * w0 + 15) // 16, (2 * h0 + 15) // 16), out=("aux", slice(0, 12 * p0)))
+    raise KeyError(name)
+
+
+CODEC_CASES = ("enc_ic", "enc1", "enc2", "enc3", "dec3", "dec2", "dec1", "out12", "pixelshuffle")
 CASES = ("attn_d256", "attn_d256_16tok", "router4", "expert_skip4", "moe_ffn_16exp", "dense_d256_h1024",
-         "dense_d128_h512", "proj_up", "proj_down")
+         "dense_d128_h512", "proj_up", "proj_down") + CODEC_CASES
 
 
 def input_digest(case) -> str:
