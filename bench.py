@@ -18,7 +18,8 @@ max over ranks).  e2e: the same metric through the C ABI's host-buffer call
 of every step's frames and the device->host copy of every step's output are inside the timed
 region, overlapped across neighbouring steps by the library's two staging slots as a serving
 loop runs.  roofline: the kernel kind with the largest share of the
-timed region, its algorithmic FLOPs per launch / its mean event-timed duration,
+timed region, its algorithmic FLOPs per launch (the attention kernel's include the router GEMM
+fused into it) / its mean event-timed duration,
 against the sustained cuBLAS bf16 figure of MEASURED_PEAKS.json.
 
 --impl reference: the reference's own implementation of the path on the host cores:
@@ -144,9 +145,14 @@ def kind_flops_per_frame(L, kind):
     moe = [b for b in L.blocks if b.kind == "moe"]
     dense = [b for b in L.blocks if b.kind == "dense"]
     if kind == "attn":
-        return T * (2.0 * 4 * D * D + 2.0 * 2 * 64 * D)
-    if kind == "router":
-        return T * 2.0 * moe[0].n_experts * D if moe else 0.0
+        # QKV, QK^T and PV over 64 keys, out-projection; on the tensor-core path (dim 256) the
+        # MoE router GEMM runs inside the same kernel
+        f = T * (2.0 * 4 * D * D + 2.0 * 2 * 64 * D)
+        if moe and D == 256:
+            f += T * 2.0 * moe[0].n_experts * D
+        return f
+    if kind == "router":  # the separate CUDA-core router (dim 128 only)
+        return T * 2.0 * moe[0].n_experts * D if moe and D != 256 else 0.0
     if kind == "expert":
         return T * 2.0 * 2 * D * D
     if kind == "dense_ffn":
