@@ -146,10 +146,11 @@ def kind_flops_per_frame(L, kind):
     dense = [b for b in L.blocks if b.kind == "dense"]
     if kind == "attn":
         # QKV, QK^T and PV over 64 keys, out-projection; on the tensor-core path (dim 256) the
-        # MoE router GEMM runs inside the same kernel
+        # MoE router GEMM runs inside the attention launch of each MoE block, so the mean
+        # launch carries the router FLOPs of the MoE blocks spread over all attention launches
         f = T * (2.0 * 4 * D * D + 2.0 * 2 * 64 * D)
         if moe and D == 256:
-            f += T * 2.0 * moe[0].n_experts * D
+            f += T * 2.0 * sum(b.n_experts for b in moe) * D / len(L.blocks)
         return f
     if kind == "router":  # the separate CUDA-core router (dim 128 only)
         return T * 2.0 * moe[0].n_experts * D if moe and D != 256 else 0.0

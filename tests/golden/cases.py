@@ -198,8 +198,10 @@ def _codec(name):
 
 
 CODEC_CASES = ("enc_ic", "enc1", "enc2", "enc3", "dec3", "dec2", "dec1", "out12", "pixelshuffle")
-CASES = ("attn_d256", "attn_d256_16tok", "router4", "expert_skip4", "moe_ffn_16exp", "dense_d256_h1024",
-         "dense_d128_h512", "proj_up", "proj_down") + CODEC_CASES
+# the transformer-stack passes (the hot path); the codec passes run through their own tests
+HOT_CASES = ("attn_d256", "attn_d256_16tok", "router4", "expert_skip4", "moe_ffn_16exp", "dense_d256_h1024",
+             "dense_d128_h512", "proj_up", "proj_down")
+CASES = HOT_CASES + CODEC_CASES
 
 
 def input_digest(case) -> str:

@@ -12,9 +12,19 @@ import bench  # noqa: E402
 from prism_inference_b200 import configs  # noqa: E402
 
 
-@pytest.mark.parametrize("key", configs.ALL)
+def _mixed_layout():
+    """Dense and MoE blocks at dim 256 in one stack (no configuration mixes them, the FLOP
+    attribution must still add up)."""
+    from prism_inference_b200 import layout
+    L = layout.build_stack(256, 3, n_experts=32, up_adapter=True, down_adapter=True)
+    D = layout.build_stack(256, 2, ffn_hidden=1024, ffn_chunk=256)
+    L.blocks = [L.blocks[0], D.blocks[0], L.blocks[1], D.blocks[1], L.blocks[2]]
+    return L
+
+
+@pytest.mark.parametrize("key", configs.ALL + ("mixed",))
 def test_kernel_flops_add_up_to_the_layout(key):
-    L = configs.get(key).layout
+    L = _mixed_layout() if key == "mixed" else configs.get(key).layout
     moe = sum(b.kind == "moe" for b in L.blocks)
     dense = len(L.blocks) - moe
     launches = {"attn": len(L.blocks), "router": moe, "expert": moe, "dense_ffn": dense,

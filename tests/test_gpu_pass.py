@@ -11,7 +11,7 @@ from prism_inference_b200.abi import AttnParams, DenseParams, ExpertParams, Pris
 
 GOLD = Path(__file__).resolve().parent / "golden"
 sys.path.insert(0, str(GOLD))
-from cases import CASES, build, output_of  # noqa: E402
+from cases import HOT_CASES, build, output_of  # noqa: E402
 
 pytestmark = pytest.mark.gpu
 
@@ -66,7 +66,7 @@ def run_gpu(ctx, c):
     return output_of(c)
 
 
-@pytest.mark.parametrize("name", CASES)
+@pytest.mark.parametrize("name", HOT_CASES)
 def test_pass_matches_reference_golden(prism_ctx, name):
     gold = np.load(GOLD / "golden.npz")[name]
     got = run_gpu(prism_ctx, build(name))

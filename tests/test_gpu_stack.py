@@ -98,6 +98,36 @@ def test_headline_stack_full_depth(prism_ctx, oracle):
     _check(prism_ctx, oracle, cfg.layout, blob, x, "moe64x16-full")
 
 
+def _truncated(L, k):
+    """The first k blocks of L over the same blob, without the down adapter (dim-256 output):
+    the stack's state after block k."""
+    import copy
+    T = copy.deepcopy(L)
+    T.blocks = T.blocks[:k]
+    T.down_w, T.down_b, T.out_dim = -1, -1, T.dim
+    return T
+
+
+@pytest.mark.parametrize("seed", [1, 2, 3, 4])
+def test_headline_stack_seeds_and_depth(prism_ctx, oracle, seed):
+    """Config 4 at full depth on four more weight and input seeds, with the error after
+    blocks 1, 2, 4, 8 and 16 reported (each a truncated stack over the same blob, checked
+    against the oracle with its own routing): the margin to the tolerance at every depth."""
+    cfg = configs.get("moe64x16")
+    L = cfg.layout
+    blob = synth.make_blob(L, seed=synth.WEIGHT_SEED + 7919 * seed)
+    x = synth.make_frames(L, 1, first=101 * seed)
+    rows = []
+    for k in (1, 2, 4, 8, 16):
+        o, a = _run(prism_ctx, _truncated(L, k), blob, x)
+        ref, _, stats = oracle.stack(_truncated(L, k), blob, x, forced=a, tie_thr=TIE_MARGIN)
+        assert stats[2] == 0, f"seed {seed}, {k} blocks: {stats[2]} hard routing mismatches"
+        m = assert_close(o, ref, f"seed {seed}, after block {k}")
+        rows.append(f"{k}:{m[0]:.2g}/{m[1]:.2g}")
+    _check(prism_ctx, oracle, L, blob, x, f"moe64x16-full seed {seed}")
+    print(f"seed {seed} max_abs/rel_l2 by depth: " + " ".join(rows))
+
+
 def test_skewed_config_full_depth(prism_ctx, oracle):
     """Config 5 at its full depth: 32 experts x 22 blocks + adapters, about half of the
     tokens routed to 4 experts (long expert segments, many full tiles of one expert)."""

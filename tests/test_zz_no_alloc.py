@@ -1,6 +1,6 @@
 """prism_expert_all_static - all experts of one MoE pass without any device
 allocation - against the reference-style loop of one prism_expert call per expert,
-through the C ABI.
+through the C ABI, and against the CPU oracle of moe_expert_skip.comp.glsl.
 
 This entry point exists for callers that cannot allocate device memory when the pass
 runs, such as a post-process hook inside a game's frame loop (the setting Prism is
@@ -62,16 +62,31 @@ def _per_expert_loop(ctx, blob, feat, aux, p, n_experts, stride):
     return _host(f)
 
 
-def test_static_expert_pass_matches_per_expert_calls(prism_ctx):
+def _oracle_loop(oracle, blob, feat, aux, p, n_experts, stride):
+    """The CPU restatement of moe_expert_skip.comp.glsl, one dispatch per expert."""
+    f = feat.copy()
+    for e in range(n_experts):
+        o = e * stride
+        q = ExpertParams(p.n_tokens, p.dim, e, p.w1_offset + o, p.b1_offset + o, p.w2_offset + o, p.b2_offset + o,
+                         p.input_offset, p.output_offset, p.assignment_offset)
+        oracle.expert(q, blob, f, aux)
+    return f
+
+
+def test_static_expert_pass_matches_per_expert_calls(prism_ctx, oracle):
     # two calls in a row on the shared scratch: a 64-expert frame, then 16 experts
-    # over 8 frames (65,280 tokens, just under the limit)
+    # over 8 frames (65,280 tokens, just under the limit); each checked against the
+    # per-expert entry point and against the CPU oracle
     for seed, n_experts, frames in ((1, 64, 1), (2, 16, 8)):
         blob, feat, aux, p, stride, T = _case(seed, n_experts, frames)
         ref = _per_expert_loop(prism_ctx, blob, feat, aux, p, n_experts, stride)
         w, f, a = _dev(blob), _dev(feat), _dev(aux)
         prism_ctx.expert_all_static(p, n_experts, stride, w, f, a)
         got = _host(f)
-        assert_close(got[T * 256:], ref[T * 256:], f"static expert pass, {n_experts} experts x {frames} frames")
+        what = f"static expert pass, {n_experts} experts x {frames} frames"
+        assert_close(got[T * 256:], ref[T * 256:], what + " vs prism_expert")
+        cpu = _oracle_loop(oracle, blob, feat, aux, p, n_experts, stride)
+        assert_close(got[T * 256:], cpu[T * 256:], what + " vs oracle")
         unowned = (aux < 0) | (aux >= n_experts)
         out = got[T * 256:].reshape(T, 256)
         assert (out[unowned] == np.float16(7.0)).all()
