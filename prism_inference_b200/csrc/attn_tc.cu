@@ -2,14 +2,16 @@
 //
 // Computes, for every 8x8 window of every frame, the first pass of a Prism MoE block
 // (split2_qkv_attn_d256.comp.glsl:24-79) and the router that follows it
-// (moe_router.comp.glsl:24-52 with N-wide logits, moe_ffn_16exp.comp.glsl:27-34):
+// (moe_router.comp.glsl:24-52 with N-wide logits, moe_ffn_16exp.comp.glsl:27-34), or the
+// attention half of a dense block (attention_windowed_d256.comp.glsl:54-141 at D = 256,
+// attention_windowed.comp.glsl:53-148 at D = 128, no router):
 //     y = x + Wo . MHA_window(x) + bo            (fp16, masked store of valid tokens)
 //     assign[t] = argmax_e (Wr . y + br)[e]      (first maximum), counts[e] += 1
 //
 // One persistent CTA per SM walks tiles of two windows (128 rows; row = window slot
 // li = 8*ty + tx, slots outside the frame are the reference's phantom zero tokens:
 // the 4-D TMA load zero-fills them and they take part as keys, :31-37, :60).
-// Per tile and head h (8 heads x 32):
+// Per tile and head h (D/32 heads x 32; the text below is for D = 256):
 //   QKV_h   TMEM[96]  = X[128x256] . Wqkv_h^T        (tcgen05, K = 256)
 //   drain   Q_h, K_h (fp16, K-major SW64) and V_h (fp16, key-major SW64: the MN-major B
 //           operand of PV, so it is stored like K, no transpose) to smem
@@ -44,22 +46,34 @@ namespace prism {
 namespace {
 
 constexpr int kThreads = 320;  // 10 warps
-constexpr int kStage = 49152;  // weight ring stage: up to 4 K-blocks x [96 rows][128 B], or [256][128 B]
 constexpr int kStages = 2;
 constexpr int kRouterRows = 96;  // router rows per ring stage
 
-// Head pair whose out-projection the MMA warp issues at head h: pair p = (2p, 2p + 1) at
-// head 2p + 2 (behind QKV_{2p+3}), the last pair after PV_7; -1 at the other heads.
-PRISM_DEV constexpr int po_pair(int h) { return h == 7 ? 3 : (h >= 2 && (h & 1) == 0) ? h / 2 - 1 : -1; }
+// Shapes of the kernel for model width D (256: the MoE / "Standard" blocks, 128: the
+// "Baseline" block, attention_windowed.comp.glsl): D / 64 K-blocks, D / 32 heads of 32.
+template <int D>
+struct AttnCfg {
+    static_assert(D == 128 || D == 256, "model width");
+    static constexpr int kKB = D / 64;      // 64-wide K-blocks of X, y and the weights
+    static constexpr int kHeads = D / 32;
+    // weight ring stage: a head's Wqkv rows at full K ([96][128 B] per K-block) or a pair's
+    // Wo columns ([D][128 B]); router rows at D = 256 (96 x 4 K-blocks)
+    static constexpr int kStage = 96 * 128 * kKB > D * 128 ? 96 * 128 * kKB : D * 128;
+    // shared-memory map (offsets from the 1024-aligned base)
+    static constexpr int kOffX = 0;                    // kKB K-blocks x [128][128 B]; y overwrites it
+    static constexpr int kOffQ = kOffX + 16384 * kKB;  // Q_h [128][64 B] SW64 8 KB
+    static constexpr int kOffK = kOffQ + 8192;         // K_h [128][64 B] SW64 8 KB
+    static constexpr int kOffV = kOffK + 8192;         // V_h, 2 buffers (head parity) x [128 keys][64 B] SW64
+    static constexpr int kOffAO = kOffV + 16384;       // [128][128 B] SW128 16 KB (one head pair)
+    static constexpr int kOffW = kOffAO + 16384;       // weight ring
+    static constexpr int kOffBar = kOffW + kStages * kStage;
+};
 
-// shared-memory map (offsets from the 1024-aligned base)
-constexpr int kOffX = 0;                // 4 K-blocks x [128][128 B] = 64 KB; y overwrites it
-constexpr int kOffQ = kOffX + 65536;    // Q_h [128][64 B] SW64 8 KB
-constexpr int kOffK = kOffQ + 8192;     // K_h [128][64 B] SW64 8 KB
-constexpr int kOffV = kOffK + 8192;     // V_h, 2 buffers (head parity) x [128 keys][64 B] SW64 = 16 KB
-constexpr int kOffAO = kOffV + 16384;   // [128][128 B] SW128 16 KB
-constexpr int kOffW = kOffAO + 16384;   // ring 2 x 48 KB
-constexpr int kOffBar = kOffW + kStages * kStage;
+// Head pair whose out-projection the MMA warp issues at head h of `heads`: pair p = (2p, 2p + 1)
+// at head 2p + 2 (behind QKV_{2p+3}), the last pair after the last PV; -1 at the other heads.
+PRISM_DEV constexpr int po_pair(int h, int heads) {
+    return h == heads - 1 ? heads / 2 - 1 : (h >= 2 && (h & 1) == 0) ? h / 2 - 1 : -1;
+}
 
 // TMEM columns
 constexpr uint32_t kTPO = 0;     // out-projection accumulator [256]; router logits reuse [0, npad)
@@ -78,8 +92,11 @@ struct Bars {
     int abort;
     int hist[256];
 };
-constexpr int kSmem = kOffBar + (int)sizeof(Bars) + 1024;  // + alignment slack of the dynamic base
-static_assert(kSmem <= 232448, "shared memory budget");
+template <int D>
+constexpr int attn_smem() {  // + alignment slack of the dynamic base
+    return AttnCfg<D>::kOffBar + (int)sizeof(Bars) + 1024;
+}
+static_assert(attn_smem<256>() <= 232448 && attn_smem<128>() <= 232448, "shared memory budget");
 
 struct Counter {  // phase bookkeeping of one barrier as seen by one role
     uint32_t n = 0;
@@ -108,43 +125,47 @@ PRISM_DEV void y_chunk(unsigned char* sX, const uint32_t (&v)[32], int r, const 
     }
 }
 
-// One SIMT group's share of y: chunk 2kb + part of every K-block kb, in order, each K-block
+// One SIMT group's share of y: chunk 2kb + part of every K-block kb < KB, in order, each K-block
 // announced on y_ready[kb] (with the other group's chunk it completes the K-block).  The
 // TMEM load of the next chunk is in flight while the current one is computed; the router
 // GEMM writes logits only over K-blocks already announced, so the load in flight is never
 // overwritten.
+template <int KB>
 PRISM_DEV void y_share(unsigned char* sX, uint32_t row_taddr, int r, const float* bo, int part, uint64_t* y_ready,
                        int lane) {
     uint32_t va[32], vb[32];
     tmem_ld32(row_taddr + kTPO + part * 32, va);
     tmem_ld_wait();
 #pragma unroll
-    for (int kb = 0; kb < 4; ++kb) {
+    for (int kb = 0; kb < KB; ++kb) {
         uint32_t(&cur)[32] = (kb & 1) ? vb : va;
         uint32_t(&nxt)[32] = (kb & 1) ? va : vb;
-        if (kb < 3) tmem_ld32(row_taddr + kTPO + (2 * (kb + 1) + part) * 32, nxt);
+        if (kb < KB - 1) tmem_ld32(row_taddr + kTPO + (2 * (kb + 1) + part) * 32, nxt);
         y_chunk(sX, cur, r, bo, 2 * kb + part);
         fence_async_shared();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&y_ready[kb]);
-        if (kb < 3) tmem_ld_wait();
+        if (kb < KB - 1) tmem_ld_wait();
     }
 }
 
+template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_tc_kernel(const AttnTcArgs a, const __grid_constant__ CUtensorMap tm_x,
                    const __grid_constant__ CUtensorMap tm_y, const __grid_constant__ CUtensorMap tm_wqkv,
                    const __grid_constant__ CUtensorMap tm_wo, const __grid_constant__ CUtensorMap tm_wr) {
+    using Cfg = AttnCfg<D>;
+    constexpr int kKB = Cfg::kKB, kHeads = Cfg::kHeads, kStage = Cfg::kStage;
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    unsigned char* sX = smem + kOffX;
-    unsigned char* sQ = smem + kOffQ;
-    unsigned char* sK = smem + kOffK;
-    unsigned char* sV = smem + kOffV;  // buffer b at +8192*b
-    unsigned char* sAO = smem + kOffAO;
-    unsigned char* sW = smem + kOffW;
-    Bars* bars = reinterpret_cast<Bars*>(smem + kOffBar);
+    unsigned char* sX = smem + Cfg::kOffX;
+    unsigned char* sQ = smem + Cfg::kOffQ;
+    unsigned char* sK = smem + Cfg::kOffK;
+    unsigned char* sV = smem + Cfg::kOffV;  // buffer b at +8192*b
+    unsigned char* sAO = smem + Cfg::kOffAO;
+    unsigned char* sW = smem + Cfg::kOffW;
+    Bars* bars = reinterpret_cast<Bars*>(smem + Cfg::kOffBar);
     volatile int* abort = &bars->abort;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -152,7 +173,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int win_per_frame = wx_n * wy_n;
     const int n_windows = win_per_frame * a.frames;
     const int n_tiles = (n_windows + 1) >> 1;
-    const bool router = a.n_experts > 0;
+    const bool router = D == 256 && a.n_experts > 0;  // MoE blocks are dim 256
     const int npad = a.n_experts_pad;
 
     if (threadIdx.x == 0) {
@@ -160,7 +181,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&bars->full[s], 1);
             mbar_init(&bars->empty[s], 1);
         }
-        for (int kb = 0; kb < 4; ++kb) {  // the X tile moves K-block by K-block at tile ends
+        for (int kb = 0; kb < kKB; ++kb) {  // the X tile moves K-block by K-block at tile ends
             mbar_init(&bars->x_full[kb], 1);
             mbar_init(&bars->x_free[kb], 1);   // y K-block read by the router GEMM (commit)
             mbar_init(&bars->y_ready[kb], 8);  // y K-block written (both SIMT groups, a chunk each)
@@ -185,10 +206,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = threadIdx.x; i < 256; i += blockDim.x) {
         bars->hist[i] = 0;
-        bars->bo[i] = a.bo[i];
+        bars->bo[i] = i < D ? a.bo[i] : 0.0f;
         bars->br[i] = router && i < a.n_experts ? a.br[i] : 0.0f;
     }
-    for (int i = threadIdx.x; i < 768; i += blockDim.x) bars->bqkv[i] = a.bqkv[i];
+    for (int i = threadIdx.x; i < 3 * D; i += blockDim.x) bars->bqkv[i] = a.bqkv[i];
     if (warp == 1) tmem_alloc(&bars->tmem_base, 512);
     tc_fence_before();
     __syncthreads();
@@ -226,7 +247,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             int prev = -1;  // previous tile
             Counter c_yst[4];
             auto store_y = [&](int t) {
-                for (int kb = 0; kb < 4; ++kb) {
+                for (int kb = 0; kb < kKB; ++kb) {
                     if (!mbar_wait(&bars->y_ready[kb], c_yst[kb].next(), abort)) return false;
                     for (int half = 0; half < 2; ++half) {
                         const int w = 2 * t + half;
@@ -252,15 +273,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // same order as the MMA warp consumes: QKV_0 (its stage frees when the previous
                 // tile's last out-projection completes), then per head h QKV_{h+1} and, at heads
                 // 2, 4, 6 and after head 7, the Wo columns of the pair before
-                ok = ring_load(&tm_wqkv, true, 0, 0, 96 * 512);
+                constexpr uint32_t kQkvBytes = 96 * 128 * kKB, kWoBytes = D * 128;
+                ok = ring_load(&tm_wqkv, true, 0, 0, kQkvBytes);
                 if (ok && prev >= 0) ok = store_y(prev);
                 // each X K-block once the previous tile's y K-block has been read by its store
                 // and by the router GEMM (x_free)
-                for (int kb = 0; kb < 4 && ok; ++kb) {
-                    if (prev >= 0) {
-                        if (kb == 0) tma_store_wait_read<3>();
-                        else if (kb == 1) tma_store_wait_read<2>();
-                        else if (kb == 2) tma_store_wait_read<1>();
+                for (int kb = 0; kb < kKB && ok; ++kb) {
+                    if (prev >= 0) {  // y K-block kb has been read out by its store
+                        if (kKB - 1 - kb == 3) tma_store_wait_read<3>();
+                        else if (kKB - 1 - kb == 2) tma_store_wait_read<2>();
+                        else if (kKB - 1 - kb == 1) tma_store_wait_read<1>();
                         else tma_store_wait_read<0>();
                     }
                     if (!mbar_wait(&bars->x_free[kb], c_xfree[kb].next_free(), abort)) {
@@ -274,9 +296,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 if (!ok) break;
                 prev = tile;
-                for (int h = 0; h < 8 && ok; ++h) {
-                    if (h < 7) ok = ring_load(&tm_wqkv, true, 0, (h + 1) * 96, 96 * 512);
-                    if (po_pair(h) >= 0 && ok) ok = ring_load(&tm_wo, false, po_pair(h) * 64, 0, 256 * 128);
+                for (int h = 0; h < kHeads && ok; ++h) {
+                    if (h < kHeads - 1) ok = ring_load(&tm_wqkv, true, 0, (h + 1) * 96, kQkvBytes);
+                    const int p = po_pair(h, kHeads);
+                    if (p >= 0 && ok) ok = ring_load(&tm_wo, false, p * 64, 0, kWoBytes);
                 }
                 if (router)
                     for (int r0 = 0; r0 < npad && ok; r0 += kRouterRows)
@@ -292,7 +315,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // last pair's PO
         {
             const uint32_t id_qkv = idesc_f16(128, 96), id_s = idesc_f16(128, 128), id_pv = idesc_f16(128, 32) | (1u << 16) /* B = V MN-major */,
-                           id_po = idesc_f16(128, 256);
+                           id_po = idesc_f16(128, D);
             const int r_rows = npad < kRouterRows ? npad : kRouterRows;
             int stage = 0;
             uint32_t phase = 0;
@@ -322,8 +345,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             auto issue_qkv = [&](bool first_of_tile) {  // the tile's first: X K-blocks as they land
                 const uint32_t b = ring_wait();  // Wqkv_h: K-block kc at +kc * 96 rows
                 if (ok) {
-#pragma unroll
-                    for (int kc = 0; kc < 4; ++kc) {
+#pragma unroll 1
+                    for (int kc = 0; kc < kKB; ++kc) {
                         if (first_of_tile) wait(&bars->x_full[kc], c_xfull[kc].next());
 #pragma unroll
                         for (int k = 0; k < 4; ++k)
@@ -338,14 +361,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             // rather than right after the pair's second PV, so the wait for the pair's
             // attention output and the four N = 256 MMAs stay off the QKV -> S chain
             auto issue_po = [&](int h) {
-                const int p = po_pair(h);
+                const int p = po_pair(h, kHeads);
                 if (p < 0) return;
                 wait(&bars->ao_ready, c_aor.next());
                 if (p == 0 && !first_tile) {  // PO and the previous tile's logits drained
                     wait(&bars->po_drained, c_pod.next());
                     wait(&bars->lg_drained, c_lgd.next());
                 }
-                const uint32_t b = ring_wait();  // Wo[:, pair]: all 256 output rows, N = 256
+                const uint32_t b = ring_wait();  // Wo[:, pair]: all D output rows, N = D
                 if (ok) {
 #pragma unroll
                     for (int k = 0; k < 4; ++k)
@@ -357,7 +380,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             };
             for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
                 issue_qkv(true);
-                for (int h = 0; h < 8 && ok; ++h) {
+                for (int h = 0; h < kHeads && ok; ++h) {
                     const uint32_t vs = smem_u32(sV + (h & 1) * 8192);
                     wait(&bars->qkv_drained, c_qkvd.next());
                     // ---- S_h = Q K^T
@@ -365,8 +388,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                         mma_f16_ss_w(tmem + kTS, sdesc(smem_u32(sQ) + k * 32, SW64), sdesc(smem_u32(sK) + k * 32, SW64),
                                    id_s, k != 0);
                     mma_commit_w(&bars->s_full);
-                    if (h < 7) issue_qkv(false);
-                    if (h < 7) issue_po(h);
+                    if (h < kHeads - 1) issue_qkv(false);
+                    if (h < kHeads - 1) issue_po(h);
                     wait(&bars->p_ready, c_pr.next());
                     // O columns free once the softmax group drained the previous head
                     if (h > 0 || !first_tile) wait(&bars->o_drained, c_od.next());
@@ -374,7 +397,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int k = 0; k < 8; ++k)
                         mma_f16_ts_w(tmem + kTO, tmem + kTS + k * 8, sdesc(vs + k * 1024, SW64), id_pv, k != 0);
                     mma_commit_w(&bars->o_full);
-                    if (h == 7) issue_po(h);
+                    if (h == kHeads - 1) issue_po(h);
                 }
                 mma_commit_w(&bars->po_full);
                 // ---- router logits = y . Wr^T, K-block by K-block as y lands; each X K-block
@@ -394,7 +417,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const uint32_t id_r = idesc_f16(128, n);
                         const bool last_stage = r0 + kRouterRows >= npad;
                         need_y((r0 + n - 1) >> 6);
-#pragma unroll
+#pragma unroll 1
                         for (int kc = 0; kc < 4; ++kc) {
                             need_y(kc);
 #pragma unroll
@@ -406,7 +429,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         ring_release();
                     }
                 } else {
-                    for (int kc = 0; kc < 4; ++kc) {
+                    for (int kc = 0; kc < kKB; ++kc) {
                         wait(&bars->y_ready[kc], c_yr[kc].next());
                         mma_commit_w(&bars->x_free[kc]);
                     }
@@ -437,7 +460,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (lane == 0) mbar_arrive(bar);
         };
         for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
-            for (int h = 0; h < 8 && ok; ++h) {
+            for (int h = 0; h < kHeads && ok; ++h) {
                 // ---- softmax over this row's window (split2_qkv_attn_d256.comp.glsl:59-66)
                 wait(&bars->s_full, c_s.next());
                 if (!ok) break;
@@ -543,7 +566,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // ---- y: the odd 32-column chunk of every K-block
             wait(&bars->po_full, c_po.next());
             if (!ok) break;
-            y_share(sX, tmem + lane_addr, r, bars->bo, 1, bars->y_ready, lane);
+            y_share<kKB>(sX, tmem + lane_addr, r, bars->bo, 1, bars->y_ready, lane);
             tc_fence_before();
             arrive(&bars->po_drained);
         }
@@ -606,13 +629,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int gy = wy * 8 + ty, gx = wx * 8 + tx;
             const bool valid = win_ok && gy < a.H && gx < a.W;
             const int64_t token = (int64_t)f * a.W * a.H + (int64_t)gy * a.W + gx;
-            for (int h = 0; h < 8 && ok; ++h) drain_qkv(h);
+            for (int h = 0; h < kHeads && ok; ++h) drain_qkv(h);
             if (!ok) break;
 
             // ---- y: the even 32-column chunk of every K-block (the producer stores y)
             wait(&bars->po_full, c_po.next());
             if (!ok) break;
-            y_share(sX, tmem + lane_addr, r, bars->bo, 0, bars->y_ready, lane);
+            y_share<kKB>(sX, tmem + lane_addr, r, bars->bo, 0, bars->y_ready, lane);
             tc_fence_before();
             arrive(&bars->po_drained);
 
@@ -677,13 +700,25 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 }  // namespace
 
-int attn_tc_smem_bytes() { return kSmem; }
+int attn_tc_smem_bytes(int dim) { return dim == 128 ? attn_smem<128>() : attn_smem<256>(); }
 
-cudaError_t launch_attn_tc(const AttnTcArgs& a, const CUtensorMap& x, const CUtensorMap& y, const CUtensorMap& wqkv,
-                           const CUtensorMap& wo, const CUtensorMap& wr, int grid, cudaStream_t s) {
-    cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+namespace {
+template <int D>
+cudaError_t launch_attn(const AttnTcArgs& a, const CUtensorMap& x, const CUtensorMap& y, const CUtensorMap& wqkv,
+                        const CUtensorMap& wo, const CUtensorMap& wr, int grid, cudaStream_t s) {
+    constexpr int smem = attn_smem<D>();
+    cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    return launch_pdl(attn_tc_kernel, dim3(grid), dim3(kThreads), kSmem, s, a, x, y, wqkv, wo, wr);
+    return launch_pdl(attn_tc_kernel<D>, dim3(grid), dim3(kThreads), smem, s, a, x, y, wqkv, wo, wr);
+}
+}  // namespace
+
+cudaError_t launch_attn_tc(int dim, const AttnTcArgs& a, const CUtensorMap& x, const CUtensorMap& y,
+                           const CUtensorMap& wqkv, const CUtensorMap& wo, const CUtensorMap& wr, int grid,
+                           cudaStream_t s) {
+    if (dim == 128) return launch_attn<128>(a, x, y, wqkv, wo, wr, grid, s);
+    if (dim == 256) return launch_attn<256>(a, x, y, wqkv, wo, wr, grid, s);
+    return cudaErrorInvalidValue;
 }
 
 }  // namespace prism

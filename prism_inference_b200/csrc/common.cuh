@@ -138,10 +138,10 @@ PRISM_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-// Bounded wait.  Returns false (and raises *abort) if the phase did not complete
-// within kWaitLimitNs or another role already aborted.
-PRISM_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
-    if (mbar_try_wait(bar, parity)) return true;
+// The spinning part of a bounded wait, out of line: the kernels wait at many places, and
+// inlining this loop at each of them costs instruction-cache capacity that the warps
+// issuing MMAs and the epilogues need.
+static __device__ __noinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, volatile int* abort) {
     uint64_t t0 = globaltimer();
     for (uint32_t it = 1;; ++it) {
         if (mbar_try_wait(bar, parity)) return true;
@@ -153,6 +153,12 @@ PRISM_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
             }
         }
     }
+}
+// Bounded wait.  Returns false (and raises *abort) if the phase did not complete
+// within kWaitLimitNs or another role already aborted.
+PRISM_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+    if (mbar_try_wait(bar, parity)) return true;
+    return mbar_wait_spin(bar, parity, abort);
 }
 // Bounded wait by a whole warp with a warp-uniform result: a lane whose wait timed
 // out raises *abort, which ends every other lane's wait at its next check.

@@ -343,17 +343,17 @@ namespace {
 
 struct FastBlock {
     prism_block_desc d;
-    __half* w1 = nullptr;  // experts: [E][256][256]; dense: [hidden][256]
-    __half* w2 = nullptr;  // experts: [E][256][256]; dense: [256][hidden]
+    __half* w1 = nullptr;  // experts: [E][256][256]; dense: [hidden][D]
+    __half* w2 = nullptr;  // experts: [E][256][256]; dense: [D][hidden]
     float* b1 = nullptr;   // [E][256] / [hidden]
-    float* b2 = nullptr;   // [E][256] / [256]
+    float* b2 = nullptr;   // [E][256] / [D]
     CUtensorMap tm_w1, tm_w2;
     int moe_index = -1;
-    // fused attention (dim 256): head-major QKV, out-projection, padded router
-    __half* wqkv = nullptr;  // [768][256], rows of head h at 96h: q(32) k(32) v(32)
-    float* bqkv = nullptr;   // [768] same order
-    __half* wo = nullptr;    // [256][256]
-    float* bo = nullptr;     // [256]
+    // fused attention: head-major QKV, out-projection, padded router (MoE blocks, D = 256)
+    __half* wqkv = nullptr;  // [3D][D], rows of head h at 96h: q(32) k(32) v(32)
+    float* bqkv = nullptr;   // [3D] same order
+    __half* wo = nullptr;    // [D][D]
+    float* bo = nullptr;     // [D]
     __half* wr = nullptr;    // [npad][256], rows >= n_experts zero
     float* br = nullptr;     // [npad]
     int npad = 0;
@@ -367,7 +367,6 @@ struct prism_stack {
     prism_stack_desc desc;
     std::vector<prism_block_desc> bdesc;
     int T = 0, max_frames = 0, n_moe = 0;
-    bool tc = false;  // dim 256: tensor-core expert / dense FFN / adapters
     __half* blob = nullptr;
     size_t blob_elems = 0;
     __half *up_w = nullptr, *dn_w = nullptr;
@@ -492,6 +491,11 @@ int validate_desc(const prism_stack_desc* d, size_t elems) {
                 return fail(PRISM_E_UNSUPPORTED, "block %d: ffn_hidden %d / ffn_chunk %d", i, b.ffn_hidden, b.ffn_chunk);
             if (D == 256 && b.ffn_chunk != 256)
                 return fail(PRISM_E_UNSUPPORTED, "block %d: dim-256 dense FFN needs ffn_chunk 256", i);
+            if (D == 128 && ffn_dense128_w1_box(b.ffn_hidden, b.ffn_chunk) == 0)
+                return fail(PRISM_E_UNSUPPORTED,
+                            "block %d: dim-128 dense FFN %d / chunk %d (chunk == hidden: 128 or a multiple of 256; "
+                            "or chunk 128 / 256 dividing hidden)",
+                            i, b.ffn_hidden, b.ffn_chunk);
             if (!in_range(b.ffn_w1, Hd * D, elems) || !in_range(b.ffn_b1, Hd, elems) ||
                 !in_range(b.ffn_w2, D * Hd, elems) || !in_range(b.ffn_b2, D, elems))
                 return fail(PRISM_E_RANGE, "block %d: FFN weights outside the blob", i);
@@ -537,7 +541,6 @@ extern "C" int prism_stack_create(prism_ctx* ctx, const prism_stack_desc* desc, 
     st->desc.blocks = st->bdesc.data();
     st->T = (int)T;
     st->max_frames = max_frames;
-    st->tc = desc->dim == 256;
 
     // host copy of the blob (repacking is done on the host once)
     std::vector<uint16_t> hb;
@@ -590,22 +593,24 @@ extern "C" int prism_stack_create(prism_ctx* ctx, const prism_stack_desc* desc, 
     for (int i = 0; i < desc->n_blocks; ++i) {
         FastBlock fb;
         fb.d = desc->blocks[i];
-        if (st->tc) {
-            std::vector<uint16_t> wqkv((size_t)768 * 256), wo((size_t)256 * 256);
-            std::vector<float> bqkv(768), bo(256);
-            for (int h = 0; h < 8; ++h)
+        {
+            // head-major Wqkv: the q, k and v rows of head h (32 each) at rows 96h .. 96h + 95
+            const int heads = (int)(D / 32);
+            std::vector<uint16_t> wqkv((size_t)3 * D * D), wo((size_t)D * D);
+            std::vector<float> bqkv(3 * D), bo(D);
+            for (int h = 0; h < heads; ++h)
                 for (int part = 0; part < 3; ++part) {
-                    copy_mat(wqkv, (size_t)(h * 96 + part * 32) * 256, fb.d.qkv_w + (int64_t)(part * 256 + h * 32) * 256,
-                             32, 256, 256);
-                    copy_bias(bqkv, h * 96 + part * 32, fb.d.qkv_b + part * 256 + h * 32, 32);
+                    copy_mat(wqkv, (size_t)(h * 96 + part * 32) * D, fb.d.qkv_w + (int64_t)(part * D + h * 32) * D, 32,
+                             D, D);
+                    copy_bias(bqkv, h * 96 + part * 32, fb.d.qkv_b + part * D + h * 32, 32);
                 }
-            copy_mat(wo, 0, fb.d.out_w, 256, 256, 256);
-            copy_bias(bo, 0, fb.d.out_b, 256);
+            copy_mat(wo, 0, fb.d.out_w, D, D, D);
+            copy_bias(bo, 0, fb.d.out_b, D);
             // Wqkv K-block-major: one TMA load brings a head's 96 rows at full K
-            if ((rc = upload(st, (uint16_t**)&fb.wqkv, kb_major(wqkv, 768, 256))) || (rc = upload(st, &fb.bqkv, bqkv)) ||
+            if ((rc = upload(st, (uint16_t**)&fb.wqkv, kb_major(wqkv, 3 * D, D))) || (rc = upload(st, &fb.bqkv, bqkv)) ||
                 (rc = upload(st, (uint16_t**)&fb.wo, wo)) || (rc = upload(st, &fb.bo, bo)))
                 return fail_cleanup(rc);
-            if ((rc = make_map_kb3d(&fb.tm_wqkv, fb.wqkv, 768, 256, 96)) || (rc = make_map_2d(&fb.tm_wo, fb.wo, 256, 256, 256)))
+            if ((rc = make_map_kb3d(&fb.tm_wqkv, fb.wqkv, 3 * D, D, 96)) || (rc = make_map_2d(&fb.tm_wo, fb.wo, D, D, D)))
                 return fail_cleanup(rc);
             if (fb.d.kind == PRISM_BLOCK_MOE) {
                 fb.npad = (fb.d.n_experts + 15) / 16 * 16;
@@ -639,7 +644,7 @@ extern "C" int prism_stack_create(prism_ctx* ctx, const prism_stack_desc* desc, 
             if ((rc = make_map_2d(&fb.tm_w1, fb.w1, (uint64_t)E * D, D, 256)) ||
                 (rc = make_map_2d(&fb.tm_w2, fb.w2, (uint64_t)E * D, D, 256)))
                 return fail_cleanup(rc);
-        } else if (st->tc) {
+        } else {
             const int64_t Hd = fb.d.ffn_hidden;
             std::vector<uint16_t> w1((size_t)Hd * D), w2((size_t)D * Hd);
             std::vector<float> b1(Hd), b2(D);
@@ -650,7 +655,10 @@ extern "C" int prism_stack_create(prism_ctx* ctx, const prism_stack_desc* desc, 
             if ((rc = upload(st, (uint16_t**)&fb.w1, w1)) || (rc = upload(st, (uint16_t**)&fb.w2, w2)) ||
                 (rc = upload(st, &fb.b1, b1)) || (rc = upload(st, &fb.b2, b2)))
                 return fail_cleanup(rc);
-            if ((rc = make_map_2d(&fb.tm_w1, fb.w1, Hd, D, 256)) || (rc = make_map_2d(&fb.tm_w2, fb.w2, D, Hd, 256)))
+            // W1 K-chunks of one GEMM1 piece (256 rows at D = 256; 128 or 256 at D = 128), W2 of
+            // all D output rows
+            const uint32_t w1_box = D == 256 ? 256u : (uint32_t)ffn_dense128_w1_box((int)Hd, fb.d.ffn_chunk);
+            if ((rc = make_map_2d(&fb.tm_w1, fb.w1, Hd, D, w1_box)) || (rc = make_map_2d(&fb.tm_w2, fb.w2, D, Hd, (uint32_t)D)))
                 return fail_cleanup(rc);
         }
         st->blocks.push_back(fb);
@@ -666,7 +674,7 @@ extern "C" int prism_stack_create(prism_ctx* ctx, const prism_stack_desc* desc, 
     if (cudaMemset(st->counts, 0, 256 * 4) != cudaSuccess || cudaMemset(st->cursor, 0, 256 * 4) != cudaSuccess ||
         cudaMemset(st->err, 0, 4) != cudaSuccess)
         return fail_cleanup(fail(PRISM_E_CUDA, "workspace memset failed"));
-    if (st->tc) {
+    {
         if ((rc = make_map_2d(&st->tm_act_a, st->act_a, rows, D, 128)) ||
             (rc = make_map_2d(&st->tm_act_b, st->act_b, rows, D, 128)) ||
             (rc = make_map_2d(&st->tm_act_y, st->act_y, rows, D, 128)))
@@ -792,112 +800,78 @@ int stack_forward(prism_stack* st, const void* in, void* out, int frames, int32_
             nxt = st->act_a;
             nxt_map = &st->tm_act_a;
         }
-        if (st->tc) {
-            // fused tcgen05 attention (+ router, histogram): x (cur) -> y (act_y)
-            int32_t* asg = assign ? assign + (size_t)std::max(b.moe_index, 0) * rows : st->assign_ws;
-            CUtensorMap tm_x, tm_y;
-            if ((rc = make_map_act4d(&tm_x, cur, D, d.spatial_w, d.spatial_h, frames)) ||
-                (rc = make_map_act4d(&tm_y, st->act_y, D, d.spatial_w, d.spatial_h, frames)))
-                return rc;
-            AttnTcArgs ta;
-            ta.W = d.spatial_w;
-            ta.H = d.spatial_h;
-            ta.frames = frames;
-            ta.n_keys = std::min(64, T);
-            ta.n_experts = b.d.kind == PRISM_BLOCK_MOE ? b.d.n_experts : 0;
-            ta.n_experts_pad = b.npad;
-            ta.scale = 0.1767766953f;
-            ta.bqkv = b.bqkv;
-            ta.bo = b.bo;
-            ta.br = b.br;
-            ta.assign = asg;
-            ta.counts = st->counts;
-            ta.err = st->err;
-            const int n_win = ((d.spatial_w + 7) / 8) * ((d.spatial_h + 7) / 8) * frames;
-            {
-                KernelTimer kt(st, s, PRISM_K_ATTN);
-                CUDA_TRY(launch_attn_tc(ta, tm_x, tm_y, b.tm_wqkv, b.tm_wo, b.tm_wr, std::min(grid, (n_win + 1) / 2), s));
-            }
-            if (b.d.kind == PRISM_BLOCK_MOE) {
-                RouteArgs ra_;
-                ra_.counts = st->counts;
-                ra_.counts_out = counts_out;
-                ra_.cursor = st->cursor;
-                ra_.assign = asg;
-                ra_.perm = st->perm;
-                ra_.tiles = st->tiles;
-                ra_.n_tiles = st->n_tiles;
-                ra_.n_experts = b.d.n_experts;
-                ra_.n_tokens = rows;
-                ra_.err = st->err;
-                {
-                    KernelTimer kt(st, s, PRISM_K_ROUTE);
-                    CUDA_TRY(launch_route(ra_, s));
-                }
-                FfnArgs fa{};
-                fa.x = st->act_y;
-                fa.y = nxt;
-                fa.perm = st->perm;
-                fa.tiles = st->tiles;
-                fa.n_tiles = st->n_tiles;
-                fa.b1 = b.b1;
-                fa.b2 = b.b2;
-                fa.err = st->err;
-                fa.route_counts = st->counts;
-                fa.route_cursor = st->cursor;
-                fa.n_route = b.d.n_experts;
-                KernelTimer kt(st, s, PRISM_K_EXPERT);
-                fa.n_rows = (int)rows;
-                CUDA_TRY(launch_ffn_expert256(fa, b.tm_w1, b.tm_w2,
-                                              std::min(grid, rows / 128 + b.d.n_experts), s));
-            } else {
-                FfnArgs fa{};
-                fa.x = st->act_y;
-                fa.y = nxt;
-                fa.n_rows = rows;
-                fa.b1 = b.b1;
-                fa.b2 = b.b2;
-                fa.err = st->err;
-                KernelTimer kt(st, s, PRISM_K_DENSE_FFN);
-                CUDA_TRY(launch_ffn_dense256(fa, st->tm_act_y, b.tm_w1, b.tm_w2, b.d.ffn_hidden / 256,
-                                             std::min(grid, (rows + 127) / 128), s));
-            }
-            cur = nxt;
-            cur_map = nxt_map;
-            continue;
-        }
-        // dim 128 (dense blocks only: MoE blocks need dim 256): CUDA-core attention into the
-        // next buffer, then the CUDA-core dense FFN in place on it
-        AttnArgs at;
-        at.weights = st->blob;
-        at.x = cur;
-        at.y = nxt;
-        at.frame_stride = (int64_t)T * D;
-        at.qkv_w = b.d.qkv_w;
-        at.qkv_b = b.d.qkv_b;
-        at.out_w = b.d.out_w;
-        at.out_b = b.d.out_b;
-        at.W = d.spatial_w;
-        at.H = d.spatial_h;
-        at.n_tokens = T;
-        at.scale = 0.1767766953f;
+        // fused tcgen05 attention (+ router, histogram): x (cur) -> y (act_y)
+        int32_t* asg = assign ? assign + (size_t)std::max(b.moe_index, 0) * rows : st->assign_ws;
+        CUtensorMap tm_x, tm_y;
+        if ((rc = make_map_act4d(&tm_x, cur, D, d.spatial_w, d.spatial_h, frames)) ||
+            (rc = make_map_act4d(&tm_y, st->act_y, D, d.spatial_w, d.spatial_h, frames)))
+            return rc;
+        AttnTcArgs ta;
+        ta.W = d.spatial_w;
+        ta.H = d.spatial_h;
+        ta.frames = frames;
+        ta.n_keys = std::min(64, T);
+        ta.n_experts = b.d.kind == PRISM_BLOCK_MOE ? b.d.n_experts : 0;
+        ta.n_experts_pad = b.npad;
+        ta.scale = 0.1767766953f;
+        ta.bqkv = b.bqkv;
+        ta.bo = b.bo;
+        ta.br = b.br;
+        ta.assign = asg;
+        ta.counts = st->counts;
+        ta.err = st->err;
+        const int n_win = ((d.spatial_w + 7) / 8) * ((d.spatial_h + 7) / 8) * frames;
         {
             KernelTimer kt(st, s, PRISM_K_ATTN);
-            CUDA_TRY(launch_attn_window(at, D, frames, s));
+            CUDA_TRY(launch_attn_tc(D, ta, tm_x, tm_y, b.tm_wqkv, b.tm_wo, b.tm_wr, std::min(grid, (n_win + 1) / 2), s));
         }
-        DenseFfnArgs f;
-        f.weights = st->blob;
-        f.io = nxt;
-        f.w1 = b.d.ffn_w1;
-        f.b1 = b.d.ffn_b1;
-        f.w2 = b.d.ffn_w2;
-        f.b2 = b.d.ffn_b2;
-        f.hidden = b.d.ffn_hidden;
-        f.chunk = b.d.ffn_chunk;
-        f.n_tokens = rows;
-        {
+        if (b.d.kind == PRISM_BLOCK_MOE) {
+            RouteArgs ra_;
+            ra_.counts = st->counts;
+            ra_.counts_out = counts_out;
+            ra_.cursor = st->cursor;
+            ra_.assign = asg;
+            ra_.perm = st->perm;
+            ra_.tiles = st->tiles;
+            ra_.n_tiles = st->n_tiles;
+            ra_.n_experts = b.d.n_experts;
+            ra_.n_tokens = rows;
+            ra_.err = st->err;
+            {
+                KernelTimer kt(st, s, PRISM_K_ROUTE);
+                CUDA_TRY(launch_route(ra_, s));
+            }
+            FfnArgs fa{};
+            fa.x = st->act_y;
+            fa.y = nxt;
+            fa.perm = st->perm;
+            fa.tiles = st->tiles;
+            fa.n_tiles = st->n_tiles;
+            fa.b1 = b.b1;
+            fa.b2 = b.b2;
+            fa.err = st->err;
+            fa.route_counts = st->counts;
+            fa.route_cursor = st->cursor;
+            fa.n_route = b.d.n_experts;
+            KernelTimer kt(st, s, PRISM_K_EXPERT);
+            fa.n_rows = (int)rows;
+            CUDA_TRY(launch_ffn_expert256(fa, b.tm_w1, b.tm_w2,
+                                          std::min(grid, rows / 128 + b.d.n_experts), s));
+        } else {
+            FfnArgs fa{};
+            fa.x = st->act_y;
+            fa.y = nxt;
+            fa.n_rows = rows;
+            fa.b1 = b.b1;
+            fa.b2 = b.b2;
+            fa.err = st->err;
             KernelTimer kt(st, s, PRISM_K_DENSE_FFN);
-            CUDA_TRY(launch_dense_ffn(f, D, s));
+            if (D == 256)
+                CUDA_TRY(launch_ffn_dense256(fa, st->tm_act_y, b.tm_w1, b.tm_w2, b.d.ffn_hidden / 256,
+                                             std::min(grid, (rows + 127) / 128), s));
+            else
+                CUDA_TRY(launch_ffn_dense128(fa, st->tm_act_y, b.tm_w1, b.tm_w2, b.d.ffn_hidden, b.d.ffn_chunk,
+                                             std::min(grid, (rows + 127) / 128), s));
         }
         cur = nxt;
         cur_map = nxt_map;

@@ -33,7 +33,8 @@ constexpr int kThreads = 32 * (2 + kEpiWarps);
 template <int MODE, int KIN, int HID, int NOUT>
 struct FfnCfg {
     static_assert(MODE != FFN_EXPERT, "the expert FFN is expert_tc.cu");
-    static constexpr bool kTwoGemm = (MODE == FFN_DENSE);
+    static constexpr bool kTwoGemm = (MODE == FFN_DENSE || MODE == FFN_DENSE_UNSPLIT);
+    static constexpr bool kUnsplit = (MODE == FFN_DENSE_UNSPLIT);  // acc2 accumulates over chunks
     static constexpr int kA = KIN * 128 * 2;                    // A tile bytes
     static constexpr int kH = kTwoGemm ? HID * 128 * 2 : 0;     // H tile bytes
     static constexpr int kWRows = HID > NOUT ? HID : NOUT;      // rows of one W K-chunk
@@ -190,10 +191,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!Cfg::kTwoGemm) continue;
                 // GEMM2 -> acc2 (columns [256, 256 + NOUT)), A = H from the epilogue,
                 // one K-block at a time as the epilogue hands them over
+                // acc2 is handed over once per chunk, or once per tile when it accumulates over chunks
+                const uint32_t acc2_it = Cfg::kUnsplit ? it : chunk_it;
                 for (int i = 0; i < HID / 64; ++i) {
                     const int kc = h_block_order<HID>(i);
                     if (!mbar_wait_w(&bars->h_full[kc], chunk_it & 1, abort)) { ok = false; break; }
-                    if (i == 0 && !mbar_wait_w(&bars->acc2_empty, (chunk_it & 1) ^ 1, abort)) { ok = false; break; }
+                    if (i == 0 && (!Cfg::kUnsplit || c == 0) &&
+                        !mbar_wait_w(&bars->acc2_empty, (acc2_it & 1) ^ 1, abort)) { ok = false; break; }
                     fence_async_shared();
                     tc_fence_after();
                     if (!mbar_wait_w(&bars->full[stage], phase, abort)) { ok = false; break; }
@@ -204,13 +208,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                         for (int k = 0; k < 4; ++k)
                             mma_f16_ss_w(tmem + Cfg::kAcc2, sdesc(a0 + k * 32, SW128), sdesc(b0 + k * 32, SW128),
-                                         idesc2, (i | k) != 0);
+                                         idesc2, (Cfg::kUnsplit && c > 0) || (i | k) != 0);
                         mma_commit_w(&bars->empty[stage]);
                     }
                     if (++stage == Cfg::kStages) { stage = 0; phase ^= 1; }
                 }
                 if (!ok) break;
-                mma_commit_w(&bars->acc2_full);
+                if (!Cfg::kUnsplit || c == n_chunks - 1) mma_commit_w(&bars->acc2_full);
             }
         }
         // every issued MMA has completed before TMEM is released
@@ -263,7 +267,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         // t = h(acc + b1): one rounding per coopVecMatMulAddNV result
                         const uint32_t t = pack_h2(__fadd_rn(__uint_as_float(r[2 * j]), bx),
                                                    __fadd_rn(__uint_as_float(r[2 * j + 1]), by));
-                        if (MODE == FFN_DENSE) {
+                        if (Cfg::kTwoGemm) {
                             packed[j] = pack_h2(gelu_f32(lo_h2f(t)), gelu_f32(hi_h2f(t)));
                         } else if (MODE == FFN_PROJ_UP) {
                             const float v0 = lo_h2f(t), v1 = hi_h2f(t);
@@ -280,7 +284,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                         for (int q = 0; q < 4; ++q)
                             *reinterpret_cast<uint4*>(blk + sw128_off(row, ch + q)) =
                                 make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
-                        if (g & 1) {  // K-block col0/64 complete for this warp's rows: hand it to GEMM2
+                        // K-block col0/64 complete for this warp's rows (its part covers 64 columns
+                        // of it, or all 32 of a 32-column part): hand it to GEMM2
+                        if ((g & 1) || kCols1 == 32) {
                             fence_async_shared();
                             __syncwarp();
                             if (lane == 0) mbar_arrive(&bars->h_full[col0 >> 6]);
@@ -303,6 +309,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // out through this warp's own slice of the H tile (free once GEMM2 is
                 // done): both global transfers are row-contiguous, 16 lanes per 256 B.
                 const bool last = (c == n_chunks - 1);
+                if (Cfg::kUnsplit && !last) continue;  // acc2 keeps accumulating over the chunks
                 constexpr int kCols2 = NOUT / kParts;      // this warp's column part
                 constexpr int kRowsPerLd = 512 / (kCols2 * 2);  // rows per 512-B warp access
                 constexpr int kLanesPerRow = 32 / kRowsPerLd;
@@ -321,7 +328,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 const float* b2 = a.b2 + (size_t)e * NOUT;
                 const float4 bias2 = 4 * lane < kCols2 ? ldg_f4(b2 + half * kCols2 + 4 * lane) : make_float4(0, 0, 0, 0);
-                if (!mbar_wait(&bars->acc2_full, chunk_it & 1, abort)) { ok = false; break; }
+                if (!mbar_wait(&bars->acc2_full, (Cfg::kUnsplit ? it : chunk_it) & 1, abort)) { ok = false; break; }
                 tc_fence_after();
                 // H-tile address of (tile row R, column col) in the K-major SW128 layout
                 auto hslot = [&](int R, int col) -> unsigned char* {
@@ -431,6 +438,21 @@ cudaError_t launch_ffn(const FfnArgs& a, const CUtensorMap& tx, const CUtensorMa
 cudaError_t launch_ffn_dense256(const FfnArgs& a, const CUtensorMap& x, const CUtensorMap& w1, const CUtensorMap& w2,
                                 int n_chunks, int grid, cudaStream_t s) {
     return launch_ffn<FFN_DENSE, 256, 256, 256>(a, x, w1, w2, n_chunks, grid, s);
+}
+int ffn_dense128_w1_box(int hidden, int chunk) {
+    if (hidden <= 0 || chunk <= 0 || hidden % chunk) return 0;
+    if (chunk == hidden) return hidden == 128 ? 128 : hidden % 256 == 0 ? 256 : 0;
+    return chunk == 128 || chunk == 256 ? chunk : 0;
+}
+
+cudaError_t launch_ffn_dense128(const FfnArgs& a, const CUtensorMap& x, const CUtensorMap& w1, const CUtensorMap& w2,
+                                int hidden, int chunk, int grid, cudaStream_t s) {
+    const int box = ffn_dense128_w1_box(hidden, chunk);
+    if (box == 0) return cudaErrorInvalidValue;
+    if (chunk == hidden && hidden > 128)  // one product, hidden in 256-wide GEMM1 pieces
+        return launch_ffn<FFN_DENSE_UNSPLIT, 128, 256, 128>(a, x, w1, w2, hidden / 256, grid, s);
+    if (box == 128) return launch_ffn<FFN_DENSE, 128, 128, 128>(a, x, w1, w2, hidden / 128, grid, s);
+    return launch_ffn<FFN_DENSE, 128, 256, 128>(a, x, w1, w2, hidden / 256, grid, s);
 }
 cudaError_t launch_ffn_proj_up(const FfnArgs& a, const CUtensorMap& x, const CUtensorMap& w, int grid,
                                cudaStream_t s) {

@@ -12,7 +12,9 @@ enum FfnMode : int {
     FFN_EXPERT = 0,     // gathered rows of one expert: x + W2 gelu(W1 x + b1) + b2, scattered back
     FFN_PROJ_UP = 1,    // relu(W x + b), 128 -> 256
     FFN_PROJ_DOWN = 2,  // W x + b, 256 -> 128
-    FFN_DENSE = 3       // dense FFN of width NCH*HID, fp16 accumulation of NCH chunk outputs
+    FFN_DENSE = 3,      // dense FFN of width NCH*HID, fp16 accumulation of NCH chunk outputs
+    FFN_DENSE_UNSPLIT = 4  // dense FFN of width NCH*HID as ONE product: GEMM2 accumulates over every
+                           // chunk's H in fp32, rounded once (attention_windowed.comp.glsl:151-170)
 };
 
 // One tile of the grouped expert GEMM: rows perm[start .. start+rows) of expert e.
@@ -41,6 +43,15 @@ cudaError_t launch_ffn_expert256(const FfnArgs& a, const CUtensorMap& w1, const 
                                  cudaStream_t s);
 cudaError_t launch_ffn_dense256(const FfnArgs& a, const CUtensorMap& x, const CUtensorMap& w1, const CUtensorMap& w2,
                                 int n_chunks, int grid, cudaStream_t s);
+// Dense FFN of a dim-128 block (x: [rows][128], w1: [hidden][128] map with box {64, chunk rows},
+// w2: [128][hidden] map with box {64, 128}).  chunk == hidden: one product (the d128 shader);
+// chunk 128 or 256 < hidden: fp16 accumulation of chunk outputs (the d256 shader's rule).
+// Supported: hidden == chunk == 128; hidden == chunk, a multiple of 256; chunk 128 or 256
+// dividing hidden.  Returns cudaErrorInvalidValue for other shapes.
+cudaError_t launch_ffn_dense128(const FfnArgs& a, const CUtensorMap& x, const CUtensorMap& w1, const CUtensorMap& w2,
+                                int hidden, int chunk, int grid, cudaStream_t s);
+// Row count of the W1 tensor-map box launch_ffn_dense128 expects for (hidden, chunk), 0 if unsupported.
+int ffn_dense128_w1_box(int hidden, int chunk);
 cudaError_t launch_ffn_proj_up(const FfnArgs& a, const CUtensorMap& x, const CUtensorMap& w, int grid,
                                cudaStream_t s);
 cudaError_t launch_ffn_proj_down(const FfnArgs& a, const CUtensorMap& x, const CUtensorMap& w, int grid,

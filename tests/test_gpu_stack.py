@@ -90,6 +90,25 @@ def test_stack_reference_ffn_widths(prism_ctx, oracle, key):
     _check(prism_ctx, oracle, cfg.layout, blob, x, key + "-ref-widths")
 
 
+@pytest.mark.parametrize("hidden,chunk", [(128, 128), (256, 256), (512, 512), (512, 128), (512, 256)])
+def test_dense128_ffn_shapes(prism_ctx, oracle, hidden, chunk):
+    """The dim-128 block on tensor cores for every FFN shape its kernels take: one product of
+    width 128, 256 or 512 (the d128 shader's unsplit FFN, attention_windowed.comp.glsl:151-170;
+    256 and 512 accumulate GEMM2 over 256-wide pieces of the hidden layer in fp32), and 128- or
+    256-wide chunks summed in fp16 (the d256 shader's rule)."""
+    L = layout.build_stack(128, 2, n_heads=4, ffn_hidden=hidden, ffn_chunk=chunk, spatial_w=40, spatial_h=20)
+    blob = synth.make_blob(L, seed=synth.WEIGHT_SEED + hidden + chunk)
+    x = synth.make_frames(L, 3)
+    _check(prism_ctx, oracle, L, blob, x, f"d128 ffn {hidden}/{chunk}")
+
+
+def test_dense128_unsupported_ffn_is_rejected(prism_ctx):
+    from prism_inference_b200.abi import PrismError
+    L = layout.build_stack(128, 1, n_heads=4, ffn_hidden=384, ffn_chunk=384)
+    with pytest.raises(PrismError, match="UNSUPPORTED"):
+        Stack(prism_ctx, L, synth.make_blob(L), 1)
+
+
 def test_headline_stack_full_depth(prism_ctx, oracle):
     """Config 4 as benchmarked: 64 experts x 16 blocks + adapters, one frame."""
     cfg = configs.get("moe64x16")
