@@ -188,6 +188,39 @@ int prism_dense_block(prism_ctx* ctx, const prism_dense_params* p,
                       const void* weights, size_t weight_elems,
                       void* features, size_t feature_elems, void* stream);
 
+/* ---- the encoder / decoder around the stack (prism_moe_bench.cpp:386-471) ----------
+ * One call = one reference vkCmdDispatch of the named shader, on CHW fp16 feature maps at
+ * element offsets of the caller's arena (binding 1), weights at element offsets of the blob
+ * (binding 0), with the shader's own push constants in its declaration order:
+ *   PRISM_CODEC_ENC_IC   conv3x3_coopvec_9ch        {in_ch, out_ch, w, h, w_off, b_off, in_off, out_off, relu}
+ *   PRISM_CODEC_ENC1     strided_conv_coopvec_32ch  {in_ch, out_ch, in_w, in_h, out_w, out_h, w_off, b_off,
+ *   PRISM_CODEC_ENC2     strided_conv_split_64ch     in_off, out_off}
+ *   PRISM_CODEC_ENC3     strided_conv_split_128ch
+ *   PRISM_CODEC_DEC3     dec3_fused                 {out_w, out_h, in_w, in_h, ch, w_off, b_off, in_off,
+ *                                                    skip_off, out_off}
+ *   PRISM_CODEC_DEC2     dec2_fused                 {out_w, out_h, in_w, in_h, up_ch, skip_ch, w_off, b_off,
+ *   PRISM_CODEC_DEC1     dec1_fused                  in_off, skip_off, out_off}
+ *   PRISM_CODEC_OUT12    pw_conv_coopvec_32to12     {in_ch, out_ch, w, h, w_off, b_off, in_off, out_off, relu}
+ *   PRISM_CODEC_PIXELSHUFFLE pixelshuffle_sigmoid   {render_w, render_h, display_w, display_h, scale,
+ *                                                    in_off, out_off}; RGB to `rgb` (binding 2, fp16)
+ * The shaders fix their channel counts in code and do not read the channel push constants;
+ * neither does this call.  The contractions run on the tensor cores with the shaders' rounding
+ * points; the first call of a kind on a context allocates that kind's weight scratch (a repacked,
+ * aligned copy made on the stream before each pass, so calls of one context go on one stream).
+ * A bounded device wait that gives up is reported by prism_ctx_status. */
+enum prism_codec_kind {
+    PRISM_CODEC_ENC_IC = 0, PRISM_CODEC_ENC1 = 1, PRISM_CODEC_ENC2 = 2, PRISM_CODEC_ENC3 = 3,
+    PRISM_CODEC_DEC3 = 4, PRISM_CODEC_DEC2 = 5, PRISM_CODEC_DEC1 = 6, PRISM_CODEC_OUT12 = 7,
+    PRISM_CODEC_PIXELSHUFFLE = 8
+};
+int prism_codec_pass(prism_ctx* ctx, int kind, const int32_t* push, int n_push,
+                     const void* weights, size_t weight_elems, void* features, size_t feature_elems,
+                     void* rgb, size_t rgb_elems, void* stream);
+
+/* Host-synchronising check (and reset) of the context's device error word, set when a bounded
+ * wait of a per-pass kernel gives up: PRISM_E_TIMEOUT, else PRISM_OK. */
+int prism_ctx_status(prism_ctx* ctx, void* stream);
+
 /* ---- fast path: a whole stack over a batch of frames ------------------------ */
 
 enum prism_block_kind { PRISM_BLOCK_MOE = 0, PRISM_BLOCK_DENSE = 1 };
@@ -261,6 +294,19 @@ int prism_moe_block(prism_stack* blk, const void* features_in, void* features_ou
  * max_frames each) and three internal streams. */
 int prism_stack_infer(prism_stack* st, const void* host_in, void* host_out, int frames,
                       float* gpu_ms);
+
+/* Device-buffer inference, the counterpart of PrismVulkan::InferGPU (prism_vulkan.h:88-95,
+ * prism_vulkan.cpp:922-1004: the caller's device buffers with BYTE offsets, for a host that
+ * already holds the frames on the GPU, e.g. a game hook).  in_buf + in_offset: device
+ * [frames][T][in_dim] fp16; out_buf + out_offset: device [frames][T][out_dim] fp16 (must not
+ * overlap the input).  Synchronous like the reference (which waits on its fences); *gpu_ms
+ * (nullable) receives the device time of the forward alone.  Both addresses 16-byte aligned:
+ * the forward reads and writes the caller's buffers directly; otherwise the data is copied
+ * through the stack's device staging slot (allocated on first use, as for prism_stack_infer),
+ * as the reference copies through its own feature buffer.  The error word is checked as
+ * prism_stack_status does. */
+int prism_stack_infer_gpu(prism_stack* st, const void* in_buf, size_t in_offset, void* out_buf,
+                          size_t out_offset, int frames, float* gpu_ms);
 
 /* Pipelined host-buffer inference for serving loops.  prism_stack_submit enqueues the
  * upload of host_in on an internal copy stream, the forward on `stream` and the download

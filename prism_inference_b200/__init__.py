@@ -106,6 +106,20 @@ class Prism:
                                                    weights.numel(), _ptr(features), features.numel(),
                                                    _stream(stream)))
 
+    def codec_pass(self, shader: str, push, weights, features, rgb=None, stream=None):
+        """prism_codec_pass: one dispatch of an encoder / decoder shader (abi.CODEC_KINDS) with
+        its push constants, on CUDA fp16 tensors (weights = binding 0, features = binding 1,
+        rgb = binding 2 for pixelshuffle_sigmoid)."""
+        pc = (C.c_int32 * len(push))(*[int(v) for v in push])
+        check(self.lib, self.lib.prism_codec_pass(self.h, abi.CODEC_KINDS.index(shader), pc, len(push),
+                                                  _ptr(weights), weights.numel(), _ptr(features), features.numel(),
+                                                  _ptr(rgb) if rgb is not None else None,
+                                                  rgb.numel() if rgb is not None else 0, _stream(stream)))
+
+    def status(self, stream=None):
+        """prism_ctx_status: raises PrismError if a per-pass kernel's bounded wait gave up."""
+        check(self.lib, self.lib.prism_ctx_status(self.h, _stream(stream)))
+
 
 class Stack:
     """The whole stack of a StackLayout (prism_stack_create / prism_stack_forward).
@@ -150,6 +164,15 @@ class Stack:
         ms = C.c_float()
         check(self.lib, self.lib.prism_stack_infer(self.h, _host_ptr(host_in), _host_ptr(host_out),
                                                    host_in.shape[0], C.byref(ms)))
+        return ms.value
+
+    def infer_gpu(self, in_buf, out_buf, frames: int, in_offset: int = 0, out_offset: int = 0) -> float:
+        """prism_stack_infer_gpu (the reference's InferGPU): in_buf / out_buf are CUDA tensors
+        (any dtype) holding [frames, T, in_dim] / [frames, T, out_dim] fp16 at the given BYTE
+        offsets; synchronous.  Returns the forward's device time in ms."""
+        ms = C.c_float()
+        check(self.lib, self.lib.prism_stack_infer_gpu(self.h, in_buf.data_ptr(), in_offset, out_buf.data_ptr(),
+                                                       out_offset, frames, C.byref(ms)))
         return ms.value
 
     def submit(self, host_in, host_out=None, stream=None) -> int:

@@ -87,7 +87,12 @@ EXPORTS = ("prism_create", "prism_destroy", "prism_last_error_string", "prism_ab
            "prism_stack_forward", "prism_stack_status", "prism_stack_launch_count",
            "prism_stack_tokens_per_frame", "prism_stack_profile", "prism_stack_profile_read",
            "prism_expert_all_static", "prism_stack_inject_stall", "prism_stack_infer",
-           "prism_stack_submit", "prism_stack_wait", "prism_moe_block")
+           "prism_stack_submit", "prism_stack_wait", "prism_moe_block", "prism_stack_infer_gpu",
+           "prism_codec_pass", "prism_ctx_status")
+# prism_codec_kind order = the shaders of oracle.CODEC_KINDS
+CODEC_KINDS = ("conv3x3_coopvec_9ch", "strided_conv_coopvec_32ch", "strided_conv_split_64ch",
+               "strided_conv_split_128ch", "dec3_fused", "dec2_fused", "dec1_fused",
+               "pw_conv_coopvec_32to12", "pixelshuffle_sigmoid")
 STATIC_MAX_TOKENS = 65536  # PRISM_STATIC_MAX_TOKENS
 KERNEL_KINDS = ("proj_up", "attn", "router", "route", "expert", "dense_ffn", "proj_down", "copy")
 
@@ -123,6 +128,9 @@ def load(path: os.PathLike | None = None) -> C.CDLL:
         "prism_stack_status": (i32, [vp, vp]),
         "prism_stack_inject_stall": (i32, [vp, vp]),
         "prism_stack_infer": (i32, [vp, vp, vp, i32, C.POINTER(C.c_float)]),
+        "prism_stack_infer_gpu": (i32, [vp, vp, sz, vp, sz, i32, C.POINTER(C.c_float)]),
+        "prism_codec_pass": (i32, [vp, i32, C.POINTER(C.c_int32), i32, vp, sz, vp, sz, vp, sz, vp]),
+        "prism_ctx_status": (i32, [vp, vp]),
         "prism_moe_block": (i32, [vp, vp, vp, i32, vp, vp, vp]),
         "prism_stack_submit": (i32, [vp, vp, vp, i32, vp, C.POINTER(C.c_int64)]),
         "prism_stack_wait": (i32, [vp, C.c_int64, vp]),

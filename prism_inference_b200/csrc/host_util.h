@@ -21,6 +21,10 @@ struct DeviceGuard {
     }
 };
 
+// Per-context scratch of the encoder / decoder passes (codec_tc.cu).
+void* codec_scratch_new();
+void codec_scratch_free(void* p);
+
 // [off, off + n) inside [0, limit)?
 inline bool in_range(int64_t off, int64_t n, size_t limit) {
     return off >= 0 && n >= 0 && (uint64_t)(off + n) <= (uint64_t)limit;
@@ -32,4 +36,6 @@ inline bool in_range(int64_t off, int64_t n, size_t limit) {
 struct prism_ctx {
     int device;
     int sm_count;
+    uint32_t* err = nullptr;  // device error word of the per-pass kernels that wait (prism_ctx_status)
+    void* codec = nullptr;    // repacked weights of the encoder / decoder passes, per kind
 };

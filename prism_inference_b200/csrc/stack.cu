@@ -148,14 +148,29 @@ extern "C" int prism_create(int device, prism_ctx** out) {
     if (prop.major != 10)
         return fail(PRISM_E_UNSUPPORTED, "prism_create: device %d is sm_%d%d; this library is built for sm_100a",
                     device, prop.major, prop.minor);
+    DeviceGuard g(device);
+    void* err = nullptr;
+    if (cudaMalloc(&err, 4) != cudaSuccess || cudaMemset(err, 0, 4) != cudaSuccess) {
+        cudaFree(err);
+        return fail(PRISM_E_NOMEM, "prism_create: error word");
+    }
     auto* c = new prism_ctx;
     c->device = device;
     c->sm_count = prop.multiProcessorCount;
+    c->err = static_cast<uint32_t*>(err);
+    c->codec = codec_scratch_new();
     *out = c;
     return PRISM_OK;
 }
 
 extern "C" int prism_destroy(prism_ctx* ctx) {
+    if (!ctx) return PRISM_OK;
+    {
+        DeviceGuard g(ctx->device);
+        cudaDeviceSynchronize();
+        codec_scratch_free(ctx->codec);
+        cudaFree(ctx->err);
+    }
     delete ctx;
     return PRISM_OK;
 }
@@ -998,6 +1013,52 @@ extern "C" int prism_stack_wait(prism_stack* st, int64_t ticket, void* stream) {
     if (stream) CUDA_TRY(cudaStreamWaitEvent(as_stream(stream), e, 0));
     else CUDA_TRY(cudaEventSynchronize(e));
     return PRISM_OK;
+}
+
+extern "C" int prism_stack_infer_gpu(prism_stack* st, const void* in_buf, size_t in_offset, void* out_buf,
+                                     size_t out_offset, int frames, float* gpu_ms) {
+    if (!st) return fail(PRISM_E_ARG, "prism_stack_infer_gpu: NULL stack");
+    if (frames < 0 || frames > st->max_frames)
+        return fail(PRISM_E_RANGE, "prism_stack_infer_gpu: frames %d (max %d)", frames, st->max_frames);
+    if (gpu_ms) *gpu_ms = 0.0f;
+    if (frames == 0) return PRISM_OK;
+    if (!in_buf || !out_buf) return fail(PRISM_E_ARG, "prism_stack_infer_gpu: NULL buffer");
+    DeviceGuard g(st->ctx->device);
+    for (const void* p : {in_buf, (const void*)out_buf}) {
+        cudaPointerAttributes attr;
+        if (cudaPointerGetAttributes(&attr, p) != cudaSuccess || attr.type != cudaMemoryTypeDevice ||
+            attr.device != st->ctx->device) {
+            cudaGetLastError();
+            return fail(PRISM_E_ARG, "prism_stack_infer_gpu: buffers must be device memory of device %d",
+                        st->ctx->device);
+        }
+    }
+    const size_t rows = (size_t)st->T * frames;
+    const size_t in_bytes = rows * st->desc.in_dim * 2, out_bytes = rows * st->desc.out_dim * 2;
+    const char* in = static_cast<const char*>(in_buf) + in_offset;
+    char* out = static_cast<char*>(out_buf) + out_offset;
+    if (in < out + out_bytes && out < in + in_bytes)
+        return fail(PRISM_E_ARG, "prism_stack_infer_gpu: the output range overlaps the input range");
+    int rc = staging_init(st);  // the internal stream and timing events (and, if needed, the slots)
+    if (rc) return rc;
+    auto& q = st->stg;
+    cudaStream_t s = q.s_fwd;
+    // the slot's events of the host-buffer path order this call after any earlier submission
+    const int p = (int)(q.next & 1);
+    CUDA_TRY(cudaStreamWaitEvent(s, q.out_done[p], 0));
+    const bool direct = ((uintptr_t)in & 15) == 0 && ((uintptr_t)out & 15) == 0;
+    if (!direct) CUDA_TRY(cudaMemcpyAsync(q.in[p], in, in_bytes, cudaMemcpyDeviceToDevice, s));
+    CUDA_TRY(cudaEventRecord(q.t0[p], s));
+    if ((rc = prism_stack_forward(st, direct ? in : (const char*)q.in[p], direct ? out : (char*)q.out[p], frames,
+                                  nullptr, s)))
+        return rc;
+    CUDA_TRY(cudaEventRecord(q.t1[p], s));
+    if (!direct) CUDA_TRY(cudaMemcpyAsync(out, q.out[p], out_bytes, cudaMemcpyDeviceToDevice, s));
+    CUDA_TRY(cudaEventRecord(q.out_done[p], s));
+    q.next += 1;
+    CUDA_TRY(cudaEventSynchronize(q.out_done[p]));
+    if (gpu_ms) CUDA_TRY(cudaEventElapsedTime(gpu_ms, q.t0[p], q.t1[p]));
+    return prism_stack_status(st, s);
 }
 
 extern "C" int prism_stack_infer(prism_stack* st, const void* host_in, void* host_out, int frames, float* gpu_ms) {

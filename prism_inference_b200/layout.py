@@ -195,6 +195,18 @@ def pack_weights(L: StackLayout, tensors) -> "np.ndarray":
     return blob
 
 
+def unpack_weights(L: StackLayout, blob) -> dict:
+    """The inverse of pack_weights: {layer name: (flat weight, flat bias)} fp16 views of blob."""
+    import numpy as np
+
+    blob = np.asarray(blob, dtype=np.float16)
+    out = {}
+    for l in L.layers:
+        wo, bo = l["weight_offset_fp16"], l["bias_offset_fp16"]
+        out[l["name"]] = (blob[wo:wo + l["weight_count"]], blob[bo:bo + l["bias_count"]])
+    return out
+
+
 def write_weights(path: str, L: StackLayout, blob) -> str:
     """Write blob as a raw fp16 .weights file and L's table as the .json beside it (the pair
     export_weights.py writes); returns the .json path."""

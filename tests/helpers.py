@@ -30,3 +30,22 @@ def routing_agreement(gpu_assign, ref_assign, margin):
     diff = np.asarray(gpu_assign) != np.asarray(ref_assign)
     ties = np.asarray(margin) < TIE_MARGIN
     return int((diff & ~ties).sum()), int((diff & ties).sum())
+
+
+def checkpoint_of(L, blob, split_qkv=False):
+    """Named tensors (default convention of export.py) holding the blob's weights."""
+    from prism_inference_b200 import export
+    names = export.default_names(L)
+    ck = {}
+    from prism_inference_b200 import layout
+    for lname, (w, b) in layout.unpack_weights(L, blob).items():
+        p = names[lname]
+        if split_qkv and lname.endswith(".qkv"):
+            D = L.dim
+            for j, x in enumerate("qkv"):
+                ck[f"{p[:-4]}.{x}.weight"] = w.reshape(3 * D, D)[j * D:(j + 1) * D].astype(np.float32)
+                ck[f"{p[:-4]}.{x}.bias"] = b[j * D:(j + 1) * D].astype(np.float32)
+        else:
+            ck[f"{p}.weight"] = w.astype(np.float32)
+            ck[f"{p}.bias"] = b.astype(np.float32)
+    return ck

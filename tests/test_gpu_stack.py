@@ -109,6 +109,23 @@ def test_dense128_unsupported_ffn_is_rejected(prism_ctx):
         Stack(prism_ctx, L, synth.make_blob(L), 1)
 
 
+def test_stack_from_exported_weight_file(prism_ctx, oracle, tmp_path):
+    """The trained-model path end to end: named checkpoint tensors -> export.py -> the
+    .weights / .json pair -> the layout rebuilt from the JSON table alone -> prism_stack_create
+    from the file's blob -> GPU forward, against the oracle run on the same file."""
+    from helpers import checkpoint_of
+    from prism_inference_b200 import export
+    L = configs.get("moe64x16", n_blocks=2).layout
+    ck = checkpoint_of(L, synth.make_blob(L, seed=synth.WEIGHT_SEED + 77), split_qkv=True)
+    np.savez(tmp_path / "ck.npz", **ck)
+    path = str(tmp_path / "prism.weights")
+    assert export.main([str(tmp_path / "ck.npz"), path, "--config", "moe64x16", "--n-blocks", "2"]) == 0
+    blob, table = layout.read_weights(path)
+    L2 = layout.stack_from_json(table, 256, 8, 64, 2)
+    x = synth.make_frames(L2, 2)
+    _check(prism_ctx, oracle, L2, blob, x, "moe64x16 from an exported weight file")
+
+
 def test_headline_stack_full_depth(prism_ctx, oracle):
     """Config 4 as benchmarked: 64 experts x 16 blocks + adapters, one frame."""
     cfg = configs.get("moe64x16")
@@ -354,6 +371,42 @@ def test_host_buffer_infer_and_pipelined_submit(prism_ctx):
     st.status()
     with pytest.raises(PrismError, match="RANGE"):
         st.wait(t + 1)
+    st.close()
+
+
+def test_infer_gpu_on_caller_buffers_with_byte_offsets(prism_ctx):
+    """prism_stack_infer_gpu (InferGPU, prism_vulkan.cpp:922-1004): frames read from and written
+    to the caller's device buffers at byte offsets.  16-byte aligned offsets run in place, a
+    2-byte offset goes through the staging slot; both give prism_stack_forward's bits and leave
+    the buffers outside the output untouched.  Overlapping ranges and host memory are refused."""
+    import torch
+    from prism_inference_b200.abi import PrismError
+    cfg = configs.get("moe64x16", n_blocks=2)
+    L = cfg.layout
+    T = L.tokens
+    blob = synth.make_blob(L)
+    x = synth.make_frames(L, 2)
+    st = Stack(prism_ctx, L, blob, 2)
+    xd = torch.from_numpy(x.view(np.int16)).cuda().view(torch.float16)
+    ref = torch.empty((2, T, L.out_dim), dtype=torch.float16, device="cuda")
+    st.forward(xd, ref)
+    torch.cuda.synchronize()
+    st.status()
+    nin, nout = x.nbytes, ref.numel() * 2
+    for off_in, off_out in ((256, 4096), (2, 6)):
+        src = torch.full((off_in + nin + 64,), 0x5A, dtype=torch.uint8, device="cuda")
+        src[off_in:off_in + nin] = xd.view(torch.uint8).reshape(-1)
+        dst = torch.full((off_out + nout + 64,), 0x33, dtype=torch.uint8, device="cuda")
+        ms = st.infer_gpu(src, dst, 2, off_in, off_out)
+        assert ms > 0.0
+        got = dst[off_out:off_out + nout].view(torch.int16).view(2, T, L.out_dim)
+        assert torch.equal(got, ref.view(torch.int16)), (off_in, off_out)
+        assert bool((dst[:off_out] == 0x33).all()) and bool((dst[off_out + nout:] == 0x33).all())
+    arena = torch.zeros(nin + nout, dtype=torch.uint8, device="cuda")
+    with pytest.raises(PrismError, match="ARG"):
+        st.infer_gpu(arena, arena, 2, 0, nin - 16)  # output overlaps the input
+    with pytest.raises(PrismError, match="ARG"):
+        st.infer_gpu(torch.zeros(nin, dtype=torch.uint8), arena, 2)  # host memory
     st.close()
 
 

@@ -4,6 +4,7 @@ import json
 import numpy as np
 import pytest
 
+from helpers import checkpoint_of
 from prism_inference_b200 import configs, layout, synth
 
 
@@ -81,3 +82,36 @@ def test_synthetic_data_is_seeded_per_frame():
     assert abs(float(a.astype(np.float32).std()) - 1.0) < 0.05
     w = synth.make_blob(L)
     assert abs(float(w.astype(np.float32).std()) - 0.02) < 0.002
+
+
+@pytest.mark.parametrize("key,split", [("moe16x1", False), ("dense256x12", True), ("dense128x4", False)])
+def test_export_checkpoint_roundtrip(tmp_path, key, split):
+    """A checkpoint named after export.py's convention (q, k, v as one tensor or three) exports
+    to the .weights / .json pair of the layout, bit-identical to the packed blob."""
+    from prism_inference_b200 import export
+    cfg = configs.get(key, n_blocks=2)
+    L = cfg.layout
+    blob = synth.make_blob(L, seed=11)
+    ck = checkpoint_of(L, blob, split_qkv=split)
+    np.savez(tmp_path / "ck.npz", **ck)
+    out = str(tmp_path / "m.weights")
+    assert export.main([str(tmp_path / "ck.npz"), out, "--config", key, "--n-blocks", "2"]) == 0
+    blob2, table = layout.read_weights(out)
+    assert blob2.view(np.uint16).tobytes() == blob.view(np.uint16).tobytes()
+    assert table["layers"] == L.layers
+
+
+def test_export_custom_names_and_missing_tensors(tmp_path):
+    from prism_inference_b200 import export
+    L = layout.build_stack(256, 1, n_experts=2)
+    blob = synth.make_blob(L, seed=3)
+    ck = checkpoint_of(L, blob)
+    ck["encoder.layer0.mha.out_proj.weight"] = ck.pop("blocks.0.attn.proj.weight")
+    ck["encoder.layer0.mha.out_proj.bias"] = ck.pop("blocks.0.attn.proj.bias")
+    with pytest.raises(KeyError, match="blocks.0.attn.proj.weight"):
+        export.export(L, ck, str(tmp_path / "a.weights"))
+    export.export(L, ck, str(tmp_path / "a.weights"), names={"blk0.out": "encoder.layer0.mha.out_proj"})
+    assert layout.read_weights(str(tmp_path / "a.weights"))[0].view(np.uint16).tobytes() == blob.view(np.uint16).tobytes()
+    del ck["blocks.0.moe.router.bias"]
+    with pytest.raises(KeyError, match="router.bias"):
+        export.export(L, ck, str(tmp_path / "b.weights"), names={"blk0.out": "encoder.layer0.mha.out_proj"})
