@@ -59,6 +59,9 @@ def parse():
     p.add_argument("--config", default="moe64x16", choices=configs.ALL)
     p.add_argument("--frames", type=int, default=64, help="frames per GPU per step")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--codec", action="store_true",
+                   help="the encoder / decoder passes around the stack at the reference's 960x540 render size "
+                        "(prism_codec_pass) instead of the stack")
     return p.parse_args()
 
 
@@ -513,8 +516,168 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------- codec -----
+def codec_cpu_baseline(fc, blob, feat, min_seconds=5.0):
+    """The reference's own encoder / decoder shader sources (oracle/_ref) for whole frames on all
+    host cores, until at least min_seconds of CPU work were timed."""
+    from oracle import REF_LIB, GlslRef, use_host_threads
+    if not REF_LIB.exists():
+        return None
+    ref = GlslRef()
+    threads = use_host_threads()
+    total, frames = 0.0, 0
+    f = feat.copy()
+    rgb = np.zeros(fc.rgb_elems, np.float16)
+    while total < min_seconds and frames < 8:
+        t0 = time.perf_counter()
+        for shader, push, _ in fc.passes:
+            if shader.startswith("strided"):
+                px = push[4] * push[5]
+            elif shader.startswith("dec"):
+                px = push[0] * push[1]
+            else:
+                px = push[2] * push[3]
+            ref.dispatch(shader, push, blob, f, None, (px + 255) // 256)
+        ps = fc.pixelshuffle
+        ref.dispatch("pixelshuffle_sigmoid", ps, blob, f, rgb, ((ps[2] + 15) // 16, (ps[3] + 15) // 16))
+        total += time.perf_counter() - t0
+        frames += 1
+    return {"value": frames / total, "unit": "frames/s", "cores": threads, "kind": "reference",
+            "sample": f"{frames} frames of the 9 encoder / decoder shaders at {fc.render[0]}x{fc.render[1]} ({total:.1f} s)"}
+
+
+def run_codec(args):
+    """One step = one frame through the nine encoder / decoder passes (prism_codec_pass each) at
+    the reference's 960x540 render size; every rank runs its own frame (weak scaling).  value: the
+    chain replayed as one CUDA graph (device time); per-pass times: CUDA events around each
+    eager call."""
+    import torch
+    import torch.distributed as dist
+    from prism_inference_b200 import Prism, codec
+    ws, rank, local = dist_env()
+    if ws > 1:
+        torch.cuda.set_device(local)
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    dev = torch.cuda.current_device()
+    fc = codec.frame_chain(960, 540)
+    blob, feat = codec.synthetic(fc, seed=0x5EED + rank)
+    ctx = Prism(dev)
+    w = torch.from_numpy(blob.view(np.int16)).cuda().view(torch.float16)
+    f = torch.from_numpy(feat.view(np.int16)).cuda().view(torch.float16)
+    rgb = torch.zeros(fc.rgb_elems, dtype=torch.float16, device="cuda")
+    names = [p[0] for p in fc.passes] + ["pixelshuffle_sigmoid"]
+    pushes = [p[1] for p in fc.passes] + [fc.pixelshuffle]
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(len(names) + 1)]
+
+    def frame(timed=False):
+        stream = torch.cuda.current_stream()
+        for i, (sh, pc) in enumerate(zip(names, pushes)):
+            if timed:
+                ev[i].record(stream)
+            ctx.codec_pass(sh, pc, w, f, rgb if sh == "pixelshuffle_sigmoid" else None, stream)
+        if timed:
+            ev[-1].record(stream)
+
+    for _ in range(args.warmup):
+        frame()
+    torch.cuda.synchronize()
+    ctx.status()
+    stream = torch.cuda.current_stream()
+    per = np.zeros(len(names))
+    for _ in range(args.steps):
+        torch.cuda.synchronize()
+        frame(timed=True)
+        torch.cuda.synchronize()
+        per += np.array([ev[i].elapsed_time(ev[i + 1]) for i in range(len(names))])
+    per /= args.steps
+    # the whole frame as one CUDA graph (no host work between the launches)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        frame()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        frame()
+    for _ in range(3):
+        g.replay()
+    clocks = ClockSampler(dev)
+    clocks.start()
+    clocks.wait_first()
+    mark = clocks.mark()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if ws > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(args.steps):
+        g.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    # end to end: the frame from page-locked host memory and the RGB back, every step
+    o, n = fc.feat_off["in"], fc.feat_size["in"]
+    xin = torch.from_numpy(feat[o:o + n].view(np.int16)).view(torch.float16).pin_memory()
+    rgb_h = torch.empty(fc.rgb_elems, dtype=torch.float16).pin_memory()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(args.steps):
+        f[o:o + n].copy_(xin, non_blocking=True)
+        g.replay()
+        rgb_h.copy_(rgb, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms_e2e = e0.elapsed_time(e1) / args.steps
+    clk = clocks.stop(mark)
+    del g
+    ctx.status()
+    if ws > 1:
+        t = torch.tensor([ms, ms_e2e], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, ms_e2e = float(t[0]), float(t[1])
+    peak_tf, peak_gbs, src = load_peaks()
+    rows = {}
+    for i, sh in enumerate(names):
+        b, fl = fc.pass_bytes_flops(sh)
+        rows[sh] = {"ms_eager": round(float(per[i]), 5), "GB_per_s": round(b / (per[i] / 1e3) / 1e9, 1),
+                    "TFLOP_per_s": round(fl / (per[i] / 1e3) / 1e12, 1)}
+    total_bytes = sum(fc.pass_bytes_flops(s)[0] for s in names)
+    achieved = total_bytes / (ms / 1e3) / 1e9
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        cpu = codec_cpu_baseline(fc, blob, feat)
+    if rank == 0:
+        line = {"metric": "encoder/decoder frames/s at 960x540 render (9 passes, 1080p RGB out)",
+                "value": ws * 1e3 / ms, "unit": "frames/s", "n_gpus": ws, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+                "config": {"workload": "encoder/decoder of prism_moe_bench.cpp:386-471 at 960x540 (the stack left out)",
+                           "frames_per_gpu": 1, "passes_eager": rows, "algorithmic_bytes_per_frame": total_bytes,
+                           "l2": "maps of one frame total 140 MB; a pass reads the previous pass's output"},
+                "e2e": {"value": ws * 1e3 / ms_e2e, "unit": "frames/s", "h2d_bytes_per_step": int(xin.numel() * 2),
+                        "d2h_bytes_per_step": int(rgb_h.numel() * 2), "ms_per_step": ms_e2e,
+                        "api": "prism_codec_pass per pass (graph replay); frame in / RGB out through page-locked host memory"},
+                "gpu_launches": 2 * len(fc.passes) + 1,
+                "roofline": {"kernel": "whole chain", "bound": "hbm", "achieved": achieved, "peak": peak_gbs,
+                             "unit": "GB/s", "frac": achieved / peak_gbs, "peak_source": f"{src} hbm_gbs",
+                             "traffic": None},
+                "cpu_baseline": cpu, "clocks": clk}
+        print(json.dumps(line))
+    ctx.close()
+    if ws > 1:
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
+    if args.codec:
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "--codec measures this library only"}))
+            return
+        run_codec(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:

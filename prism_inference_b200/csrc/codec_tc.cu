@@ -56,10 +56,17 @@ struct CodecCfg {
                                                                 : 128;
     static constexpr int kNP = (kN + 15) / 16 * 16;             // MMA N (multiple of 16)
     static constexpr int kG = KIND == C_ENC2 ? 2 : KIND == C_ENC3 ? 4 : 1;  // channel groups
-    static constexpr int kKG = kType == 0 ? (kIn / kG) * 9 : kType == 1 ? kUp + kSkip : kIn;  // K per group
+    static constexpr int kCg = kIn / kG;                        // conv: input channels per group
+    // K of one group in the blob (the shader's order: channel, then ky, then kx)
+    static constexpr int kKsrc = kType == 0 ? kCg * 9 : kType == 1 ? kUp + kSkip : kIn;
+    static constexpr int kLd = kG * kKsrc;                      // row stride of the blob's matrix
+    // The GEMM's K order for the 3x3 convolutions is tap-major (k = tap * kCgP + channel), so one
+    // 32-value half of a K-block is one tap (or two taps of 16 channel slots when a group has 9
+    // channels): the gather checks bounds once per half and steps through the channel planes.
+    static constexpr int kCgP = kCg >= 32 ? 32 : 16;
+    static constexpr int kKG = kType == 0 ? 9 * kCgP : kKsrc;   // GEMM K per group
     static constexpr int kKGP = (kKG + 63) / 64 * 64;           // padded to whole K-blocks
     static constexpr int kKB = kKGP / 64;
-    static constexpr int kLd = kG * kKG;                        // row stride of the blob's matrix
     static constexpr int kAccCols = kG * kNP;
     static constexpr int kAccBufs = kAccCols <= 256 ? 2 : 1;    // TMEM accumulator buffers
     static constexpr int kBBytes = kNP * 128;                   // one weight K-block
@@ -188,66 +195,96 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_wait_w(&bars->drain, 0, abort);
     } else if (warp < 10) {
         // ============================ gather ============================
+        // The values are fp16 already and go to the A tile unchanged, so each lane issues its 32
+        // raw 16-bit loads of a K-block without branches (an address outside the map or the
+        // padding reads element 0 of the map and is then replaced by zero) and keeps the next
+        // K-block's loads in flight while it stores the current one.
         const int gw = warp - 2, quad = gw & 3, half = gw >> 2;
         const int row = quad * 32 + lane;
         const int in_px = a.in_w * a.in_h;
+        const unsigned short* in = reinterpret_cast<const unsigned short*>(a.in);
+        const unsigned short* skip = reinterpret_cast<const unsigned short*>(a.skip);
+        constexpr int kItems = C::kG * C::kKB;  // K-blocks per tile
+        // issue the loads of the 32 values of K-block `item` of `tile` into r; bit j of the result
+        // says whether value j is real (else the shader reads zero there, and nothing is loaded)
+        auto issue = [&](int tile, int item, uint32_t (&r)[32]) -> uint32_t {
+            const int g = item / C::kKB, kb = item % C::kKB;
+            const int p = tile * 128 + row;
+            if (p >= out_px) return 0u;
+            const int oy = p / a.out_w, ox = p % a.out_w;
+            if constexpr (C::kType == 0) {
+                const unsigned short* base = in + (int64_t)g * C::kCg * in_px;
+                uint32_t mask = 0;
+#pragma unroll
+                for (int tt = 0; tt < 32 / C::kCgP; ++tt) {  // the taps of this half
+                    const int t = (kb * 64 + half * 32) / C::kCgP + tt;
+                    const int y = oy * C::kStride + t / 3 - 1, x = ox * C::kStride + t % 3 - 1;
+                    if (t < 9 && y >= 0 && y < a.in_h && x >= 0 && x < a.in_w) {
+                        const unsigned short* q = base + (int64_t)y * a.in_w + x;
+#pragma unroll
+                        for (int c = 0; c < (C::kCg < C::kCgP ? C::kCg : C::kCgP); ++c)
+                            r[tt * C::kCgP + c] = __ldg(q + (int64_t)c * in_px);
+                        mask |= (C::kCg < C::kCgP ? (1u << C::kCg) - 1u : 0xffffffffu) << (tt * C::kCgP);
+                    }
+                }
+                return mask;
+            } else {
+                const int k0 = kb * 64 + half * 32;  // one map per half: up / skip / pointwise input
+                if (k0 >= C::kKG) return 0u;
+                const unsigned short* q;
+                int64_t plane;
+                if (C::kType == 1 && k0 < C::kUp) {
+                    q = in + (int64_t)k0 * in_px + min(oy >> 1, a.in_h - 1) * a.in_w + min(ox >> 1, a.in_w - 1);
+                    plane = in_px;
+                } else {
+                    q = (C::kType == 1 ? skip + (int64_t)(k0 - C::kUp) * out_px : in + (int64_t)k0 * out_px) + p;
+                    plane = out_px;
+                }
+#pragma unroll
+                for (int j = 0; j < 32; ++j) r[j] = __ldg(q + j * plane);
+                return 0xffffffffu;
+            }
+        };
         int s = 0;
         uint32_t ph = 0;
         bool ok = true;
-        for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
-            const int p = tile * 128 + row;
-            const bool valid = p < out_px;
-            const int oy = valid ? p / a.out_w : 0, ox = valid ? p % a.out_w : 0;
-            for (int g = 0; g < C::kG && ok; ++g)
-#pragma unroll 1
-                for (int kb = 0; kb < C::kKB; ++kb) {
-                    // this lane's 32 values of the K-block (loads issued before the slot wait)
-                    uint32_t pk[16];
+        uint32_t cur[32], nxt[32], m_cur = 0, m_nxt = 0;
+        int tile = blockIdx.x, item = 0;
+        if (tile < n_tiles) m_cur = issue(tile, 0, cur);
+        while (tile < n_tiles && ok) {
+            int nt = tile, ni = item + 1;
+            if (ni == kItems) {
+                ni = 0;
+                nt += gridDim.x;
+            }
+            if (nt < n_tiles) m_nxt = issue(nt, ni, nxt);
+            if (!mbar_wait(&bars->empty[s], ph ^ 1, abort)) {
+                ok = false;
+                break;
+            }
+            unsigned char* dst = stage_a(s);
 #pragma unroll
-                    for (int j = 0; j < 32; j += 2) {
-                        float v[2];
+            for (int c = 0; c < 4; ++c) {
+                uint32_t w4[4];
 #pragma unroll
-                        for (int e = 0; e < 2; ++e) {
-                            const int k = kb * 64 + half * 32 + j + e;  // K index within the group
-                            float x = 0.0f;
-                            if (valid && k < C::kKG) {
-                                if constexpr (C::kType == 0) {  // 3x3 patch, channel then ky then kx
-                                    const int c = g * (C::kIn / C::kG) + k / 9, t = k % 9;
-                                    const int y = oy * C::kStride + t / 3 - 1, xx = ox * C::kStride + t % 3 - 1;
-                                    if (y >= 0 && y < a.in_h && xx >= 0 && xx < a.in_w)
-                                        x = __half2float(a.in[(size_t)c * in_px + y * a.in_w + xx]);
-                                } else if constexpr (C::kType == 1) {  // upsampled deeper map, then skip
-                                    if (k < C::kUp) {
-                                        const int iy = min(oy >> 1, a.in_h - 1), ix = min(ox >> 1, a.in_w - 1);
-                                        x = __half2float(a.in[(size_t)k * in_px + iy * a.in_w + ix]);
-                                    } else {
-                                        x = __half2float(a.skip[(size_t)(k - C::kUp) * out_px + p]);
-                                    }
-                                } else {  // pointwise
-                                    x = __half2float(a.in[(size_t)k * out_px + p]);
-                                }
-                            }
-                            v[e] = x;
-                        }
-                        pk[j >> 1] = pack_h2(v[0], v[1]);  // exact: the values are fp16
-                    }
-                    if (!mbar_wait(&bars->empty[s], ph ^ 1, abort)) {
-                        ok = false;
-                        break;
-                    }
-                    unsigned char* dst = stage_a(s);
-#pragma unroll
-                    for (int c = 0; c < 4; ++c)
-                        *reinterpret_cast<uint4*>(dst + sw128_off(row, half * 4 + c)) =
-                            make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-                    fence_async_shared();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&bars->a_full[s]);
-                    if (++s == kStages) {
-                        s = 0;
-                        ph ^= 1;
-                    }
+                for (int q = 0; q < 4; ++q) {
+                    const int j = 8 * c + 2 * q;
+                    w4[q] = ((m_cur >> j) & 1u ? cur[j] : 0u) | ((m_cur >> (j + 1)) & 1u ? cur[j + 1] << 16 : 0u);
                 }
+                *reinterpret_cast<uint4*>(dst + sw128_off(row, half * 4 + c)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+            }
+            fence_async_shared();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->a_full[s]);
+            if (++s == kStages) {
+                s = 0;
+                ph ^= 1;
+            }
+#pragma unroll
+            for (int j = 0; j < 32; ++j) cur[j] = nxt[j];
+            m_cur = m_nxt;
+            tile = nt;
+            item = ni;
         }
     } else {
         // ============================ epilogue ============================
@@ -331,7 +368,14 @@ __global__ void codec_repack_kernel(const __half* blob, int wo, int bo, __half* 
     const int total = C::kG * C::kNP * C::kKGP;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
         const int k = i % C::kKGP, n = (i / C::kKGP) % C::kNP, g = i / (C::kKGP * C::kNP);
-        w[i] = n < C::kN && k < C::kKG ? blob[wo + (size_t)n * C::kLd + g * C::kKG + k] : __float2half(0.0f);
+        int src = -1;  // element of the group's row in the blob's (channel, tap) order
+        if (C::kType == 0) {
+            const int t = k / C::kCgP, c = k % C::kCgP;
+            if (t < 9 && c < C::kCg) src = c * 9 + t;
+        } else if (k < C::kKG) {
+            src = k;
+        }
+        w[i] = n < C::kN && src >= 0 ? blob[wo + (size_t)n * C::kLd + g * C::kKsrc + src] : __float2half(0.0f);
     }
     if (blockIdx.x == 0)
         for (int n = threadIdx.x; n < C::kN; n += blockDim.x) bias[n] = __half2float(blob[bo + n]);
@@ -339,13 +383,17 @@ __global__ void codec_repack_kernel(const __half* blob, int wo, int bo, __half* 
 
 // pixelshuffle_sigmoid.comp.glsl:26-56: display pixel (ox, oy) of colour c takes channel
 // c*s*s + (oy%s)*s + ox%s of render pixel (ox/s, oy/s), through 1/(1 + exp(-v)) in fp32
+// One thread per display pixel (blockIdx.y = display row), its three colours.
 __global__ void pixelshuffle_kernel(const __half* in, __half* rgb, int rw, int rh, int dw, int dh, int sc) {
-    const size_t n = (size_t)3 * dw * dh, rpx = (size_t)rw * rh;
-    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
-        const int ox = (int)(i % dw), oy = (int)((i / dw) % dh), c = (int)(i / ((size_t)dw * dh));
-        const int src = c * sc * sc + (oy % sc) * sc + ox % sc;
-        const float v = __half2float(in[(size_t)src * rpx + (size_t)(oy / sc) * rw + ox / sc]);
-        rgb[i] = __float2half_rn(__fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-v))));
+    const int ox = blockIdx.x * blockDim.x + threadIdx.x, oy = blockIdx.y;
+    if (ox >= dw) return;
+    const int64_t rpx = (int64_t)rw * rh, dpx = (int64_t)dw * dh;
+    const int64_t at = (int64_t)(oy / sc) * rw + ox / sc;
+    const int sub = (oy % sc) * sc + ox % sc;
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+        const float v = __half2float(in[(int64_t)(c * sc * sc + sub) * rpx + at]);
+        rgb[c * dpx + (int64_t)oy * dw + ox] = __float2half_rn(__fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-v))));
     }
 }
 
@@ -501,9 +549,9 @@ extern "C" int prism_codec_pass(prism_ctx* ctx, int kind, const int32_t* push, i
     if (!in_range(in_off, (int64_t)3 * sc * sc * rw * rh, feature_elems) ||
         !in_range(out_off, (int64_t)3 * dw * dh, rgb_elems))
         return set_error(PRISM_E_RANGE, "prism_codec_pass: pixel shuffle outside its buffers");
-    const int64_t n = (int64_t)3 * dw * dh;
-    pixelshuffle_kernel<<<(int)std::min<int64_t>((n + 255) / 256, 4 * ctx->sm_count), 256, 0, s>>>(
-        f + in_off, static_cast<__half*>(rgb) + out_off, rw, rh, dw, dh, sc);
+    if (dh > 65535) return set_error(PRISM_E_RANGE, "prism_codec_pass: display height %d", dh);
+    pixelshuffle_kernel<<<dim3((dw + 255) / 256, dh), 256, 0, s>>>(f + in_off, static_cast<__half*>(rgb) + out_off, rw,
+                                                                  rh, dw, dh, sc);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return set_error(PRISM_E_CUDA, "prism_codec_pass: %s", cudaGetErrorString(e));
     return PRISM_OK;

@@ -42,50 +42,13 @@ def test_codec_pass_matches_reference_golden(prism_ctx, name):
     assert_close(output_of(c), gold, name)
 
 
-def _pyramid(w0, h0):
-    r = [(w0, h0)]
-    for _ in range(3):
-        r.append(((r[-1][0] + 1) // 2, (r[-1][1] + 1) // 2))
-    return r
-
-
 def _chain(w0, h0, seed):
-    """Weights, a feature arena and the nine passes of prism_moe_bench.cpp:386-471 (the stack
-    left out: the bottleneck map goes to dec3 directly) at a render size of w0 x h0."""
-    rng = np.random.Generator(np.random.PCG64(seed))
-    r = _pyramid(w0, h0)
-    p = [w * h for w, h in r]
-    shapes = {"ic": (32, 81), "e1": (64, 288), "e2": (128, 576), "e3": (128, 1152), "d3": (128, 256),
-              "d2": (64, 192), "d1": (32, 96), "o": (12, 32)}
-    off, parts, n = {}, [], 0
-    for k, (rows, cols) in shapes.items():
-        wt = (rng.standard_normal(rows * cols, dtype=np.float32) / np.float32(np.sqrt(cols))).astype(np.float16)
-        b = (rng.standard_normal(rows, dtype=np.float32) * np.float32(0.1)).astype(np.float16)
-        off[k] = (n + 3, n + 3 + rows * cols)  # odd element offsets: the blob is read at any alignment
-        parts += [np.zeros(3, np.float16), wt, b]
-        n += 3 + rows * cols + rows
-    blob = np.concatenate(parts)
-    sizes = {"in": 9 * p[0], "e0": 32 * p[0], "e1": 64 * p[1], "e2": 128 * p[2], "e3": 128 * p[3],
-             "d3": 128 * p[2], "d2": 64 * p[1], "d1": 32 * p[0], "o12": 12 * p[0]}
-    fo, n = {}, 1
-    for k, s in sizes.items():
-        fo[k] = n
-        n += s
-    feat = np.zeros(n, np.float16)
-    feat[fo["in"]:fo["in"] + sizes["in"]] = rng.standard_normal(sizes["in"], dtype=np.float32).astype(np.float16)
-    (w0_, h0_), (w1, h1), (w2, h2), (w3, h3) = r
-    passes = [
-        ("conv3x3_coopvec_9ch", [9, 32, w0_, h0_, *off["ic"], fo["in"], fo["e0"], 1], "e0"),
-        ("strided_conv_coopvec_32ch", [32, 64, w0_, h0_, w1, h1, *off["e1"], fo["e0"], fo["e1"]], "e1"),
-        ("strided_conv_split_64ch", [64, 128, w1, h1, w2, h2, *off["e2"], fo["e1"], fo["e2"]], "e2"),
-        ("strided_conv_split_128ch", [128, 128, w2, h2, w3, h3, *off["e3"], fo["e2"], fo["e3"]], "e3"),
-        ("dec3_fused", [w2, h2, w3, h3, 128, *off["d3"], fo["e3"], fo["e2"], fo["d3"]], "d3"),
-        ("dec2_fused", [w1, h1, w2, h2, 128, 64, *off["d2"], fo["d3"], fo["e1"], fo["d2"]], "d2"),
-        ("dec1_fused", [w0_, h0_, w1, h1, 64, 32, *off["d1"], fo["d2"], fo["e0"], fo["d1"]], "d1"),
-        ("pw_conv_coopvec_32to12", [32, 12, w0_, h0_, *off["o"], fo["d1"], fo["o12"], 0], "o12"),
-    ]
-    ps = [w0_, h0_, 2 * w0_, 2 * h0_, 2, fo["o12"], 0]
-    return blob, feat, passes, ps, fo, sizes, 12 * p[0]
+    """Weights, feature arena and dispatch list of one frame's encoder / decoder path at a
+    render size of w0 x h0, with weights and maps at odd (unaligned) element offsets."""
+    from prism_inference_b200 import codec
+    fc = codec.frame_chain(w0, h0, weight_pad=3, feat_pad=1)
+    blob, feat = codec.synthetic(fc, seed)
+    return blob, feat, fc.passes, fc.pixelshuffle, fc.feat_off, fc.feat_size, fc.rgb_elems
 
 
 def test_codec_passes_at_reference_frame_size(prism_ctx, oracle):
