@@ -27,8 +27,10 @@
 //               swizzled A tile
 //   warps 10-13 epilogue: TMEM -> the shader's rounding / group rule -> CHW stores (each warp
 //               instruction writes 32 consecutive pixels of one channel)
-// A 4-stage ring holds {A K-block 16 KB, B K-block N x 128 B}.  Every wait is bounded
-// (common.cuh); on timeout the CTA sets the context's error word and winds down.
+// Weight matrices of up to 64 KB (all but the two split convolutions) are loaded into shared
+// memory once per CTA and an 8-stage ring carries the A K-blocks; the split convolutions' weights
+// stream through a 4-stage ring of {A K-block 16 KB, B K-block N x 128 B}.  Every wait is
+// bounded (common.cuh); on timeout the CTA sets the context's error word and winds down.
 #include <cudaTypedefs.h>
 
 #include <mutex>
@@ -70,12 +72,19 @@ struct CodecCfg {
     static constexpr int kAccCols = kG * kNP;
     static constexpr int kAccBufs = kAccCols <= 256 ? 2 : 1;    // TMEM accumulator buffers
     static constexpr int kBBytes = kNP * 128;                   // one weight K-block
+    static constexpr int kWBytes = kG * kKB * kBBytes;          // the whole repacked weight matrix
+    // Weights of up to 64 KB stay in shared memory for the whole CTA (loaded once); larger ones
+    // (the split convolutions) stream through the ring beside the A K-blocks.
+    static constexpr bool kResident = kWBytes <= 65536;
+    static constexpr int kStages = kResident ? 8 : 4;
+    static constexpr int kStageBytes = kResident ? 16384 : 32768;  // A (+ B when streamed)
+    static constexpr int kWOff = kStages * kStageBytes;         // resident weights
+    static constexpr int kBarOff = kWOff + (kResident ? (kWBytes + 1023) / 1024 * 1024 : 0);
 };
 
 constexpr int kThreads = 32 * 14;
-constexpr int kStages = 4;
+constexpr int kMaxStages = 8;
 constexpr int kABytes = 128 * 128;  // one A K-block: 128 rows x 64 fp16, SW128
-constexpr int kStageBytes = kABytes + 128 * 128;  // A + the largest B K-block (N = 128)
 
 struct CodecArgs {
     const __half* in;    // conv / pw: the input map; dec: the deeper map (CHW)
@@ -88,13 +97,16 @@ struct CodecArgs {
 };
 
 struct Bars {
-    uint64_t a_full[kStages], b_full[kStages], empty[kStages];
-    uint64_t acc_full[2], acc_empty[2], drain;
+    uint64_t a_full[kMaxStages], b_full[kMaxStages], empty[kMaxStages];
+    uint64_t acc_full[2], acc_empty[2], drain, w_full;
     uint32_t tmem_base;
     int abort;
     float bias[128];
 };
-constexpr int kSmem = kStages * kStageBytes + (int)sizeof(Bars) + 1024;
+template <int KIND>
+constexpr int codec_smem() {  // + alignment slack of the dynamic base
+    return CodecCfg<KIND>::kBarOff + (int)sizeof(Bars) + 1024;
+}
 
 PRISM_DEV uint16_t h_bits(float f) { return __half_as_ushort(__float2half_rn(f)); }
 PRISM_DEV float bits_h(uint16_t b) { return __half2float(__ushort_as_half(b)); }
@@ -105,9 +117,10 @@ template <int KIND>
 __global__ void __launch_bounds__(kThreads, 1)
     codec_tc_kernel(const CodecArgs a, const __grid_constant__ CUtensorMap tm_w) {
     using C = CodecCfg<KIND>;
+    constexpr int kStages = C::kStages, kStageBytes = C::kStageBytes;
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    Bars* bars = reinterpret_cast<Bars*>(smem + kStages * kStageBytes);
+    Bars* bars = reinterpret_cast<Bars*>(smem + C::kBarOff);
     volatile int* abort = &bars->abort;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int out_px = a.out_w * a.out_h;
@@ -124,6 +137,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&bars->acc_empty[b], 4);
         }
         mbar_init(&bars->drain, 1);
+        mbar_init(&bars->w_full, 1);
         bars->abort = 0;
         fence_barrier_init();
     }
@@ -134,11 +148,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     const uint32_t tmem = bars->tmem_base;
     auto stage_a = [&](int s) { return smem + s * kStageBytes; };
-    auto stage_b = [&](int s) { return smem + s * kStageBytes + kABytes; };
+    // weight K-block (g, kb) of `stage`: resident copy, or the stage's B slot when streamed
+    auto b_block = [&](int s, int g, int kb) {
+        return C::kResident ? smem + C::kWOff + (g * C::kKB + kb) * C::kBBytes : smem + s * kStageBytes + kABytes;
+    };
 
     if (warp == 0) {
         // ============================ producer ============================
-        if (lane == 0) {
+        if (lane == 0 && C::kResident) {  // the whole weight matrix, once
+            prefetch_tmap(&tm_w);
+            mbar_expect_tx(&bars->w_full, C::kWBytes);
+            for (int g = 0; g < C::kG; ++g)
+                for (int kb = 0; kb < C::kKB; ++kb)
+                    tma_load_2d(smem_u32(b_block(0, g, kb)), &tm_w, &bars->w_full, kb * 64, g * C::kNP);
+        } else if (lane == 0) {
             prefetch_tmap(&tm_w);
             int s = 0;
             uint32_t ph = 0;
@@ -151,7 +174,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             break;
                         }
                         mbar_expect_tx(&bars->b_full[s], C::kBBytes);
-                        tma_load_2d(smem_u32(stage_b(s)), &tm_w, &bars->b_full[s], kb * 64, g * C::kNP);
+                        tma_load_2d(smem_u32(b_block(s, g, kb)), &tm_w, &bars->b_full[s], kb * 64, g * C::kNP);
                         if (++s == kStages) {
                             s = 0;
                             ph ^= 1;
@@ -164,6 +187,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         int s = 0;
         uint32_t ph = 0, it = 0;
         bool ok = true;
+        if (C::kResident && !mbar_wait_w(&bars->w_full, 0, abort)) ok = false;
         for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, ++it) {
             const int buf = C::kAccBufs == 2 ? (int)(it & 1) : 0;
             const uint32_t use = C::kAccBufs == 2 ? (it >> 1) : it;  // uses of this buffer so far
@@ -172,13 +196,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int g = 0; g < C::kG && ok; ++g)
 #pragma unroll 1
                 for (int kb = 0; kb < C::kKB; ++kb) {
-                    if (!mbar_wait_w(&bars->a_full[s], ph, abort) || !mbar_wait_w(&bars->b_full[s], ph, abort)) {
+                    if (!mbar_wait_w(&bars->a_full[s], ph, abort) ||
+                        (!C::kResident && !mbar_wait_w(&bars->b_full[s], ph, abort))) {
                         ok = false;
                         break;
                     }
                     fence_async_shared();  // the gathered rows are read by the tensor core
                     tc_fence_after();
-                    const uint32_t a0 = smem_u32(stage_a(s)), b0 = smem_u32(stage_b(s));
+                    const uint32_t a0 = smem_u32(stage_a(s)), b0 = smem_u32(b_block(s, g, kb));
 #pragma unroll
                     for (int k = 0; k < 4; ++k)
                         mma_f16_ss_w(tmem + buf * 256 + g * C::kNP, sdesc(a0 + k * 32, SW128), sdesc(b0 + k * 32, SW128),
@@ -486,9 +511,11 @@ int run_codec(prism_ctx* ctx, const int32_t* q, const __half* weights, size_t we
     a.bias = cs.bias[KIND];
     a.err = ctx->err;
     const int n_tiles = (int)((out_px + 127) / 128);
-    cudaError_t e = cudaFuncSetAttribute(codec_tc_kernel<KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    constexpr int smem = codec_smem<KIND>();
+    static_assert(smem <= 232448, "shared memory budget");
+    cudaError_t e = cudaFuncSetAttribute(codec_tc_kernel<KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e == cudaSuccess) {
-        codec_tc_kernel<KIND><<<std::min(ctx->sm_count, n_tiles), kThreads, kSmem, s>>>(a, tm);
+        codec_tc_kernel<KIND><<<std::min(ctx->sm_count, n_tiles), kThreads, smem, s>>>(a, tm);
         e = cudaGetLastError();
     }
     if (e != cudaSuccess) return set_error(PRISM_E_CUDA, "prism_codec_pass: %s", cudaGetErrorString(e));
