@@ -435,6 +435,24 @@ def run_ours(args):
     ms_b1_graph = max_over_ranks(e0.elapsed_time(e1) / n1)
     del g
     st.status()
+    # the same graph with the attention tiles on one CTA each (PRISM_OPT_PAIR_ATTENTION off):
+    # what the CTA-pair latency path gains at batch 1
+    st.set_pair_attention(False)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        st.forward(x1, o1)
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(n1):
+        g.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms_b1_graph_one_cta = max_over_ranks(e0.elapsed_time(e1) / n1)
+    del g
+    st.set_pair_attention(True)
+    st.status()
     # batch 1 is bound by streaming the weights the frame touches from HBM
     asg1 = torch.empty((max(1, L.n_moe_blocks), T), dtype=torch.int32, device="cuda")
     st.forward(x1, o1, asg1 if L.n_moe_blocks else None)
@@ -499,6 +517,7 @@ def run_ours(args):
                            "parallelism": f"frame-sharded x{ws}, weights replicated",
                            "l2": "inputs/activations larger than L2 (134 MB in, 267 MB per activation buffer)",
                            "frames_per_s": B * ws / (ms / 1e3), "batch1_ms": ms_b1, "batch1_graph_ms": ms_b1_graph,
+                           "batch1_graph_ms_one_cta_attention": ms_b1_graph_one_cta,
                            "batch1_roofline": b1_roof,
                            "output_gather": gather,
                            "tflops_effective": flops_step / (ms / 1e3) / 1e12,

@@ -350,6 +350,21 @@ enum prism_kernel_kind {
 int prism_stack_profile(prism_stack* st, int enable);
 int prism_stack_profile_read(prism_stack* st, double* ms, int64_t* launches, int n_kinds);
 
+/* Stack options (no counterpart in the reference, whose engine has one dispatch plan).
+ * PRISM_OPT_PAIR_ATTENTION (default 1): forwards of dim-256 blocks whose attention has at
+ * most half as many 128-row tiles as the GPU has SMs (one 68x120 frame: 68 tiles) split every
+ * tile's heads over a cluster of two CTAs, which shortens the serial chain per tile (the
+ * batch-1 latency path); 0 keeps one CTA per tile.  Results are bit-identical either way.
+ * PRISM_OPT_BUCKET_ROUTING (default 1): the router of a MoE block writes every token into its
+ * expert's bucket (one bucket per expert with room for all tokens: max experts x rows int32,
+ * allocated at prism_stack_create when that is at most 256 MB) and the grouped expert kernel
+ * plans its tiles from the counts, so a MoE block is two launches instead of three; 0, or a
+ * stack over the budget, builds the compact permutation with the route kernel.  Results are
+ * bit-identical either way (each expert row depends only on its own token).
+ * Returns PRISM_E_ARG for an unknown option. */
+enum prism_stack_option { PRISM_OPT_PAIR_ATTENTION = 1, PRISM_OPT_BUCKET_ROUTING = 2 };
+int prism_stack_set_option(prism_stack* st, int option, int value);
+
 /* Number of kernel launches one prism_stack_forward issues for `frames`. */
 int prism_stack_launch_count(const prism_stack* st, int frames);
 

@@ -194,6 +194,14 @@ class Stack:
         next status() raises PRISM_E_TIMEOUT after the library's wait limit."""
         check(self.lib, self.lib.prism_stack_inject_stall(self.h, _stream(stream)))
 
+    def set_pair_attention(self, enable: bool):
+        """PRISM_OPT_PAIR_ATTENTION: few-tile dim-256 attention on CTA pairs (default on)."""
+        check(self.lib, self.lib.prism_stack_set_option(self.h, abi.OPT_PAIR_ATTENTION, int(enable)))
+
+    def set_bucket_routing(self, enable: bool):
+        """PRISM_OPT_BUCKET_ROUTING: router-filled expert buckets, no route kernel (default on)."""
+        check(self.lib, self.lib.prism_stack_set_option(self.h, abi.OPT_BUCKET_ROUTING, int(enable)))
+
     def profile(self, enable: bool = True):
         check(self.lib, self.lib.prism_stack_profile(self.h, int(enable)))
 

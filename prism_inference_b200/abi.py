@@ -85,7 +85,7 @@ EXPORTS = ("prism_create", "prism_destroy", "prism_last_error_string", "prism_ab
            "prism_attn_window", "prism_router", "prism_expert", "prism_proj_up",
            "prism_proj_down", "prism_dense_block", "prism_stack_create", "prism_stack_destroy",
            "prism_stack_forward", "prism_stack_status", "prism_stack_launch_count",
-           "prism_stack_tokens_per_frame", "prism_stack_profile", "prism_stack_profile_read",
+           "prism_stack_tokens_per_frame", "prism_stack_profile", "prism_stack_profile_read", "prism_stack_set_option",
            "prism_expert_all_static", "prism_stack_inject_stall", "prism_stack_infer",
            "prism_stack_submit", "prism_stack_wait", "prism_moe_block", "prism_stack_infer_gpu",
            "prism_codec_pass", "prism_ctx_status")
@@ -94,6 +94,9 @@ CODEC_KINDS = ("conv3x3_coopvec_9ch", "strided_conv_coopvec_32ch", "strided_conv
                "strided_conv_split_128ch", "dec3_fused", "dec2_fused", "dec1_fused",
                "pw_conv_coopvec_32to12", "pixelshuffle_sigmoid")
 STATIC_MAX_TOKENS = 65536  # PRISM_STATIC_MAX_TOKENS
+# prism_stack_option
+OPT_PAIR_ATTENTION = 1
+OPT_BUCKET_ROUTING = 2
 KERNEL_KINDS = ("proj_up", "attn", "router", "route", "expert", "dense_ffn", "proj_down", "copy")
 
 _lib = None
@@ -137,6 +140,7 @@ def load(path: os.PathLike | None = None) -> C.CDLL:
         "prism_stack_launch_count": (i32, [vp, i32]),
         "prism_stack_tokens_per_frame": (i32, [vp]),
         "prism_stack_profile": (i32, [vp, i32]),
+        "prism_stack_set_option": (i32, [vp, i32, i32]),
         "prism_expert_all_static": (i32, [vp, C.POINTER(ExpertParams), C.c_int32, C.c_int32, vp, sz, vp, sz, vp,
                                           sz, vp]),
         "prism_stack_profile_read": (i32, [vp, C.POINTER(C.c_double), C.POINTER(C.c_int64), i32]),

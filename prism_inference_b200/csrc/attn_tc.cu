@@ -39,6 +39,7 @@
 // (~300-400 cycles) whatever its size, so few large loads keep the stream ahead.
 // Every wait is bounded (common.cuh); on timeout the CTA sets the error word and
 // winds down.  No TMA multicast.
+#include "attn_parts.cuh"
 #include "attn_tc.cuh"
 #include "common.cuh"
 
@@ -103,52 +104,6 @@ struct Counter {  // phase bookkeeping of one barrier as seen by one role
     PRISM_DEV uint32_t next() { return (n++) & 1u; }              // consumer: wait phase parity
     PRISM_DEV uint32_t next_free() { return ((n++) & 1u) ^ 1u; }  // producer of a free slot
 };
-
-// y = fp16(fp16(PO + bo) + x) for the 32 columns [32g, 32g + 32) of tile row r (v = PO of
-// those columns), written over X in its swizzled slot (bo staged in shared memory).
-PRISM_DEV void y_chunk(unsigned char* sX, const uint32_t (&v)[32], int r, const float* bo, int g) {
-    unsigned char* xblk = sX + (g >> 1) * 16384;
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-        const int off = sw128_off(r, (g & 1) * 4 + c);
-        const uint4 x = *reinterpret_cast<const uint4*>(xblk + off);
-        const float4 b0 = *reinterpret_cast<const float4*>(bo + g * 32 + 8 * c);
-        const float4 b1 = *reinterpret_cast<const float4*>(bo + g * 32 + 8 * c + 4);
-        const float* fv = reinterpret_cast<const float*>(&v[8 * c]);
-        // y = h( h(PO + bo) + x ): the second rounding is the fp16 add of :76
-        uint4 y;
-        y.x = hadd2_u32(add_pack_h2(fv[0], fv[1], b0.x, b0.y), x.x);
-        y.y = hadd2_u32(add_pack_h2(fv[2], fv[3], b0.z, b0.w), x.y);
-        y.z = hadd2_u32(add_pack_h2(fv[4], fv[5], b1.x, b1.y), x.z);
-        y.w = hadd2_u32(add_pack_h2(fv[6], fv[7], b1.z, b1.w), x.w);
-        *reinterpret_cast<uint4*>(xblk + off) = y;
-    }
-}
-
-// One SIMT group's share of y: chunk 2kb + part of every K-block kb < KB, in order, each K-block
-// announced on y_ready[kb] (with the other group's chunk it completes the K-block).  The
-// TMEM load of the next chunk is in flight while the current one is computed; the router
-// GEMM writes logits only over K-blocks already announced, so the load in flight is never
-// overwritten.
-template <int KB>
-PRISM_DEV void y_share(unsigned char* sX, uint32_t row_taddr, int r, const float* bo, int part, uint64_t* y_ready,
-                       int lane) {
-    uint32_t va[32], vb[32];
-    tmem_ld32(row_taddr + kTPO + part * 32, va);
-    tmem_ld_wait();
-#pragma unroll
-    for (int kb = 0; kb < KB; ++kb) {
-        uint32_t(&cur)[32] = (kb & 1) ? vb : va;
-        uint32_t(&nxt)[32] = (kb & 1) ? va : vb;
-        if (kb < KB - 1) tmem_ld32(row_taddr + kTPO + (2 * (kb + 1) + part) * 32, nxt);
-        y_chunk(sX, cur, r, bo, 2 * kb + part);
-        fence_async_shared();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&y_ready[kb]);
-        if (kb < KB - 1) tmem_ld_wait();
-    }
-}
 
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -215,7 +170,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = bars->tmem_base;
-    grid_dep_wait();  // x and the routing counters come from the previous kernels
+    // Programmatic dependent launch: the next kernel may place its CTAs now (they wait for this
+    // grid to complete before reading its results).  This grid's own wait for the previous
+    // kernels is taken only by the roles that touch their memory: the producer after the first
+    // weight load (x, and y over the previous kernel's input) and the drain group (routing
+    // outputs); the weights and biases are never written by a forward.
+    grid_dep_launch();
 
     if (warp == 0) {
         // ============================ TMA producer ============================
@@ -275,6 +235,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // 2, 4, 6 and after head 7, the Wo columns of the pair before
                 constexpr uint32_t kQkvBytes = 96 * 128 * kKB, kWoBytes = D * 128;
                 ok = ring_load(&tm_wqkv, true, 0, 0, kQkvBytes);
+                if (prev < 0) grid_dep_wait();
                 if (ok && prev >= 0) ok = store_y(prev);
                 // each X K-block once the previous tile's y K-block has been read by its store
                 // and by the router GEMM (x_free)
@@ -468,67 +429,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tmem_ld32(tmem + lane_addr + kTS + wnd * 64, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
                 tmem_ld32(tmem + lane_addr + kTS + wnd * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
                 tmem_ld_wait();
-                // s_j = acc_j * scale; p_j = exp(s_j - max_j s_j).  scale > 0, so the max of
-                // the scaled scores is the scaled max; exp(x) = 2^(x log2 e).
                 uint32_t pk[32];
-                float se;
-                if (nkeys >= 64) {
-                    float m0 = __uint_as_float(sv[0]), m1 = __uint_as_float(sv[1]), m2 = __uint_as_float(sv[2]),
-                          m3 = __uint_as_float(sv[3]);
-#pragma unroll
-                    for (int j = 4; j < 64; j += 4) {
-                        m0 = fmaxf(m0, __uint_as_float(sv[j]));
-                        m1 = fmaxf(m1, __uint_as_float(sv[j + 1]));
-                        m2 = fmaxf(m2, __uint_as_float(sv[j + 2]));
-                        m3 = fmaxf(m3, __uint_as_float(sv[j + 3]));
-                    }
-                    const float mc = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3)) * c2;
-                    // the per-key fma(s, scale log2 e, -max) and the four running sums as
-                    // f32x2 pairs (the same operations per element)
-                    const uint64_t c22 = f2_pack(c2, c2), nmc = f2_pack(-mc, -mc);
-                    uint64_t s01 = f2_pack(0.f, 0.f), s23 = f2_pack(0.f, 0.f);
-#pragma unroll
-                    for (int j = 0; j < 64; j += 4) {
-                        float a0, a1, a2, a3;
-                        f2_unpack(f2_fma(f2_pack(__uint_as_float(sv[j]), __uint_as_float(sv[j + 1])), c22, nmc), a0, a1);
-                        f2_unpack(f2_fma(f2_pack(__uint_as_float(sv[j + 2]), __uint_as_float(sv[j + 3])), c22, nmc), a2, a3);
-                        const float p0 = ex2_approx(a0), p1 = ex2_approx(a1), p2 = ex2_approx(a2), p3 = ex2_approx(a3);
-                        s01 = f2_add(s01, f2_pack(p0, p1));
-                        s23 = f2_add(s23, f2_pack(p2, p3));
-                        pk[j >> 1] = pack_h2(p0, p1);
-                        pk[(j >> 1) + 1] = pack_h2(p2, p3);
-                    }
-                    float s0, s1, s2, s3;
-                    f2_unpack(s01, s0, s1);
-                    f2_unpack(s23, s2, s3);
-                    se = (s0 + s1) + (s2 + s3);
-                } else {
-                    // frames of fewer than 64 tokens: keys are the first n_keys slots (:33)
-                    float m = -1e9f;
-#pragma unroll
-                    for (int j = 0; j < 64; ++j)
-                        if (j < nkeys) m = fmaxf(m, __uint_as_float(sv[j]));
-                    const float mc = m * c2;
-                    se = 0.f;
-#pragma unroll
-                    for (int j = 0; j < 64; j += 2) {
-                        const float p0 = j < nkeys ? ex2_approx(fmaf(__uint_as_float(sv[j]), c2, -mc)) : 0.f;
-                        const float p1 = j + 1 < nkeys ? ex2_approx(fmaf(__uint_as_float(sv[j + 1]), c2, -mc)) : 0.f;
-                        se += p0 + p1;
-                        pk[j >> 1] = pack_h2(p0, p1);
-                    }
-                }
+                const float se = attn_softmax_row(sv, c2, nkeys, pk);
                 const float inv = __frcp_rn(fmaxf(se, 1e-6f));
-                {
-                    // P row: keys of window A in columns [0, 32), window B in [32, 64);
-                    // this row's keys get the weights, the other window's keys zero
-                    uint32_t zero[32];
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) zero[j] = 0u;
-                    tmem_st32(tmem + lane_addr + kTS + wnd * 32, pk);
-                    tmem_st32(tmem + lane_addr + kTS + (wnd ^ 1) * 32, zero);
-                    tmem_st_wait();
-                }
+                attn_store_p(tmem + lane_addr + kTS, wnd, pk);
                 tc_fence_before();
                 arrive(&bars->p_ready);
 
@@ -542,13 +446,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tmem_ld32(tmem + lane_addr + kTO, v);
                     tmem_ld_wait();
                     uint32_t po[16];
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) {  // O / sum, as f32x2 pairs
-                        float o0, o1;
-                        f2_unpack(f2_mul(f2_pack(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1])), f2_pack(inv, inv)),
-                                  o0, o1);
-                        po[j] = pack_h2(o0, o1);
-                    }
+                    attn_scale_o(v, inv, po);
 #pragma unroll
                     for (int c = 0; c < 4; ++c)
                         *reinterpret_cast<uint4*>(sAO + sw128_off(r, (h & 1) * 4 + c)) =
@@ -589,33 +487,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(bar);
         };
+        grid_dep_wait();  // the routing outputs of the previous block are consumed
         // QKV_h (TMEM) -> fp16 Q, K (K-major SW64) and V (key-major SW64, buffer h&1)
         auto drain_qkv = [&](int h) {
             wait(&bars->qkv_full, c_qkv.next());
             if (!ok) return;
-            const float* bq = bars->bqkv + h * 96;
-#pragma unroll
-            for (int part = 0; part < 3; ++part) {  // Q, K, V
-                uint32_t v[32];
-                tmem_ld32(tmem + lane_addr + kTQKV + part * 32, v);
-                float4 bb[8];
-#pragma unroll
-                for (int i = 0; i < 8; ++i) bb[i] = *reinterpret_cast<const float4*>(bq + part * 32 + 4 * i);
-                tmem_ld_wait();
-                uint32_t pk[16];
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    pk[2 * i] = add_pack_h2(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]), bb[i].x, bb[i].y);
-                    pk[2 * i + 1] = add_pack_h2(__uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]), bb[i].z, bb[i].w);
-                }
-                // Q, K and V rows alike: row r, 32 fp16 = four 16-byte chunks, SW64 (V is the
-                // MN-major B operand of PV, which has exactly this layout)
-                unsigned char* dst = part == 0 ? sQ : part == 1 ? sK : sV + (h & 1) * 8192;
-#pragma unroll
-                for (int c = 0; c < 4; ++c)
-                    *reinterpret_cast<uint4*>(dst + sw64_off(r, c)) =
-                        make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-            }
+            attn_drain_row(tmem + lane_addr + kTQKV, bars->bqkv + h * 96, r, sQ, sK, sV + (h & 1) * 8192);
             fence_async_shared();
             tc_fence_before();
             arrive(&bars->qkv_drained);
@@ -668,18 +545,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                     }
                 }
-                if (valid) {
-                    a.assign[token] = best;
-                    atomicAdd(&bars->hist[best], 1);
-                }
+                tc_fence_before();
+                arrive(&bars->lg_drained);  // the logits are read: the next tile's out-projection may go
+                route_token(a, bars->hist, valid, token, best, lane);
+            } else {
+                tc_fence_before();
+                arrive(&bars->lg_drained);
             }
-            tc_fence_before();
-            arrive(&bars->lg_drained);
             first_tile = false;
         }
         // flush the CTA's routing histogram once every drain warp is done
         arrive(&bars->ep_done);
-        if (mbar_wait(&bars->ep_done, 0, abort) && router)
+        if (mbar_wait(&bars->ep_done, 0, abort) && router && !a.perm_b)
             for (int e = threadIdx.x - 192; e < a.n_experts; e += 128)
                 if (bars->hist[e]) atomicAdd(&a.counts[e], bars->hist[e]);
     }

@@ -17,6 +17,12 @@ struct AttnTcArgs {
     const float* br;         // [n_experts_pad]
     int32_t* assign;         // [frames * W * H] expert of every token
     int32_t* counts;         // [n_experts] += tokens routed
+    // Bucket permutation (nullable): token t routed to expert e goes to perm_b[e * perm_stride + k],
+    // k = the value counts[e] had before this token (so counts doubles as the bucket cursor), and
+    // the grouped expert kernel reads its tiles straight from the buckets; null: the CTA
+    // histograms are added to counts and the route kernel builds the permutation.
+    int32_t* perm_b;
+    int perm_stride;         // bucket capacity, >= the tokens of the forward
     uint32_t* err;
 };
 
@@ -28,5 +34,11 @@ cudaError_t launch_attn_tc(int dim, const AttnTcArgs& a, const CUtensorMap& x, c
                            const CUtensorMap& wqkv, const CUtensorMap& wo, const CUtensorMap& wr, int grid,
                            cudaStream_t s);
 int attn_tc_smem_bytes(int dim);
+
+// The same block at D = 256 with every tile's heads split over a cluster of two CTAs (the
+// latency path for forwards of few tiles): 2 * n_tiles CTAs, one tile per cluster; same maps.
+cudaError_t launch_attn_pair(const AttnTcArgs& a, const CUtensorMap& x, const CUtensorMap& y, const CUtensorMap& wqkv,
+                             const CUtensorMap& wo, const CUtensorMap& wr, int n_tiles, cudaStream_t s);
+int attn_pair_smem_bytes();
 
 }  // namespace prism

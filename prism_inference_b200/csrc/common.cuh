@@ -427,4 +427,94 @@ PRISM_DEV void named_bar_sync(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// ---- thread-block clusters (distributed shared memory between the CTAs of one cluster) ----
+PRISM_DEV uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// the shared::cluster address of the same shared-memory location in CTA `rank` of the cluster
+PRISM_DEV uint32_t peer_addr(uint32_t saddr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+    return r;
+}
+// whole-cluster execution barrier (every thread of every CTA); orders the shared-memory
+// writes before it (barrier initialisation) with the other CTAs' accesses after it
+PRISM_DEV void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// arrive on an mbarrier of another CTA of the cluster, releasing this thread's prior writes
+PRISM_DEV void mbar_arrive_peer(uint32_t bar_cluster) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+// arrive on a peer's mbarrier and raise its expected transaction bytes (the data follows by
+// cp.async.bulk into the peer's shared memory, completing on the same barrier)
+PRISM_DEV void mbar_expect_tx_peer(uint32_t bar_cluster, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.release.cluster.shared::cluster.b64 _, [%0], %1;" ::"r"(bar_cluster),
+                 "r"(bytes)
+                 : "memory");
+}
+// bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned) from this CTA's
+// shared memory into a peer CTA's shared memory; completes as transaction bytes on the
+// peer's mbarrier
+PRISM_DEV void bulk_copy_to_peer(uint32_t dst_cluster, uint32_t src, uint32_t bytes, uint32_t bar_cluster) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            dst_cluster),
+        "r"(src), "r"(bytes), "r"(bar_cluster)
+        : "memory");
+}
+// try_wait with cluster-scope acquire: for barriers that peers arrive on
+PRISM_DEV bool mbar_try_wait_cl(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+static __device__ __noinline__ bool mbar_wait_cl_spin(uint64_t* bar, uint32_t parity, volatile int* abort) {
+    uint64_t t0 = globaltimer();
+    for (uint32_t it = 1;; ++it) {
+        if (mbar_try_wait_cl(bar, parity)) return true;
+        if ((it & 255u) == 0) {
+            if (*abort) return false;
+            if (globaltimer() - t0 > kWaitLimitNs) {
+                *abort = 1;
+                return false;
+            }
+        }
+    }
+}
+// bounded wait (as mbar_wait) on a barrier that a peer CTA arrives on
+PRISM_DEV bool mbar_wait_cl(uint64_t* bar, uint32_t parity, volatile int* abort) {
+    if (mbar_try_wait_cl(bar, parity)) return true;
+    return mbar_wait_cl_spin(bar, parity, abort);
+}
+
+// launch with programmatic dependent launch and thread-block clusters of `cluster` CTAs
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, int cluster,
+                                      cudaStream_t s, Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = cluster;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 }  // namespace prism

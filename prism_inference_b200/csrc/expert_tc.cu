@@ -55,6 +55,11 @@ struct Bars {
     uint64_t a_full, a_empty, acc1_full, acc1_empty, h_full[4], acc2_full, acc2_empty, drain;
     uint32_t tmem_base;
     int abort;
+    // bucket routing: inclusive prefix of the experts' tile counts, the rows of each expert's
+    // last tile (1..128), the tile count and scan scratch
+    int tinc[256];
+    uint8_t last_rows[256];
+    int n_tiles, wsum[8], wcnt[8];
 };
 constexpr int kSmem = kOffBar + (int)sizeof(Bars) + 1024;  // + alignment slack of the dynamic base
 static_assert(kSmem <= 232448, "shared memory budget");
@@ -64,6 +69,81 @@ static_assert(kSmem <= 232448, "shared memory budget");
 PRISM_DEV constexpr int h_order(int i) { return (i & 1) * 2 + (i >> 1); }
 // TMEM column of H K-block kb (32 columns = 64 fp16 K values)
 PRISM_DEV constexpr uint32_t h_col(int kb) { return kAcc1 + 128u * (kb >> 1) + 32u * (kb & 1); }
+
+// Tile i of the launch: from the route kernel's list, or (bucket routing) from the prefix of the
+// experts' tile counts: expert e = the first whose inclusive prefix exceeds i.
+PRISM_DEV ExpertTile tile_at(const FfnArgs& a, const Bars* bars, int i) {
+    if (a.tiles) return a.tiles[i];
+    int lo = 0, hi = a.n_route - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (bars->tinc[mid] > i) hi = mid;
+        else lo = mid + 1;
+    }
+    const int first = lo > 0 ? bars->tinc[lo - 1] : 0;  // the expert's first tile
+    const int j = i - first;
+    ExpertTile t;
+    t.expert = lo;
+    t.start = lo * a.perm_stride + j * 128;
+    t.rows = j == bars->tinc[lo] - first - 1 ? (int)bars->last_rows[lo] : 128;
+    t.pad = 0;
+    return t;
+}
+
+// Bucket routing, by every CTA after the grid dependency wait: the counts -> the tile prefix
+// (two-level shuffle scan over 256 entries, warps 0-7), the invariant sum(counts) == tokens
+// (otherwise: no tiles and ERR_ROUTE) and the copy of the counts (CTA 0).  Every thread of the
+// CTA calls it; release_counts() follows off the critical path.
+PRISM_DEV int plan_buckets(const FfnArgs& a, Bars* bars) {
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    const int n = a.n_route;
+    int c = 0;
+    if (tid < 256) {
+        c = tid < n ? a.route_counts[tid] : 0;
+        int t = (c + 127) >> 7, sum = c;
+        bars->last_rows[tid] = (uint8_t)(c - ((t > 0 ? t : 1) - 1) * 128);
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+            const int tv = __shfl_up_sync(0xffffffffu, t, d), sv = __shfl_up_sync(0xffffffffu, sum, d);
+            if (lane >= d) {
+                t += tv;
+                sum += sv;
+            }
+        }
+        bars->tinc[tid] = t;
+        if (lane == 31) {
+            bars->wsum[w] = t;
+            bars->wcnt[w] = sum;
+        }
+    }
+    __syncthreads();
+    if (tid < 256) {
+        int off = 0;
+        for (int v = 0; v < w; ++v) off += bars->wsum[v];
+        bars->tinc[tid] += off;
+    }
+    if (blockIdx.x == 0 && a.counts_out && tid < n) a.counts_out[tid] = c;
+    __syncthreads();
+    if (tid == 0) {
+        int tokens = 0;
+        for (int v = 0; v < 8; ++v) tokens += bars->wcnt[v];
+        const bool consistent = tokens == a.n_rows;
+        if (!consistent && blockIdx.x == 0) atomicOr(a.err, ERR_ROUTE);
+        bars->n_tiles = consistent ? bars->tinc[255] : 0;
+    }
+    __syncthreads();
+    return bars->n_tiles;
+}
+
+// Bucket routing, one thread per CTA once plan_buckets() has returned (the CTA's reads of the
+// counts are complete): the last CTA to arrive clears the counts for the next router.
+PRISM_DEV void release_counts(const FfnArgs& a) {
+    __threadfence();
+    if (atomicAdd(a.route_done, 1u) == gridDim.x - 1) {
+        for (int i = 0; i < a.n_route; ++i) a.route_counts[i] = 0;
+        *a.route_done = 0;
+    }
+}
 
 // staging-tile address of (tile row R, column col): K-major SW128 K-blocks of 64 columns
 PRISM_DEV unsigned char* oslot(unsigned char* sO, int R, int col) {
@@ -105,15 +185,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = bars->tmem_base;
-    grid_dep_wait();  // tile list, permutation and rows come from the previous kernels
-    const int n_tiles = *a.n_tiles;
-    // the routing kernel is done with the counts and cursors: clear them for the next block's
-    // router (which starts only after this kernel completes)
-    if (blockIdx.x == 0 && a.route_counts)
-        for (int i = threadIdx.x; i < a.n_route; i += blockDim.x) {
-            a.route_counts[i] = 0;
-            a.route_cursor[i] = 0;
-        }
+    grid_dep_launch();  // the next kernel may place its CTAs (it waits for this grid to complete)
+    grid_dep_wait();    // tile list, permutation and rows come from the previous kernels
+    int n_tiles;
+    if (a.tiles) {
+        n_tiles = *a.n_tiles;
+        // the routing kernel is done with the counts and cursors: clear them for the next
+        // block's router (which starts only after this kernel completes)
+        if (blockIdx.x == 0 && a.route_counts)
+            for (int i = threadIdx.x; i < a.n_route; i += blockDim.x) {
+                a.route_counts[i] = 0;
+                a.route_cursor[i] = 0;
+            }
+    } else {
+        n_tiles = plan_buckets(a, bars);
+    }
 
     if (warp == 0) {
         // ============================ producer ============================
@@ -134,10 +220,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 return true;
             };
             for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
-                const int e = a.tiles[tile].expert;
+                const int e = tile_at(a, bars, tile).expert;
                 for (int kc = 0; kc < 4 && ok; ++kc) ok = load(&tm_w1, kc * 64, e * kD);      // W1_e
                 for (int i = 0; i < 4 && ok; ++i) ok = load(&tm_w2, h_order(i) * 64, e * kD);  // W2_e
             }
+        } else if (lane == 1 && !a.tiles) {
+            release_counts(a);
         }
     } else if (warp == 2 || warp == kGather2) {
         // ============================ row gather ============================
@@ -148,7 +236,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t a_base = smem_u32(sA);
         const uint32_t dst_lane = a_base + (lane >> 3) * 16384;
         for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
-            const ExpertTile t = a.tiles[tile];
+            const ExpertTile t = tile_at(a, bars, tile);
             const int j0 = warp == 2 ? 0 : 2;  // this warp's row blocks: j0, j0 + 1 (32 rows each)
             int tok[4];                        // token of row 32j + lane (own blocks only)
 #pragma unroll
@@ -234,7 +322,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t it = 0;
         bool ok = true;
         for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, ++it) {
-            const int e = a.tiles[tile].expert;
+            const int e = tile_at(a, bars, tile).expert;
             // lane l holds bias columns 4l .. 4l+3 of the part, handed out by shuffles
             const float4 bias = ldg_f4(a.b1 + (size_t)e * kD + part * 128 + 4 * lane);
             if (!mbar_wait_w(&bars->acc1_full, it & 1, abort)) {
@@ -289,7 +377,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t it = 0;
         bool ok = true;
         for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, ++it) {
-            const ExpertTile t = a.tiles[tile];
+            const ExpertTile t = tile_at(a, bars, tile);
             const bool row_valid = row < t.rows;
             const int out_row = row_valid ? a.perm[t.start + row] : 0;
             // the residual rows (the tile's input rows, L2-resident) into this warp's slice of

@@ -356,6 +356,10 @@ extern "C" int prism_dense_block(prism_ctx* ctx, const prism_dense_params* p, in
 
 namespace {
 
+// Bucket routing needs max_experts * rows int32 slots (a bucket per expert that could take every
+// token); above this budget the route kernel builds a compact permutation instead.
+constexpr size_t kBucketBudget = 256ull << 20;
+
 struct FastBlock {
     prism_block_desc d;
     __half* w1 = nullptr;  // experts: [E][256][256]; dense: [hidden][D]
@@ -391,6 +395,13 @@ struct prism_stack {
     __half *act_a = nullptr, *act_b = nullptr, *act_y = nullptr;
     int32_t *assign_ws = nullptr, *counts = nullptr, *cursor = nullptr, *perm = nullptr,
             *n_tiles = nullptr;
+    // bucket routing (PRISM_OPT_BUCKET_ROUTING): the router writes each expert's tokens into a
+    // bucket of `rows` slots and the expert kernel plans its tiles from the counts, so no route
+    // kernel runs; allocated when max_experts * rows int32 fit kBucketBudget
+    int32_t* perm_b = nullptr;
+    uint32_t* route_done = nullptr;
+    bool bucket_routing = false;   // buffers allocated
+    bool use_buckets = true;        // PRISM_OPT_BUCKET_ROUTING
     ExpertTile* tiles = nullptr;
     uint32_t* err = nullptr;
     std::vector<void*> allocs;
@@ -403,6 +414,10 @@ struct prism_stack {
         cudaEvent_t in_ready[2] = {}, out_done[2] = {}, t0[2] = {}, t1[2] = {};
         int64_t next = 0;  // ticket of the next submission; slot = ticket & 1
     } stg;
+    // PRISM_OPT_PAIR_ATTENTION: dim-256 attention of forwards with at most sm_count / 2 tiles
+    // runs with each tile's heads split over a CTA pair (attn_pair.cu)
+    bool pair_attention = true;
+    int max_experts = 0;
     // per-kernel profiling (prism_stack_profile)
     bool profiling = false;
     std::vector<cudaEvent_t> ev_pool;
@@ -689,6 +704,14 @@ extern "C" int prism_stack_create(prism_ctx* ctx, const prism_stack_desc* desc, 
     if (cudaMemset(st->counts, 0, 256 * 4) != cudaSuccess || cudaMemset(st->cursor, 0, 256 * 4) != cudaSuccess ||
         cudaMemset(st->err, 0, 4) != cudaSuccess)
         return fail_cleanup(fail(PRISM_E_CUDA, "workspace memset failed"));
+    st->max_experts = st->n_moe ? max_experts : 0;
+    if (st->n_moe && (size_t)max_experts * rows * 4 <= kBucketBudget) {
+        if ((rc = dev_alloc(st, &st->perm_b, (size_t)max_experts * rows)) || (rc = dev_alloc(st, &st->route_done, 1)))
+            return fail_cleanup(rc);
+        if (cudaMemset(st->route_done, 0, 4) != cudaSuccess)
+            return fail_cleanup(fail(PRISM_E_CUDA, "workspace memset failed"));
+        st->bucket_routing = true;
+    }
     {
         if ((rc = make_map_2d(&st->tm_act_a, st->act_a, rows, D, 128)) ||
             (rc = make_map_2d(&st->tm_act_b, st->act_b, rows, D, 128)) ||
@@ -715,7 +738,8 @@ extern "C" int prism_stack_launch_count(const prism_stack* st, int frames) {
     if (!st || frames <= 0) return 0;
     int n = (st->desc.up_w >= 0 ? 1 : 0) + (st->desc.down_w >= 0 ? 1 : 0);
     // MoE (dim 256): attention with the fused router, routing, experts; dense: attention, FFN
-    for (const auto& b : st->blocks) n += b.d.kind == PRISM_BLOCK_MOE ? 3 : 2;
+    const bool buckets = st->bucket_routing && st->use_buckets;
+    for (const auto& b : st->blocks) n += b.d.kind == PRISM_BLOCK_MOE && !buckets ? 3 : 2;
     if (st->desc.down_w < 0 && st->blocks.empty()) n += 1;  // plain copy
     return n;
 }
@@ -730,6 +754,7 @@ extern "C" int prism_stack_status(prism_stack* st, void* stream) {
     if (e) {  // a forward that gave up may have left routing counts behind: start the next one clean
         CUDA_TRY(cudaMemsetAsync(st->counts, 0, 256 * 4, as_stream(stream)));
         CUDA_TRY(cudaMemsetAsync(st->cursor, 0, 256 * 4, as_stream(stream)));
+        if (st->route_done) CUDA_TRY(cudaMemsetAsync(st->route_done, 0, 4, as_stream(stream)));
     }
     CUDA_TRY(cudaStreamSynchronize(as_stream(stream)));
     if (e & ERR_TIMEOUT) return fail(PRISM_E_TIMEOUT, "a device-side wait timed out (error word 0x%x)", e);
@@ -834,13 +859,40 @@ int stack_forward(prism_stack* st, const void* in, void* out, int frames, int32_
         ta.br = b.br;
         ta.assign = asg;
         ta.counts = st->counts;
+        const bool buckets = b.d.kind == PRISM_BLOCK_MOE && st->bucket_routing && st->use_buckets;
+        ta.perm_b = buckets ? st->perm_b : nullptr;
+        ta.perm_stride = (int)rows;
         ta.err = st->err;
         const int n_win = ((d.spatial_w + 7) / 8) * ((d.spatial_h + 7) / 8) * frames;
         {
             KernelTimer kt(st, s, PRISM_K_ATTN);
-            CUDA_TRY(launch_attn_tc(D, ta, tm_x, tm_y, b.tm_wqkv, b.tm_wo, b.tm_wr, std::min(grid, (n_win + 1) / 2), s));
+            const int n_attn_tiles = (n_win + 1) / 2;
+            if (D == 256 && st->pair_attention && 2 * n_attn_tiles <= grid)
+                CUDA_TRY(launch_attn_pair(ta, tm_x, tm_y, b.tm_wqkv, b.tm_wo, b.tm_wr, n_attn_tiles, s));
+            else
+                CUDA_TRY(launch_attn_tc(D, ta, tm_x, tm_y, b.tm_wqkv, b.tm_wo, b.tm_wr, std::min(grid, n_attn_tiles), s));
         }
-        if (b.d.kind == PRISM_BLOCK_MOE) {
+        if (b.d.kind == PRISM_BLOCK_MOE && buckets) {
+            // the router filled the buckets: the expert kernel plans its tiles from the counts
+            FfnArgs fa{};
+            fa.x = st->act_y;
+            fa.y = nxt;
+            fa.perm = st->perm_b;
+            fa.tiles = nullptr;
+            fa.n_tiles = nullptr;
+            fa.perm_stride = (int)rows;
+            fa.route_done = st->route_done;
+            fa.counts_out = counts_out;
+            fa.b1 = b.b1;
+            fa.b2 = b.b2;
+            fa.err = st->err;
+            fa.route_counts = st->counts;
+            fa.route_cursor = nullptr;
+            fa.n_route = b.d.n_experts;
+            fa.n_rows = (int)rows;
+            KernelTimer kt(st, s, PRISM_K_EXPERT);
+            CUDA_TRY(launch_ffn_expert256(fa, b.tm_w1, b.tm_w2, grid, s));
+        } else if (b.d.kind == PRISM_BLOCK_MOE) {
             RouteArgs ra_;
             ra_.counts = st->counts;
             ra_.counts_out = counts_out;
@@ -1072,6 +1124,20 @@ extern "C" int prism_stack_infer(prism_stack* st, const void* host_in, void* hos
     CUDA_TRY(cudaEventSynchronize(st->stg.out_done[p]));
     if (gpu_ms) CUDA_TRY(cudaEventElapsedTime(gpu_ms, st->stg.t0[p], st->stg.t1[p]));
     return prism_stack_status(st, st->stg.s_fwd);
+}
+
+extern "C" int prism_stack_set_option(prism_stack* st, int option, int value) {
+    if (!st) return fail(PRISM_E_ARG, "prism_stack_set_option: NULL");
+    switch (option) {
+        case PRISM_OPT_PAIR_ATTENTION:
+            st->pair_attention = value != 0;
+            return PRISM_OK;
+        case PRISM_OPT_BUCKET_ROUTING:
+            st->use_buckets = value != 0;
+            return PRISM_OK;
+        default:
+            return fail(PRISM_E_ARG, "prism_stack_set_option: unknown option %d", option);
+    }
 }
 
 extern "C" int prism_stack_profile(prism_stack* st, int enable) {

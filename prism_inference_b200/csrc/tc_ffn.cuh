@@ -35,6 +35,13 @@ struct FfnArgs {
     int32_t* route_counts;     // FFN_EXPERT: the router's counts and the scatter cursors, cleared by
     int32_t* route_cursor;     //   the expert kernel for the next MoE block (nullable)
     int n_route;               // FFN_EXPERT: entries of route_counts / route_cursor
+    // FFN_EXPERT with tiles == nullptr: bucket routing.  Expert e's rows are the tokens
+    // perm[e * perm_stride + k], k < route_counts[e] (written by the router, attn_tc.cuh); every
+    // CTA derives the tile list from the counts itself, and the last CTA to read them clears them
+    // (route_done counts the CTAs that have read; it is zero between launches).
+    int perm_stride;
+    uint32_t* route_done;
+    int32_t* counts_out;       // optional copy of the counts (bucket routing)
 };
 
 // Grouped expert FFN (expert_tc.cu): w1, w2 = 2-D [E*256][256] maps with box {64, 256}; the token

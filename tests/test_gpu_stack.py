@@ -13,10 +13,12 @@ from prism_inference_b200 import Prism, Stack, configs, layout, synth
 pytestmark = pytest.mark.gpu
 
 
-def _run(ctx, L, blob, x, max_frames=None):
+def _run(ctx, L, blob, x, max_frames=None, pair=True, buckets=True):
     import torch
     F = x.shape[0]
     st = Stack(ctx, L, blob, max_frames or F)
+    st.set_pair_attention(pair)
+    st.set_bucket_routing(buckets)
     xd = torch.from_numpy(x.view(np.int16)).cuda().view(torch.float16)
     out = torch.empty((F, L.tokens, L.out_dim), dtype=torch.float16, device="cuda")
     asg = torch.full((max(1, L.n_moe_blocks), F * L.tokens), -1, dtype=torch.int32, device="cuda")
@@ -78,6 +80,34 @@ def test_stack_odd_frame_shapes(prism_ctx, oracle, w, h, frames):
     blob = synth.make_blob(L)
     x = synth.make_frames(L, frames)
     _check(prism_ctx, oracle, L, blob, x, f"{w}x{h}x{frames}")
+
+
+@pytest.mark.parametrize("what,dim_blocks,kw,frames", [
+    ("moe64 68x120", 2, dict(n_experts=64), 1),
+    ("moe100 68x120", 1, dict(n_experts=100), 1),
+    ("moe256 68x120", 1, dict(n_experts=256), 1),
+    ("dense256 68x120", 2, dict(ffn_hidden=1024, ffn_chunk=256), 1),
+    ("moe8 20x12", 2, dict(n_experts=8, spatial_w=20, spatial_h=12), 3),
+    ("moe8 4x4", 2, dict(n_experts=8, spatial_w=4, spatial_h=4), 1),
+    ("moe8 40x9", 1, dict(n_experts=8, spatial_w=40, spatial_h=9), 2),
+])
+def test_pair_attention_is_bit_identical(prism_ctx, oracle, what, dim_blocks, kw, frames):
+    """The latency paths against the plain ones: attention with each tile split over a CTA pair
+    (taken when a forward has at most sm_count / 2 attention tiles) against one CTA per tile, and
+    bucket routing (router-filled expert buckets, no route kernel) against the route kernel's
+    compact permutation: all four combinations give the same output and routing bit for bit, and
+    the default one matches the oracle within tolerance.  Covers one 68x120 frame, router widths
+    of 1-3 weight stages, a dense block, partial windows, a tile with one window and frames of
+    fewer than 64 tokens."""
+    L = layout.build_stack(256, dim_blocks, up_adapter=True, down_adapter=True, **kw)
+    blob = synth.make_blob(L)
+    x = synth.make_frames(L, frames)
+    o1, a1 = _check(prism_ctx, oracle, L, blob, x, what)
+    for pair, buckets in ((False, True), (True, False), (False, False)):
+        o0, a0 = _run(prism_ctx, L, blob, x, pair=pair, buckets=buckets)
+        how = f"{what} (pair {pair}, buckets {buckets})"
+        assert np.array_equal(a0, a1), f"{how}: routing differs from the default path"
+        assert np.array_equal(o0.view(np.int16), o1.view(np.int16)), f"{how}: outputs differ"
 
 
 @pytest.mark.parametrize("key", ["dense256x12", "dense128x4"])
