@@ -10,23 +10,24 @@
 //   - computes heads 4r..4r+3 (head pairs 2r, 2r+1) for all 128 rows: QKV_h, S_h, softmax,
 //     PV_h as attn_tc (the per-row steps of attn_parts.cuh);
 //   - owns window r: the out-projection, residual, y store and router of rows [64r, 64r + 64).
-// The attention output O of a head pair is therefore needed by both CTAs: each CTA sends the
-// other the rows of the other's window (64 rows x 128 B per pair, 16 KB in all) by
-// cp.async.bulk into the peer's shared memory (its Q/K/V buffers, free once its last PV has
-// completed); the peer's MMAs read them in place.  One exchange, no y exchange.
+// The attention output O of a head pair is therefore needed by both CTAs: the threads of the
+// peer's window rows write their O_h rows straight into the peer's shared memory with st.async
+// as each head finishes (a landing buffer per head pair, 64 rows x 128 B), and the stores
+// complete as transaction bytes on the peer's mbarrier of that pair; the peer's MMAs read the
+// rows in place.  No staging, no end-of-loop copy, no y exchange.
 // The out-projection accumulates the head pairs in the order 0, 1, 2, 3 on both CTAs, as
-// attn_tc does, so the fp32 sums round alike: rank 0 adds its own pairs while its heads run and
-// pairs 2, 3 when they arrive; rank 1 keeps its own pairs' rows and adds 0, 1, 2, 3 at the end.
-// An M = 128 MMA whose A rows of the other window are not needed reads them from whatever lies
-// before or after the needed 8 KB (those PO rows are never used).
-// Hand-offs between the CTAs are mbarriers: a CTA announces by a remote arrive that its landing
-// buffers are free; the sender arms the peer's barrier with the byte count and its bulk copies
-// complete on it.  All waits are bounded (common.cuh); on timeout a CTA sets the error word and
-// winds down, and its peer's waits for it time out likewise.  No TMA multicast.
+// attn_tc does, so the fp32 sums round alike: rank 0 adds its own pairs 0, 1 while its heads
+// run and the peer's 2, 3 as they land; rank 1 adds the peer's pair 0 while its heads run, then
+// pair 1 when it lands and its own pairs 2, 3, whose window rows it kept.  An M = 128 MMA whose
+// A rows of the other window are not needed reads them from whatever lies before or after the
+// needed 8 KB (those PO rows are never used).
+// All waits are bounded (common.cuh); on timeout a CTA sets the error word and winds down, and
+// its peer's waits for it time out likewise.  No TMA multicast.
 //
 // Warp roles (320 threads) as attn_tc: producer, MMA issuer, softmax group (warps 2-5) and drain
 // group (warps 6-9); the y epilogue and the router argmax run on the warps whose TMEM lanes are
-// the rows of the CTA's window.
+// the rows of the CTA's window.  The QKV biases are read through L1; the out-projection and
+// router biases are staged in shared memory (the router's as fp16, the blob's own precision).
 #include "attn_parts.cuh"
 #include "attn_tc.cuh"
 #include "common.cuh"
@@ -40,14 +41,14 @@ constexpr int kHeads = 4;             // heads per CTA (8 heads of 32 over the p
 constexpr int kRouterRows = 96;       // router rows per ring stage
 constexpr int kStage = 96 * 128 * 4;  // a head's Wqkv rows at full K (48 KB); Wo: 256 rows x 128 B
 // shared-memory map (offsets from the 1024-aligned base)
-constexpr int kOffX = 0;              // 4 K-blocks x [128][128 B] SW128; y overwrites its own rows
-constexpr int kOffQ = kOffX + 65536;  // Q_h [128][64 B] SW64; after the last PV: the landing of
-constexpr int kOffK = kOffQ + 8192;   //   the peer's O (2 K-blocks, this CTA's window rows)
-constexpr int kOffV = kOffK + 8192;   // V_h, 2 buffers (head parity)
-constexpr int kOffAO = kOffV + 16384; // rank 0: the current pair's O (SW128 K-block); rank 1: its
-                                      //   own window rows of both pairs (8 KB each)
-constexpr int kOffOut = kOffAO + 16384;  // the first pair's O rows of the peer's window (8 KB)
-constexpr int kOffW = kOffOut + 8192;    // weight ring
+constexpr int kOffX = 0;               // 4 K-blocks x [128][128 B] SW128; y overwrites its own rows
+constexpr int kOffQ = kOffX + 65536;   // Q_h [128][64 B] SW64
+constexpr int kOffK = kOffQ + 8192;    // K_h
+constexpr int kOffV = kOffK + 8192;    // V_h, 2 buffers (head parity)
+constexpr int kOffAO = kOffV + 16384;  // rank 0: the current pair's O (SW128 K-block); rank 1: its
+                                       //   own window rows of both pairs (8 KB each)
+constexpr int kOffL = kOffAO + 16384;  // landings: the peer's O rows of this window, pair 0 | pair 1
+constexpr int kOffW = kOffL + 16384;   // weight ring
 constexpr int kOffBar = kOffW + kStages * kStage;
 
 // TMEM columns (as attn_tc)
@@ -57,20 +58,20 @@ constexpr uint32_t kTS = 352;    // S_h [128]; P_h over [352, 416)
 constexpr uint32_t kTO = 480;    // PV_h [32]
 
 struct Bars {
-    float bqkv[kHeads * 96];  // this CTA's heads
-    float bo[256];
-    float br[256];
     uint64_t full[kStages], empty[kStages];
     uint64_t x_full[4], qkv_full, qkv_drained, s_full, p_ready, o_full, o_drained, ao_ready, ao_free;
-    // ao_staged: every O row for the peer and (rank 1) for itself is written;
-    // land_free: the peer's landing buffers are free (remote arrive);
-    // land_full: the peer's O rows arrived here (remote expect_tx + bulk copies)
-    uint64_t ao_staged, land_free, land_full, po_full, y_ready[4], lg_full, drain, ep_done;
+    // land[p]: the peer's 64 O rows of head pair p landed here (8 KB of st.async transactions);
+    // ao_staged: (rank 1) its own window rows of both pairs are written
+    uint64_t land[2], ao_staged, po_full, y_ready[4], lg_full, drain, ep_done;
     uint32_t tmem_base;
     int abort;
+    float bo[256];
+    __half br[256];
     int hist[256];
 };
-constexpr int kSmem = kOffBar + (int)sizeof(Bars) + 1024;  // + alignment slack of the dynamic base
+// No alignment slack: the dynamic shared memory of a kernel without static shared memory starts
+// 1024-aligned (checked at run time; a misaligned base would end the launch with an error).
+constexpr int kSmem = kOffBar + (int)sizeof(Bars);
 static_assert(kSmem <= 232448, "shared memory budget");
 
 struct Counter {
@@ -78,16 +79,16 @@ struct Counter {
     PRISM_DEV uint32_t next() { return (n++) & 1u; }
 };
 
-// own head pair whose out-projection rank 0 issues at head h: pair 0 behind QKV_3 (h = 2),
-// pair 1 after the last PV (h = 3)
-PRISM_DEV constexpr int own_pair(int h) { return h == 3 ? 1 : h == 2 ? 0 : -1; }
-
 __global__ void __launch_bounds__(kThreads, 1)
     attn_pair_kernel(const AttnTcArgs a, const __grid_constant__ CUtensorMap tm_x,
                      const __grid_constant__ CUtensorMap tm_y, const __grid_constant__ CUtensorMap tm_wqkv,
                      const __grid_constant__ CUtensorMap tm_wo, const __grid_constant__ CUtensorMap tm_wr) {
-    extern __shared__ unsigned char smem_raw[];
-    unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* smem = smem_raw;
+    if (smem_u32(smem) & 1023u) {  // the same in both CTAs of the cluster: both leave here
+        if (threadIdx.x == 0) atomicOr(a.err, ERR_TIMEOUT);
+        return;
+    }
     unsigned char* sX = smem + kOffX;
     unsigned char* sQ = smem + kOffQ;
     unsigned char* sK = smem + kOffK;
@@ -106,11 +107,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int my_w = 2 * tile + (int)rank;  // this CTA's window
     const bool router = a.n_experts > 0;
     const int npad = a.n_experts_pad;
-    // K-block-shaped bases (SW128, 128 rows) whose rows of window w are 8 KB at `rows8k`
+    // The SW128 K-block (128 rows) whose rows of window w are the 8 KB at `rows8k`
     auto kblock_of = [](uint32_t rows8k, uint32_t w) { return rows8k - 8192u * w; };
-    // where the two own pairs' O rows of the peer's window are staged (pair 0: a buffer of its
-    // own; pair 1: the peer-window rows of X K-block 0, free once the last QKV GEMM completed)
-    auto out_rows = [&](int p) { return p == 0 ? smem_u32(smem + kOffOut) : smem_u32(sX) + 8192u * peer; };
+    const uint32_t landing = smem_u32(smem + kOffL);  // pair p at + 8 KB * p
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -130,12 +129,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_init(&bars->ao_ready, 4);
         mbar_init(&bars->ao_free, 1);
         mbar_init(&bars->ao_staged, 4);
-        mbar_init(&bars->land_free, 1);
-        mbar_init(&bars->land_full, 1);
         mbar_init(&bars->po_full, 1);
         mbar_init(&bars->lg_full, 1);
         mbar_init(&bars->drain, 1);
         mbar_init(&bars->ep_done, 4);
+        for (int p = 0; p < 2; ++p) {
+            mbar_init(&bars->land[p], 1);
+            mbar_expect_tx(&bars->land[p], 8192);  // the peer's st.async bytes complete the phase
+        }
         bars->abort = 0;
         fence_barrier_init();
         fence_async_shared();
@@ -143,14 +144,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = threadIdx.x; i < 256; i += blockDim.x) {
         bars->hist[i] = 0;
         bars->bo[i] = a.bo[i];
-        bars->br[i] = router && i < a.n_experts ? a.br[i] : 0.0f;
+        bars->br[i] = __float2half_rn(router && i < a.n_experts ? a.br[i] : 0.0f);  // exact: fp16 values
     }
-    for (int i = threadIdx.x; i < kHeads * 96; i += blockDim.x) bars->bqkv[i] = a.bqkv[kHeads * 96 * rank + i];
     if (warp == 1) tmem_alloc(&bars->tmem_base, 512);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    cluster_sync();  // both CTAs' barriers are initialised before either arrives on the other's
+    cluster_sync();  // both CTAs' barriers are initialised before either stores into the other
     const uint32_t tmem = bars->tmem_base;
     // Programmatic dependent launch as attn_tc: the next kernel may place its CTAs now; the wait
     // for the previous kernels is taken by the producer after its first weight loads and by the
@@ -204,16 +204,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tma_load_4d(smem_u32(sX + kb * 16384 + half * 8192), &tm_x, &bars->x_full[kb], kb * 64,
                                 wxx[half] * 8, wyy[half] * 8, wf[half]);
             }
-            // the consumption order of the MMA warp: QKV_{h+1} at head h; rank 0: Wo columns of
-            // pairs 0, 1 at heads 2, 3, then of pairs 2, 3; rank 1: pairs 0, 1, 2, 3 at the end
-            for (int h = 0; h < kHeads; ++h) {
-                if (h > 0 && h < kHeads - 1) ring_load(&tm_wqkv, true, 0, (kHeads * rank + h + 1) * 96, kQkvBytes);
-                const int p = own_pair(h);
-                if (p >= 0 && rank == 0) ring_load(&tm_wo, false, p * 64, 0, kWoBytes);
-            }
-            for (int q = 0; q < 2; ++q) ring_load(&tm_wo, false, (2 * peer + q) * 64, 0, kWoBytes);
-            if (rank == 1)
-                for (int q = 0; q < 2; ++q) ring_load(&tm_wo, false, (2 + q) * 64, 0, kWoBytes);
+            // the consumption order of the MMA warp: QKV_{h+1} at head h, Wo columns of pair 0 at
+            // head 2 (rank 0: its own; rank 1: the peer's), then pairs 1, 2, 3 at the end
+            ring_load(&tm_wqkv, true, 0, (kHeads * rank + 2) * 96, kQkvBytes);
+            ring_load(&tm_wqkv, true, 0, (kHeads * rank + 3) * 96, kQkvBytes);
+            for (int p = 0; p < 4; ++p) ring_load(&tm_wo, false, p * 64, 0, kWoBytes);
             if (router)
                 for (int r0 = 0; r0 < npad; r0 += kRouterRows) {
                     const int rows = npad < kRouterRows ? npad : kRouterRows;
@@ -255,6 +250,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (ok && !mbar_wait_w(bar, par, abort)) ok = false;
             tc_fence_after();
         };
+        // the peer's O rows of pair p have landed (st.async, generic proxy): make them visible to
+        // the tensor core's reads
+        auto wait_landed = [&](int p) {
+            if (ok && !__all_sync(0xffffffffu, mbar_wait_cl(&bars->land[p], 0, abort))) ok = false;
+            fence_async_shared();
+            tc_fence_after();
+        };
         const uint32_t xs = smem_u32(sX);
         auto issue_qkv = [&](bool first) {  // the first: X K-blocks as they land
             const uint32_t b = ring_wait();
@@ -271,7 +273,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             mma_commit_w(&bars->qkv_full);
         };
-        // PO += O_pair . Wo[:, pair]^T with A = the pair's O (an SW128 K-block at `a_base`)
+        // PO += O_pair . Wo[:, pair]^T with A = the pair's O (an SW128 K-block at `a_base`), the
+        // pairs in the order 0, 1, 2, 3
         bool po_first = true;
         auto po_mmas = [&](uint32_t a_base) {
             const uint32_t b = ring_wait();  // Wo[:, pair]: all 256 output rows
@@ -283,6 +286,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             po_first = false;
             ring_release();
         };
+        const uint32_t land_kb0 = kblock_of(landing, rank), land_kb1 = kblock_of(landing + 8192, rank);
         issue_qkv(true);
         for (int h = 0; h < kHeads && ok; ++h) {
             const uint32_t vs = smem_u32(sV + (h & 1) * 8192);
@@ -293,10 +297,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                              k != 0);
             mma_commit_w(&bars->s_full);
             if (h < kHeads - 1) issue_qkv(false);
-            if (rank == 0 && own_pair(h) == 0) {  // rank 0: pair 0 behind QKV_3
-                wait(&bars->ao_ready, c_aor.next());
-                po_mmas(smem_u32(sAO));
-                mma_commit_w(&bars->ao_free);
+            if (h == 2) {  // pair 0, behind QKV_3: rank 0 its own, rank 1 the peer's
+                if (rank == 0) {
+                    wait(&bars->ao_ready, c_aor.next());
+                    po_mmas(smem_u32(sAO));
+                    mma_commit_w(&bars->ao_free);
+                } else {
+                    wait_landed(0);
+                    po_mmas(land_kb0);
+                }
             }
             wait(&bars->p_ready, c_pr.next());
             if (h > 0) wait(&bars->o_drained, c_od.next());  // O columns free
@@ -304,22 +313,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int k = 0; k < 8; ++k)
                 mma_f16_ts_w(tmem + kTO, tmem + kTS + k * 8, sdesc(vs + k * 1024, SW64), id_pv, k != 0);
             mma_commit_w(&bars->o_full);
-            if (rank == 0 && h == kHeads - 1) {  // rank 0: pair 1 after the last PV
-                wait(&bars->ao_ready, c_aor.next());
-                po_mmas(smem_u32(sAO));
-            }
         }
-        // ---- the peer's pairs (landed in the Q/K/V buffers, this window's rows); rank 1 then
-        // adds its own pairs, whose rows of its window it kept in the AO buffer
-        {
-            const bool landed = __all_sync(0xffffffffu, !ok || mbar_wait_cl(&bars->land_full, 0, abort));
-            if (!landed) ok = false;
-            tc_fence_after();
-        }
-        for (int q = 0; q < 2 && ok; ++q) po_mmas(kblock_of(smem_u32(sQ) + q * 16384 + 8192u * rank, rank));
-        if (rank == 1) {
+        // ---- pairs 1, 2, 3
+        if (rank == 0) {
+            wait(&bars->ao_ready, c_aor.next());
+            po_mmas(smem_u32(sAO));  // own pair 1
+            wait_landed(0);
+            po_mmas(land_kb0);       // the peer's pair 2
+            wait_landed(1);
+            po_mmas(land_kb1);       // the peer's pair 3
+        } else {
+            wait_landed(1);
+            po_mmas(land_kb1);       // the peer's pair 1
             wait(&bars->ao_staged, 0);
-            for (int q = 0; q < 2 && ok; ++q) po_mmas(kblock_of(smem_u32(sAO) + q * 8192, 1));
+            for (int q = 0; q < 2 && ok; ++q) po_mmas(kblock_of(smem_u32(sAO) + q * 8192, 1));  // own 2, 3
         }
         mma_commit_w(&bars->po_full);
         // ---- router logits = y . Wr^T (this window's rows of y are whole here)
@@ -378,13 +385,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             attn_store_p(tmem + lane_addr + kTS, wnd, pk);
             tc_fence_before();
             arrive(&bars->p_ready);
-            // ---- O_h = PV / sum -> fp16: the rows of this CTA's window to the AO buffer (rank 0:
-            // the pair's K-block; rank 1: its rows of the pair), the peer's rows to the outbox
+            // ---- O_h = PV / sum -> fp16: the peer's window rows straight into the peer's landing
+            // of the pair; this window's rows to the AO buffer (rank 0: the pair's K-block, read
+            // by its out-projection; rank 1: its rows of the pair, kept for the end)
             wait(&bars->o_full, c_o.next());
-            if (!ok) break;
-            if (h == kHeads - 1 && warp == 2 && lane == 0)  // the last PV has read Q, K and V
-                mbar_arrive_peer(peer_addr(smem_u32(&bars->land_free), peer));
-            if (rank == 0 && h == 2) wait(&bars->ao_free, 0);  // pair 0's out-projection done
+            if (rank == 0 && mine && h == 2) wait(&bars->ao_free, 0);  // pair 0's out-projection done
             if (!ok) break;
             {
                 uint32_t v[32];
@@ -393,13 +398,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                 uint32_t po[16];
                 attn_scale_o(v, inv, po);
                 const int p = h >> 1;
-                const uint32_t row8k = mine ? (rank == 0 ? smem_u32(sAO) : smem_u32(sAO) + p * 8192u) : out_rows(p);
-                const uint32_t base = kblock_of(row8k, wnd);
-                unsigned char* dst = smem + (base - smem_u32(smem));
+                if (mine) {
+                    const uint32_t base = rank == 0 ? smem_u32(sAO) : kblock_of(smem_u32(sAO) + p * 8192u, 1);
+                    unsigned char* dst = smem + (base - smem_u32(smem));
 #pragma unroll
-                for (int c = 0; c < 4; ++c)
-                    *reinterpret_cast<uint4*>(dst + sw128_off(r, (h & 1) * 4 + c)) =
-                        make_uint4(po[4 * c], po[4 * c + 1], po[4 * c + 2], po[4 * c + 3]);
+                    for (int c = 0; c < 4; ++c)
+                        *reinterpret_cast<uint4*>(dst + sw128_off(r, (h & 1) * 4 + c)) =
+                            make_uint4(po[4 * c], po[4 * c + 1], po[4 * c + 2], po[4 * c + 3]);
+                } else {
+                    const uint32_t base = peer_addr(kblock_of(landing + p * 8192u, wnd), peer);
+                    const uint32_t bar = peer_addr(smem_u32(&bars->land[p]), peer);
+#pragma unroll
+                    for (int c = 0; c < 4; ++c)
+                        st_async_peer(base + sw128_off(r, (h & 1) * 4 + c), po[4 * c], po[4 * c + 1], po[4 * c + 2],
+                                      po[4 * c + 3], bar);
+                }
             }
             fence_async_shared();
             tc_fence_before();
@@ -407,19 +420,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             if ((h & 1) && rank == 0) arrive(&bars->ao_ready);
         }
         arrive(&bars->ao_staged);
-        if (warp == 2) {
-            // ---- the exchange: the own pairs' O rows of the peer's window into the peer's
-            // landing buffers, once every softmax warp wrote them and the peer's last PV is done
-            if (lane == 0 && ok && mbar_wait(&bars->ao_staged, 0, abort) &&
-                mbar_wait_cl(&bars->land_free, 0, abort)) {
-                const uint32_t peer_full = peer_addr(smem_u32(&bars->land_full), peer);
-                mbar_expect_tx_peer(peer_full, 16384);
-                for (int q = 0; q < 2; ++q)
-                    bulk_copy_to_peer(peer_addr(smem_u32(sQ) + q * 16384 + 8192u * peer, peer), out_rows(q), 8192,
-                                      peer_full);
-            }
-            __syncwarp();
-        }
         // ---- y: the odd 32-column chunk of every K-block, this CTA's window rows
         if (mine) {
             wait(&bars->po_full, 0);
@@ -449,7 +449,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // QKV_h (TMEM) -> fp16 Q, K (K-major SW64) and V (key-major SW64, buffer h&1)
             wait(&bars->qkv_full, c_qkv.next());
             if (!ok) break;
-            attn_drain_row(tmem + lane_addr + kTQKV, bars->bqkv + h * 96, r, sQ, sK, sV + (h & 1) * 8192);
+            attn_drain_row(tmem + lane_addr + kTQKV, a.bqkv + (kHeads * rank + h) * 96, r, sQ, sK, sV + (h & 1) * 8192);
             fence_async_shared();
             tc_fence_before();
             arrive(&bars->qkv_drained);
@@ -481,7 +481,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         for (int j = 0; j < 32; ++j) {
                             const int e = g + j;
                             if (e < a.n_experts) {
-                                const float l = rh(__fadd_rn(__uint_as_float(v[j]), bars->br[e]));
+                                const float l = rh(__fadd_rn(__uint_as_float(v[j]), __half2float(bars->br[e])));
                                 if (e == 0 || l > bv) {
                                     bv = l;
                                     best = e;
@@ -505,12 +505,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     if (bars->abort) {
         if (threadIdx.x == 0) atomicOr(a.err, ERR_TIMEOUT);
-        const uint64_t t0 = globaltimer();  // copies in flight land
+        const uint64_t t0 = globaltimer();  // stores in flight land
         while (globaltimer() - t0 < 1000000ull) {
         }
     }
     __syncwarp();
-    cluster_sync();  // neither CTA leaves while the other may still copy into or out of it
+    cluster_sync();  // neither CTA leaves while the other may still store into it
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem, 512);

@@ -465,6 +465,15 @@ PRISM_DEV void bulk_copy_to_peer(uint32_t dst_cluster, uint32_t src, uint32_t by
         "r"(src), "r"(bytes), "r"(bar_cluster)
         : "memory");
 }
+// asynchronous 16-byte store into a peer CTA's shared memory; its completion adds 16 transaction
+// bytes to the peer's mbarrier (with release semantics at cluster scope)
+PRISM_DEV void st_async_peer(uint32_t dst_cluster, uint32_t x, uint32_t y, uint32_t z, uint32_t w,
+                             uint32_t bar_cluster) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+                     dst_cluster),
+                 "r"(x), "r"(y), "r"(z), "r"(w), "r"(bar_cluster)
+                 : "memory");
+}
 // try_wait with cluster-scope acquire: for barriers that peers arrive on
 PRISM_DEV bool mbar_try_wait_cl(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
