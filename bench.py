@@ -678,7 +678,9 @@ def run_codec(args):
                 "e2e": {"value": ws * 1e3 / ms_e2e, "unit": "frames/s", "h2d_bytes_per_step": int(xin.numel() * 2),
                         "d2h_bytes_per_step": int(rgb_h.numel() * 2), "ms_per_step": ms_e2e,
                         "api": "prism_codec_pass per pass (graph replay); frame in / RGB out through page-locked host memory"},
-                "gpu_launches": 2 * len(fc.passes) + 1,
+                # a pass kernel each, a weight repack before each pass whose matrix streams (over
+                # 64 KB: the two split convolutions), the pixel shuffle
+                "gpu_launches": len(fc.passes) + sum(p[0].startswith("strided_conv_split") for p in fc.passes) + 1,
                 "roofline": {"kernel": "whole chain", "bound": "hbm", "achieved": achieved, "peak": peak_gbs,
                              "unit": "GB/s", "frac": achieved / peak_gbs, "peak_source": f"{src} hbm_gbs",
                              "traffic": None},

@@ -92,13 +92,14 @@ struct CodecArgs {
     __half* out;         // the output map (CHW)
     int in_w, in_h, out_w, out_h;
     int relu;            // conv3x3_9ch / pw: the push constant (1 = ReLU)
-    const float* bias;   // [N] fp32 copies of the fp16 biases
+    const __half* blob;  // the weights arena: matrix at element wo, biases at bo (any alignment)
+    int wo, bo;
     uint32_t* err;
 };
 
 struct Bars {
     uint64_t a_full[kMaxStages], b_full[kMaxStages], empty[kMaxStages];
-    uint64_t acc_full[2], acc_empty[2], drain, w_full;
+    uint64_t acc_full[2], acc_empty[2], drain;
     uint32_t tmem_base;
     int abort;
     float bias[128];
@@ -137,15 +138,53 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&bars->acc_empty[b], 4);
         }
         mbar_init(&bars->drain, 1);
-        mbar_init(&bars->w_full, 1);
         bars->abort = 0;
         fence_barrier_init();
     }
-    for (int i = threadIdx.x; i < 128; i += blockDim.x) bars->bias[i] = i < C::kN ? a.bias[i] : 0.0f;
+    for (int i = threadIdx.x; i < 128; i += blockDim.x) bars->bias[i] = i < C::kN ? __half2float(a.blob[a.bo + i]) : 0.0f;
+    if constexpr (C::kResident) {
+        // The whole weight matrix into shared memory, straight from the blob: [g][kb] K-blocks of
+        // {kNP rows, 64 K values} in the MMA's SW128 layout, K in the GEMM's order (tap-major for the
+        // 3x3 convolutions: k = tap * kCgP + channel), zero padding.  Every thread builds 16-byte
+        // chunks; weights are never written by a pass, so this runs before the wait for the
+        // previous kernel and overlaps its end.
+        constexpr int kChunks = C::kG * C::kKB * C::kNP * 8;
+        for (int ci = threadIdx.x; ci < kChunks; ci += blockDim.x) {
+            const int chunk = ci & 7, n = (ci >> 3) % C::kNP, gk = (ci >> 3) / C::kNP;  // gk = g * kKB + kb
+            const int g = gk / C::kKB, kb = gk % C::kKB;
+            uint32_t w4[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                uint32_t pair = 0;
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int k = kb * 64 + chunk * 8 + 2 * q + h;
+                    int src = -1;  // element of the group's row in the blob's (channel, tap) order
+                    if (C::kType == 0) {
+                        const int t = k / C::kCgP, c = k % C::kCgP;
+                        if (t < 9 && c < C::kCg) src = c * 9 + t;
+                    } else if (k < C::kKG) {
+                        src = k;
+                    }
+                    if (n < C::kN && src >= 0)
+                        pair |= (uint32_t)__half_as_ushort(a.blob[a.wo + (size_t)n * C::kLd + g * C::kKsrc + src]) << (16 * h);
+                }
+                w4[q] = pair;
+            }
+            *reinterpret_cast<uint4*>(smem + C::kWOff + gk * C::kBBytes + sw128_off(n, chunk)) =
+                make_uint4(w4[0], w4[1], w4[2], w4[3]);
+        }
+        fence_async_shared();  // read by the tensor cores
+    }
     if (warp == 1) tmem_alloc(&bars->tmem_base, 512);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    // Programmatic dependent launch: the next pass may place its CTAs now; this one waits for the
+    // previous kernels (its input maps, the repacked weights of a streamed matrix, and the
+    // memory its output overwrites) only here, after the prologue above.
+    grid_dep_launch();
+    grid_dep_wait();
     const uint32_t tmem = bars->tmem_base;
     auto stage_a = [&](int s) { return smem + s * kStageBytes; };
     // weight K-block (g, kb) of `stage`: resident copy, or the stage's B slot when streamed
@@ -155,13 +194,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (warp == 0) {
         // ============================ producer ============================
-        if (lane == 0 && C::kResident) {  // the whole weight matrix, once
-            prefetch_tmap(&tm_w);
-            mbar_expect_tx(&bars->w_full, C::kWBytes);
-            for (int g = 0; g < C::kG; ++g)
-                for (int kb = 0; kb < C::kKB; ++kb)
-                    tma_load_2d(smem_u32(b_block(0, g, kb)), &tm_w, &bars->w_full, kb * 64, g * C::kNP);
-        } else if (lane == 0) {
+        if (lane == 0 && !C::kResident) {  // the streamed weight K-blocks beside the A K-blocks
             prefetch_tmap(&tm_w);
             int s = 0;
             uint32_t ph = 0;
@@ -187,7 +220,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         int s = 0;
         uint32_t ph = 0, it = 0;
         bool ok = true;
-        if (C::kResident && !mbar_wait_w(&bars->w_full, 0, abort)) ok = false;
         for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, ++it) {
             const int buf = C::kAccBufs == 2 ? (int)(it & 1) : 0;
             const uint32_t use = C::kAccBufs == 2 ? (it >> 1) : it;  // uses of this buffer so far
@@ -386,10 +418,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
-// [G][NP][KGP] K-major fp16 weights (zero padding) and fp32 biases from the blob at any alignment
+// [G][NP][KGP] K-major fp16 weights (zero padding) from the blob at any alignment, for the weight
+// matrices streamed by TMA (over 64 KB).  It waits for the previous kernel before writing: a pass
+// of the same kind may still be reading the scratch.
 template <int KIND>
-__global__ void codec_repack_kernel(const __half* blob, int wo, int bo, __half* w, float* bias) {
+__global__ void codec_repack_kernel(const __half* blob, int wo, __half* w) {
     using C = CodecCfg<KIND>;
+    grid_dep_wait();
     const int total = C::kG * C::kNP * C::kKGP;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
         const int k = i % C::kKGP, n = (i / C::kKGP) % C::kNP, g = i / (C::kKGP * C::kNP);
@@ -402,14 +437,13 @@ __global__ void codec_repack_kernel(const __half* blob, int wo, int bo, __half* 
         }
         w[i] = n < C::kN && src >= 0 ? blob[wo + (size_t)n * C::kLd + g * C::kKsrc + src] : __float2half(0.0f);
     }
-    if (blockIdx.x == 0)
-        for (int n = threadIdx.x; n < C::kN; n += blockDim.x) bias[n] = __half2float(blob[bo + n]);
 }
 
 // pixelshuffle_sigmoid.comp.glsl:26-56: display pixel (ox, oy) of colour c takes channel
 // c*s*s + (oy%s)*s + ox%s of render pixel (ox/s, oy/s), through 1/(1 + exp(-v)) in fp32
 // One thread per display pixel (blockIdx.y = display row), its three colours.
 __global__ void pixelshuffle_kernel(const __half* in, __half* rgb, int rw, int rh, int dw, int dh, int sc) {
+    grid_dep_wait();  // the input is the previous pass's output
     const int ox = blockIdx.x * blockDim.x + threadIdx.x, oy = blockIdx.y;
     if (ox >= dw) return;
     const int64_t rpx = (int64_t)rw * rh, dpx = (int64_t)dw * dh;
@@ -434,12 +468,11 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_tiled() {
     return fn;
 }
 
-// Per-context scratch of the codec passes: the repacked weights and biases of each kind (so
-// passes of different kinds never share them) and the context's device error word.
+// Per-context scratch of the codec passes: the repacked weights of each kind whose matrix is
+// streamed (so passes of different kinds never share them).
 struct CodecScratch {
     std::mutex mu;
     __half* w[C_COUNT] = {};
-    float* bias[C_COUNT] = {};
 };
 
 template <int KIND>
@@ -474,49 +507,50 @@ int run_codec(prism_ctx* ctx, const int32_t* q, const __half* weights, size_t we
     if (overlap(out_off, C::kN * out_px, in_off, in_ch * in_px) ||
         (C::kType == 1 && overlap(out_off, C::kN * out_px, skip_off, C::kSkip * out_px)))
         return set_error(PRISM_E_ARG, "prism_codec_pass: the output map overlaps an input map");
-    if (!ctx->codec) return set_error(PRISM_E_ARG, "prism_codec_pass: context without codec scratch");
-    CodecScratch& cs = *static_cast<CodecScratch*>(ctx->codec);
-    {
-        std::lock_guard<std::mutex> lock(cs.mu);
-        if (!cs.w[KIND]) {
-            void *w = nullptr, *b = nullptr;
-            if (cudaMalloc(&w, (size_t)C::kG * C::kNP * C::kKGP * 2) != cudaSuccess ||
-                cudaMalloc(&b, 128 * sizeof(float)) != cudaSuccess) {
-                cudaFree(w);
-                cudaGetLastError();
-                return set_error(PRISM_E_NOMEM, "prism_codec_pass: weight scratch");
+    CUtensorMap tm{};
+    if constexpr (!C::kResident) {  // the streamed matrix: repacked into the context's scratch
+        if (!ctx->codec) return set_error(PRISM_E_ARG, "prism_codec_pass: context without codec scratch");
+        CodecScratch& cs = *static_cast<CodecScratch*>(ctx->codec);
+        {
+            std::lock_guard<std::mutex> lock(cs.mu);
+            if (!cs.w[KIND]) {
+                void* w = nullptr;
+                if (cudaMalloc(&w, (size_t)C::kG * C::kNP * C::kKGP * 2) != cudaSuccess) {
+                    cudaGetLastError();
+                    return set_error(PRISM_E_NOMEM, "prism_codec_pass: weight scratch");
+                }
+                cs.w[KIND] = static_cast<__half*>(w);
             }
-            cs.w[KIND] = static_cast<__half*>(w);
-            cs.bias[KIND] = static_cast<float*>(b);
         }
+        auto fn = encode_tiled();
+        if (!fn) return set_error(PRISM_E_CUDA, "cuTensorMapEncodeTiled is not available");
+        cuuint64_t dims[2] = {(cuuint64_t)C::kKGP, (cuuint64_t)C::kG * C::kNP};
+        cuuint64_t strides[1] = {(cuuint64_t)C::kKGP * 2};
+        cuuint32_t box[2] = {64, (cuuint32_t)C::kNP};
+        cuuint32_t estr[2] = {1, 1};
+        if (fn(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, cs.w[KIND], dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return set_error(PRISM_E_CUDA, "prism_codec_pass: weight tensor map");
+        const cudaError_t e = launch_pdl(codec_repack_kernel<KIND>, dim3(64), dim3(256), 0, s, weights, wo, cs.w[KIND]);
+        if (e != cudaSuccess) return set_error(PRISM_E_CUDA, "prism_codec_pass: %s", cudaGetErrorString(e));
     }
-    auto fn = encode_tiled();
-    if (!fn) return set_error(PRISM_E_CUDA, "cuTensorMapEncodeTiled is not available");
-    CUtensorMap tm;
-    cuuint64_t dims[2] = {(cuuint64_t)C::kKGP, (cuuint64_t)C::kG * C::kNP};
-    cuuint64_t strides[1] = {(cuuint64_t)C::kKGP * 2};
-    cuuint32_t box[2] = {64, (cuuint32_t)C::kNP};
-    cuuint32_t estr[2] = {1, 1};
-    if (fn(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, cs.w[KIND], dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
-        CUDA_SUCCESS)
-        return set_error(PRISM_E_CUDA, "prism_codec_pass: weight tensor map");
-    codec_repack_kernel<KIND><<<64, 256, 0, s>>>(weights, wo, bo, cs.w[KIND], cs.bias[KIND]);
     CodecArgs a;
     a.in = feat + in_off;
     a.skip = feat + skip_off;
     a.out = feat + out_off;
     a.in_w = in_w, a.in_h = in_h, a.out_w = out_w, a.out_h = out_h;
     a.relu = relu;
-    a.bias = cs.bias[KIND];
+    a.blob = weights;
+    a.wo = wo;
+    a.bo = bo;
     a.err = ctx->err;
     const int n_tiles = (int)((out_px + 127) / 128);
     constexpr int smem = codec_smem<KIND>();
     static_assert(smem <= 232448, "shared memory budget");
     cudaError_t e = cudaFuncSetAttribute(codec_tc_kernel<KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e == cudaSuccess) {
-        codec_tc_kernel<KIND><<<std::min(ctx->sm_count, n_tiles), kThreads, smem, s>>>(a, tm);
-        e = cudaGetLastError();
+        e = launch_pdl(codec_tc_kernel<KIND>, dim3(std::min(ctx->sm_count, n_tiles)), dim3(kThreads), smem, s, a, tm);
     }
     if (e != cudaSuccess) return set_error(PRISM_E_CUDA, "prism_codec_pass: %s", cudaGetErrorString(e));
     return PRISM_OK;
@@ -529,10 +563,7 @@ void* codec_scratch_new() { return new CodecScratch; }
 void codec_scratch_free(void* p) {
     auto* cs = static_cast<CodecScratch*>(p);
     if (!cs) return;
-    for (int k = 0; k < C_COUNT; ++k) {
-        cudaFree(cs->w[k]);
-        cudaFree(cs->bias[k]);
-    }
+    for (int k = 0; k < C_COUNT; ++k) cudaFree(cs->w[k]);
     delete cs;
 }
 
@@ -577,9 +608,9 @@ extern "C" int prism_codec_pass(prism_ctx* ctx, int kind, const int32_t* push, i
         !in_range(out_off, (int64_t)3 * dw * dh, rgb_elems))
         return set_error(PRISM_E_RANGE, "prism_codec_pass: pixel shuffle outside its buffers");
     if (dh > 65535) return set_error(PRISM_E_RANGE, "prism_codec_pass: display height %d", dh);
-    pixelshuffle_kernel<<<dim3((dw + 255) / 256, dh), 256, 0, s>>>(f + in_off, static_cast<__half*>(rgb) + out_off, rw,
-                                                                  rh, dw, dh, sc);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_pdl(pixelshuffle_kernel, dim3((dw + 255) / 256, dh), dim3(256), 0, s,
+                               static_cast<const __half*>(f + in_off), static_cast<__half*>(rgb) + out_off, rw, rh, dw,
+                               dh, sc);
     if (e != cudaSuccess) return set_error(PRISM_E_CUDA, "prism_codec_pass: %s", cudaGetErrorString(e));
     return PRISM_OK;
 }
