@@ -150,6 +150,128 @@ PRISM_DEV unsigned char* oslot(unsigned char* sO, int R, int col) {
     return sO + (col >> 6) * 16384 + sw128_off(R, (col & 63) >> 3);
 }
 
+PRISM_DEV void arrive_warp(uint64_t* bar, int lane) {
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bar);
+}
+
+// TMEM column of H K-block kb when the E1 parts are W columns wide (each part writes its H over
+// the fp32 columns it has already read: part p, 32-column group g -> 16 columns at W p + 16 g)
+PRISM_DEV uint32_t h_col_w(int kb, bool narrow) { return narrow ? kAcc1 + 64u * kb : h_col(kb); }
+
+// E1 of one tile for the calling warp: acc1 columns [W part, W part + W) of its 32 rows ->
+// h = fp16(gelu(fp16(acc + b1))) (moe_expert_skip.comp.glsl:39-46) as fp16 pairs over the columns
+// already read; each completed 64-column H K-block is announced on h_full.
+template <int W>
+PRISM_DEV bool e1_tile(const FfnArgs& a, Bars* bars, uint32_t tmem, uint32_t lane_addr, int e, int part, int lane,
+                       uint32_t it, volatile int* abort) {
+    // lane l holds bias columns 4l .. 4l+3 of the part, handed out by shuffles
+    const float4 bias =
+        4 * lane < W ? ldg_f4(a.b1 + (size_t)e * kD + part * W + 4 * lane) : make_float4(0.f, 0.f, 0.f, 0.f);
+    if (!mbar_wait_w(&bars->acc1_full, it & 1, abort)) return false;
+    tc_fence_after();
+#pragma unroll 1
+    for (int g = 0; g < W / 32; ++g) {
+        uint32_t r[32];
+        tmem_ld32(tmem + lane_addr + kAcc1 + part * W + g * 32, r);
+        tmem_ld_wait();
+        uint32_t packed[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            // columns 32g + 2j, +1 of the part live in lane 8g + j/2
+            const float bx = __shfl_sync(0xffffffffu, (j & 1) ? bias.z : bias.x, g * 8 + (j >> 1));
+            const float by = __shfl_sync(0xffffffffu, (j & 1) ? bias.w : bias.y, g * 8 + (j >> 1));
+            // t = h(acc + b1): one rounding per coopVecMatMulAddNV result; both columns of the pair
+            // in one f32x2 instruction per step
+            float s0, s1;
+            f2_unpack(f2_add(f2_pack(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1])), f2_pack(bx, by)), s0,
+                      s1);
+            const uint32_t t = pack_h2(s0, s1);
+            float g0, g1;
+            f2_unpack(gelu_f32x2(f2_pack(lo_h2f(t), hi_h2f(t))), g0, g1);
+            packed[j] = pack_h2(g0, g1);
+        }
+        tmem_st16(tmem + lane_addr + kAcc1 + part * W + g * 16, packed);
+        if (g & 1) {  // an H K-block (64 hidden units) complete for this warp's rows
+            tmem_st_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->h_full[(part * W) / 64 + (g >> 1)]);
+        }
+    }
+    tc_fence_before();
+    return true;
+}
+
+// E2 of one tile for the calling warp: out = fp16(fp16(acc2 + b2) + x) (moe_expert_skip.comp.glsl:
+// 48-52) for output columns [W part, W part + W) of its 32 rows; x (the tile's own input rows)
+// comes into the staging tile by cp.async while GEMM2 runs; rows are written back
+// row-contiguously (W/8 lanes per row).  acc2_done (nullable) is arrived on once acc2 is read.
+template <int W>
+PRISM_DEV bool e2_tile(const FfnArgs& a, Bars* bars, uint32_t tmem, uint32_t lane_addr, unsigned char* sO,
+                       const ExpertTile& t, int quad, int part, int lane, uint32_t it, volatile int* abort,
+                       uint64_t* acc2_done) {
+    constexpr int kLanesPerRow = W / 8, kRowsPerInstr = 32 / kLanesPerRow;
+    const int row = quad * 32 + lane;  // tile row of this thread (= TMEM lane)
+    const int sub_row = lane / kLanesPerRow, sub_col = (lane % kLanesPerRow) * 8;
+    const bool row_valid = row < t.rows;
+    const int out_row = row_valid ? a.perm[t.start + row] : 0;
+    // the residual rows (L2-resident) into this warp's slice of the staging tile; invalid rows
+    // zero-filled
+#pragma unroll
+    for (int i = 0; i < 32 / kRowsPerInstr; ++i) {
+        const int lr = kRowsPerInstr * i + sub_row;
+        const int tk = __shfl_sync(0xffffffffu, out_row, lr);
+        const int vld = __shfl_sync(0xffffffffu, (int)row_valid, lr);
+        cp_async16(smem_u32(oslot(sO, quad * 32 + lr, part * W + sub_col)),
+                   a.x + (size_t)(vld ? tk : 0) * kD + part * W + sub_col, vld ? 16u : 0u);
+    }
+    cp_async_commit();
+    const float4 bias =
+        4 * lane < W ? ldg_f4(a.b2 + (size_t)t.expert * kD + part * W + 4 * lane) : make_float4(0.f, 0.f, 0.f, 0.f);
+    if (!mbar_wait_w(&bars->acc2_full, it & 1, abort)) return false;
+    tc_fence_after();
+    cp_async_wait_all();
+    __syncwarp();
+#pragma unroll 1
+    for (int g = 0; g < W / 32; ++g) {
+        const int col0 = part * W + g * 32;
+        uint32_t r[32];
+        tmem_ld32(tmem + lane_addr + kAcc2 + col0, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            uint4* slot = reinterpret_cast<uint4*>(oslot(sO, row, col0 + 8 * q));
+            const uint4 x = *slot;
+            const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
+            uint32_t z[4];
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+                const int j = 4 * q + jj;
+                const float bx = __shfl_sync(0xffffffffu, (j & 1) ? bias.z : bias.x, g * 8 + (j >> 1));
+                const float by = __shfl_sync(0xffffffffu, (j & 1) ? bias.w : bias.y, g * 8 + (j >> 1));
+                // z = h(h(acc + b2) + x): the fp16 residual add of moe_expert_skip.comp.glsl:52
+                z[jj] = hadd2_u32(pack_h2(__fadd_rn(__uint_as_float(r[2 * j]), bx), __fadd_rn(__uint_as_float(r[2 * j + 1]), by)),
+                                  xs[jj]);
+            }
+            *slot = make_uint4(z[0], z[1], z[2], z[3]);
+        }
+    }
+    tc_fence_before();
+    if (acc2_done) arrive_warp(acc2_done, lane);  // acc2 read: GEMM2 of the next tile may go
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < 32 / kRowsPerInstr; ++i) {
+        const int lr = kRowsPerInstr * i + sub_row;
+        const int tk = __shfl_sync(0xffffffffu, out_row, lr);
+        const int vld = __shfl_sync(0xffffffffu, (int)row_valid, lr);
+        const uint4 v = *reinterpret_cast<const uint4*>(oslot(sO, quad * 32 + lr, part * W + sub_col));
+        if (vld) *reinterpret_cast<uint4*>(a.y + (size_t)tk * kD + part * W + sub_col) = v;
+    }
+    __syncwarp();  // the slice is free for the next tile's residual rows
+    return true;
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     expert_tc_kernel(const FfnArgs a, const __grid_constant__ CUtensorMap tm_w1,
                      const __grid_constant__ CUtensorMap tm_w2) {
@@ -200,6 +322,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
         n_tiles = plan_buckets(a, bars);
     }
+    // no CTA has a second tile: the epilogues split each one over all 16 epilogue warps
+    const bool single = n_tiles <= (int)gridDim.x;
 
     if (warp == 0) {
         // ============================ producer ============================
@@ -301,7 +425,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t b0 = smem_u32(sW + stage * kStage);
 #pragma unroll
                 for (int k = 0; k < 4; ++k)
-                    mma_f16_ts_w(tmem + kAcc2, tmem + h_col(kb) + 8 * k, sdesc(b0 + k * 32, SW128), idesc,
+                    mma_f16_ts_w(tmem + kAcc2, tmem + h_col_w(kb, single) + 8 * k, sdesc(b0 + k * 32, SW128), idesc,
                                  (i | k) != 0);
                 mma_commit_w(&bars->empty[stage]);
                 if (++stage == kStages) {
@@ -314,131 +438,41 @@ __global__ void __launch_bounds__(kThreads, 1)
         // every issued MMA has completed before TMEM is released
         mma_commit_w(&bars->drain);
         mbar_wait_w(&bars->drain, 0, abort);
-    } else if (warp < kE2Base) {
-        // ============================ E1: acc1 -> H ============================
-        const int quad = warp & 3;               // TMEM lanes 32*quad .. +31
-        const int part = (warp - kE1Base) >> 2;  // columns [128 part, 128 part + 128)
+    } else if (warp < kE2Base + 8) {
+        // ============================ epilogues ============================
+        // E1 (acc1 -> H) and E2 (acc2 -> out + residual) of a tile.  Normally warps 3-10 run E1 and
+        // warps 11-18 E2, each warp on its TMEM row quad and a 128-column part, so E1 of tile i+1
+        // runs beside E2 of tile i.  When no CTA has a second tile (a small forward: one frame is
+        // ~100 tiles on 148 SMs) the two groups would take turns on the one tile, so all 16 warps
+        // run E1 and then E2 on 64-column parts.
+        const int quad = warp & 3;  // TMEM lanes 32*quad .. +31
         const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
-        uint32_t it = 0;
-        bool ok = true;
-        for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, ++it) {
-            const int e = tile_at(a, bars, tile).expert;
-            // lane l holds bias columns 4l .. 4l+3 of the part, handed out by shuffles
-            const float4 bias = ldg_f4(a.b1 + (size_t)e * kD + part * 128 + 4 * lane);
-            if (!mbar_wait_w(&bars->acc1_full, it & 1, abort)) {
-                ok = false;
-                break;
+        if (single) {
+            const int part = (warp - kE1Base) >> 2;  // columns [64 part, 64 part + 64)
+            if ((int)blockIdx.x < n_tiles) {
+                const ExpertTile t = tile_at(a, bars, blockIdx.x);
+                if (e1_tile<64>(a, bars, tmem, lane_addr, t.expert, part, lane, 0u, abort) && warp < kE2Base)
+                    arrive_warp(&bars->acc1_empty, lane);
+                e2_tile<64>(a, bars, tmem, lane_addr, sO, t, quad, part, lane, 0u, abort,
+                            warp >= kE2Base ? &bars->acc2_empty : nullptr);
             }
-            tc_fence_after();
-#pragma unroll 1
-            for (int g = 0; g < 4; ++g) {
-                uint32_t r[32];
-                tmem_ld32(tmem + lane_addr + kAcc1 + part * 128 + g * 32, r);
-                tmem_ld_wait();
-                uint32_t packed[16];
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    // columns 32g + 2j, +1 of the part live in lane 8g + j/2
-                    const float bx = __shfl_sync(0xffffffffu, (j & 1) ? bias.z : bias.x, g * 8 + (j >> 1));
-                    const float by = __shfl_sync(0xffffffffu, (j & 1) ? bias.w : bias.y, g * 8 + (j >> 1));
-                    // t = h(acc + b1): one rounding per coopVecMatMulAddNV result; both columns
-                    // of the pair in one f32x2 instruction per step
-                    float s0, s1;
-                    f2_unpack(f2_add(f2_pack(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1])), f2_pack(bx, by)),
-                              s0, s1);
-                    const uint32_t t = pack_h2(s0, s1);
-                    float g0, g1;
-                    f2_unpack(gelu_f32x2(f2_pack(lo_h2f(t), hi_h2f(t))), g0, g1);
-                    packed[j] = pack_h2(g0, g1);
-                }
-                // H columns 32g .. 32g+31 of the part -> TMEM [128 part + 16g, +16), over
-                // fp32 columns this thread has already read
-                tmem_st16(tmem + lane_addr + kAcc1 + part * 128 + g * 16, packed);
-                if (g & 1) {  // H K-block 2 part + g/2 complete for this warp's rows
-                    tmem_st_wait();
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&bars->h_full[2 * part + (g >> 1)]);
-                }
+        } else if (warp < kE2Base) {
+            const int part = (warp - kE1Base) >> 2;  // columns [128 part, 128 part + 128)
+            uint32_t it = 0;
+            for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
+                if (!e1_tile<128>(a, bars, tmem, lane_addr, tile_at(a, bars, tile).expert, part, lane, it, abort)) break;
+                arrive_warp(&bars->acc1_empty, lane);
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bars->acc1_empty);
-        }
-    } else {
-        // ====================== E2: acc2 -> out (+ residual) ======================
-        const int quad = warp & 3;
-        const int part = (warp - kE2Base) >> 2;
-        const int row = quad * 32 + lane;  // tile row of this thread (= TMEM lane)
-        const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
-        // row-contiguous transfers: 16 lanes x 16 B cover a row's 128 columns of the part,
-        // two rows per warp instruction
-        const int sub_row = lane >> 4, sub_col = (lane & 15) * 8;
-        uint32_t it = 0;
-        bool ok = true;
-        for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, ++it) {
-            const ExpertTile t = tile_at(a, bars, tile);
-            const bool row_valid = row < t.rows;
-            const int out_row = row_valid ? a.perm[t.start + row] : 0;
-            // the residual rows (the tile's input rows, L2-resident) into this warp's slice of
-            // the staging tile; invalid rows zero-filled
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                const int lr = 2 * i + sub_row;
-                const int tk = __shfl_sync(0xffffffffu, out_row, lr);
-                const int vld = __shfl_sync(0xffffffffu, (int)row_valid, lr);
-                cp_async16(smem_u32(oslot(sO, quad * 32 + lr, part * 128 + sub_col)),
-                           a.x + (size_t)(vld ? tk : 0) * kD + part * 128 + sub_col, vld ? 16u : 0u);
+        } else {
+            const int part = (warp - kE2Base) >> 2;
+            uint32_t it = 0;
+            for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
+                if (!e2_tile<128>(a, bars, tmem, lane_addr, sO, tile_at(a, bars, tile), quad, part, lane, it, abort,
+                                  &bars->acc2_empty))
+                    break;
             }
-            cp_async_commit();
-            const float4 bias = ldg_f4(a.b2 + (size_t)t.expert * kD + part * 128 + 4 * lane);
-            if (!mbar_wait_w(&bars->acc2_full, it & 1, abort)) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            cp_async_wait_all();
-            __syncwarp();
-#pragma unroll 1
-            for (int g = 0; g < 4; ++g) {
-                const int col0 = part * 128 + g * 32;
-                uint32_t r[32];
-                tmem_ld32(tmem + lane_addr + kAcc2 + col0, r);
-                tmem_ld_wait();
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    uint4* slot = reinterpret_cast<uint4*>(oslot(sO, row, col0 + 8 * q));
-                    const uint4 x = *slot;
-                    const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
-                    uint32_t z[4];
-#pragma unroll
-                    for (int jj = 0; jj < 4; ++jj) {
-                        const int j = 4 * q + jj;
-                        const float bx = __shfl_sync(0xffffffffu, (j & 1) ? bias.z : bias.x, g * 8 + (j >> 1));
-                        const float by = __shfl_sync(0xffffffffu, (j & 1) ? bias.w : bias.y, g * 8 + (j >> 1));
-                        // z = h(h(acc + b2) + x): the fp16 residual add of moe_expert_skip.comp.glsl:52
-                        z[jj] = hadd2_u32(pack_h2(__fadd_rn(__uint_as_float(r[2 * j]), bx),
-                                                  __fadd_rn(__uint_as_float(r[2 * j + 1]), by)),
-                                          xs[jj]);
-                    }
-                    *slot = make_uint4(z[0], z[1], z[2], z[3]);
-                }
-            }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bars->acc2_empty);  // acc2 read: GEMM2 of the next tile may go
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                const int lr = 2 * i + sub_row;
-                const int tk = __shfl_sync(0xffffffffu, out_row, lr);
-                const int vld = __shfl_sync(0xffffffffu, (int)row_valid, lr);
-                const uint4 v = *reinterpret_cast<const uint4*>(oslot(sO, quad * 32 + lr, part * 128 + sub_col));
-                if (vld) *reinterpret_cast<uint4*>(a.y + (size_t)tk * kD + part * 128 + sub_col) = v;
-            }
-            __syncwarp();  // the slice is free for the next tile's residual rows
         }
     }
-
     tc_fence_before();
     __syncthreads();
     if (bars->abort) {
