@@ -464,31 +464,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (ok && my_w < n_windows) {
                     const int f = my_w / win_per_frame, wl = my_w % win_per_frame;
                     const int gy = (wl / wx_n) * 8 + ty, gx = (wl % wx_n) * 8 + tx;
-                    int best = 0;
-                    float bv = 0.0f;
-#pragma unroll 1
-                    for (int g = 0; g < npad; g += 32) {
-                        uint32_t v[32];
-                        if (g + 32 <= npad) {
-                            tmem_ld32(tmem + lane_addr + kTPO + g, v);
-                        } else {  // npad is a multiple of 16: the last 16 columns
-                            tmem_ld16(tmem + lane_addr + kTPO + g, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
-#pragma unroll
-                            for (int j = 16; j < 32; ++j) v[j] = 0u;
-                        }
-                        tmem_ld_wait();
-#pragma unroll
-                        for (int j = 0; j < 32; ++j) {
-                            const int e = g + j;
-                            if (e < a.n_experts) {
-                                const float l = rh(__fadd_rn(__uint_as_float(v[j]), __half2float(bars->br[e])));
-                                if (e == 0 || l > bv) {
-                                    bv = l;
-                                    best = e;
-                                }
-                            }
-                        }
-                    }
+                    const __half* br = bars->br;
+                    const int best = router_argmax(tmem + lane_addr + kTPO, npad, a.n_experts,
+                                                   [br](int e) { return __half2float(br[e]); });
                     route_token(a, bars->hist, gy < a.H && gx < a.W,
                                 (int64_t)f * a.W * a.H + (int64_t)gy * a.W + gx, best, lane);
                 }

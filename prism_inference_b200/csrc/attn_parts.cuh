@@ -158,6 +158,51 @@ PRISM_DEV void y_share(unsigned char* sX, uint32_t po_taddr, int r, const float*
     }
 }
 
+// The router's choice for one row: the first maximum of the logits l_e = fp16(acc_e + br_e),
+// e < n_experts (the lowest index among equal maxima, which the sequential scan
+// `if (e == 0 || l > best)` of moe_router.comp.glsl picks), with acc_e in TMEM columns [0, npad)
+// at taddr and br_e = bias(e).  The 32 logits of a TMEM load are rounded independently and
+// reduced as a tree in which the higher index of a pair wins only when strictly greater (so ties
+// keep the lower index); batches of 32 combine the same way.  A serial scan would be a chain of
+// 64 dependent compare-selects at 64 experts.
+template <typename Bias>
+PRISM_DEV int router_argmax(uint32_t taddr, int npad, int n_experts, Bias bias) {
+    float bv = 0.0f;
+    int best = 0;
+#pragma unroll 1
+    for (int g = 0; g < npad; g += 32) {
+        uint32_t v[32];
+        if (g + 32 <= npad) {
+            tmem_ld32(taddr + g, v);
+        } else {  // npad is a multiple of 16: the last 16 columns
+            tmem_ld16(taddr + g, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
+#pragma unroll
+            for (int j = 16; j < 32; ++j) v[j] = 0u;
+        }
+        tmem_ld_wait();
+        float l[32];
+        int id[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            l[j] = g + j < n_experts ? rh(__fadd_rn(__uint_as_float(v[j]), bias(g + j))) : -INFINITY;
+            id[j] = g + j;
+        }
+#pragma unroll
+        for (int s = 1; s < 32; s <<= 1)
+#pragma unroll
+            for (int j = 0; j < 32; j += 2 * s)
+                if (l[j + s] > l[j]) {
+                    l[j] = l[j + s];
+                    id[j] = id[j + s];
+                }
+        if (g == 0 || l[0] > bv) {
+            bv = l[0];
+            best = id[0];
+        }
+    }
+    return best;
+}
+
 // Record the expert e of a routed token (valid: this lane's row is a token of the frame):
 // assign[token] = e, then either the CTA histogram (added to counts once per CTA; the route
 // kernel builds the permutation from counts) or the token's slot in expert e's bucket, with

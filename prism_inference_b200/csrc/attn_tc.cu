@@ -520,31 +520,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             wait(&bars->lg_full, c_lg.next());
             if (!ok) break;
             if (router) {
-                int best = 0;
-                float bv = 0.0f;
-#pragma unroll 1
-                for (int g = 0; g < npad; g += 32) {
-                    uint32_t v[32];
-                    if (g + 32 <= npad) {
-                        tmem_ld32(tmem + lane_addr + kTPO + g, v);
-                    } else {  // npad is a multiple of 16: the last 16 columns
-                        tmem_ld16(tmem + lane_addr + kTPO + g, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
-#pragma unroll
-                        for (int j = 16; j < 32; ++j) v[j] = 0u;
-                    }
-                    tmem_ld_wait();
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const int e = g + j;
-                        if (e < a.n_experts) {
-                            const float l = rh(__fadd_rn(__uint_as_float(v[j]), bars->br[e]));
-                            if (e == 0 || l > bv) {
-                                bv = l;
-                                best = e;
-                            }
-                        }
-                    }
-                }
+                const float* br = bars->br;
+                const int best = router_argmax(tmem + lane_addr + kTPO, npad, a.n_experts, [br](int e) { return br[e]; });
                 tc_fence_before();
                 arrive(&bars->lg_drained);  // the logits are read: the next tile's out-projection may go
                 route_token(a, bars->hist, valid, token, best, lane);

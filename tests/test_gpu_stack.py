@@ -502,4 +502,7 @@ def test_stack_argument_errors(prism_ctx):
     L = layout.build_stack(256, 1, n_experts=16)
     with pytest.raises(PrismError, match="RANGE"):
         Stack(prism_ctx, L, blob[:1000], 1)
+    from prism_inference_b200 import abi
+    assert st.lib.prism_stack_set_option(st.h, 99, 1) == abi.PRISM_E_ARG  # unknown option
+    assert st.lib.prism_stack_set_option(st.h, abi.OPT_BUCKET_ROUTING, 0) == 0
     st.close()
