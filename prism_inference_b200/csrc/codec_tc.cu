@@ -12,25 +12,38 @@
 //   dec3 / dec2 / dec1_fused   nearest 2x upsample of the deeper map (clamped to its edge)
 //                              concatenated with the skip map, pointwise product, ReLU
 //   pw_conv_coopvec_32to12     32 -> 12 pointwise, ReLU by push constant
-// Each runs here as an implicit GEMM: a tile is 128 consecutive output pixels (rows = MMA M),
-// N = output channels, K = the shader's input vector (channel, ky, kx order), one TMEM
-// accumulator per channel group.  Feature maps are CHW fp16 at element offsets of the caller's
-// arena, read with plain loads at any alignment; the weights are repacked by a small kernel into
-// an aligned K-major copy ([group][N][K padded to 64]) that the weight ring loads by TMA.
+// Each runs here as an implicit GEMM: a tile is 128 output pixels (rows = MMA M), N = output
+// channels, K = the shader's input vector (channel, ky, kx order; tap-major for the 3x3
+// convolutions), one TMEM accumulator per channel group.  Feature maps are CHW fp16 at element
+// offsets of the caller's arena.  Weight matrices of up to 64 KB are built in shared memory from
+// the blob once per CTA (SW128 K-blocks); the two split convolutions' matrices are repacked by a
+// small kernel into an aligned K-major copy that a ring streams by TMA.
 // The ninth shader, pixelshuffle_sigmoid, is elementwise (SIMT kernel at the end of the file).
 //
-// Warp roles (448 threads):
-//   warp 0      producer: weight K-blocks {64 K, N rows} by TMA (128B swizzle, no multicast)
+// Two forms of the contraction kernel:
+//   plain   tiles of 128 consecutive pixels of the map; the gather warps load the patch values
+//           with per-lane 16-bit loads (any alignment; zero outside the map)
+//   staged  (conv3x3_9ch, dec2, dec1, pointwise, when the maps' bases and row pitches are
+//           16-byte multiples) tiles of 128 pixels of one output row; the producer brings each
+//           tile's input rows into shared memory by TMA (3-D boxes {x, y, channel}; the zero fill
+//           outside the map is the padding), up to 8 tiles ahead; the gather warps build the A
+//           tile from there; two epilogue groups take alternate tiles (one TMEM accumulator
+//           buffer each) and stage their output tiles in shared memory for one TMA store each
+//           (clipped at the map's edge).  The per-tile epilogue chain (TMEM load, bias, fp16,
+//           ReLU, stores) is what bounds these passes; the second group and the bulk stores
+//           halve its share.
+//
+// Warp roles (448 threads; 576 in the staged form):
+//   warp 0      producer: staged input rows by TMA; streamed weight K-blocks {64 K, N rows}
+//               (128B swizzle, no multicast)
 //   warp 1      TMEM owner + tcgen05.mma issuer
 //   warps 2-9   gather: warp 2 + 4h + q fills rows 32q.. with K columns [32h, 32h + 32) of every
-//               K-block (the patch values, zero outside the map), 16-byte stores into the
-//               swizzled A tile
-//   warps 10-13 epilogue: TMEM -> the shader's rounding / group rule -> CHW stores (each warp
-//               instruction writes 32 consecutive pixels of one channel)
-// Weight matrices of up to 64 KB (all but the two split convolutions) are loaded into shared
-// memory once per CTA and an 8-stage ring carries the A K-blocks; the split convolutions' weights
-// stream through a 4-stage ring of {A K-block 16 KB, B K-block N x 128 B}.  Every wait is
-// bounded (common.cuh); on timeout the CTA sets the context's error word and winds down.
+//               K-block, 16-byte stores into the swizzled A tile
+//   warps 10-13 epilogue: TMEM -> the shader's rounding / group rule -> CHW output (direct
+//   (+14-17)    stores: each warp instruction writes 32 consecutive pixels of one channel)
+// The A K-blocks pass through a ring of 8 stages (4 in the staged form and with streamed
+// weights, whose B K-blocks share the stage).  Every wait is bounded (common.cuh); on timeout
+// the CTA sets the context's error word and winds down.
 #include <cudaTypedefs.h>
 
 #include <mutex>
@@ -44,7 +57,25 @@ namespace {
 // kinds in the order of prism_codec_kind (include/prism_moe.h)
 enum : int { C_ENC_IC = 0, C_ENC1, C_ENC2, C_ENC3, C_DEC3, C_DEC2, C_DEC1, C_OUT12, C_PS, C_COUNT };
 
-template <int KIND>
+constexpr int kMaxStages = 8;
+constexpr int kMaxStg = 8;  // staging buffers (staged form)
+
+struct Bars {
+    uint64_t a_full[kMaxStages], b_full[kMaxStages], empty[kMaxStages];
+    uint64_t acc_full[2], acc_empty[2], drain, stg_full[kMaxStg], stg_empty[kMaxStg], out_full[2], out_free[2];
+    uint32_t tmem_base;
+    int abort;
+    alignas(8) float bias[128];  // (read as float2 pairs)
+};
+
+// STG: the staged form of a pass whose input is plain row segments (conv3x3_coopvec_9ch, the
+// three decoder passes, the pointwise output): tiles are 128 pixels of one output row and the
+// producer brings each tile's input rows into shared memory by TMA (3-D boxes {x, y, channel} of
+// the CHW maps; the zero fill outside the map is the convolution's padding), two tiles ahead of
+// the gather warps, which then build the A tile from shared memory.  As many staging buffers as
+// shared memory holds (up to 8) keep that many tiles' row loads in flight, which is what a pass
+// of ~0.5 us tiles needs against a ~2 us load latency.
+template <int KIND, bool STG = false>
 struct CodecCfg {
     static constexpr int kType = KIND <= C_ENC3 ? 0 : KIND <= C_DEC1 ? 1 : 2;  // conv3x3, dec, pointwise
     static constexpr int kStride = KIND == C_ENC_IC ? 1 : 2;  // of the 3x3 convolutions
@@ -76,14 +107,35 @@ struct CodecCfg {
     // Weights of up to 64 KB stay in shared memory for the whole CTA (loaded once); larger ones
     // (the split convolutions) stream through the ring beside the A K-blocks.
     static constexpr bool kResident = kWBytes <= 65536;
-    static constexpr int kStages = kResident ? 8 : 4;
+    // (dec3's staging buffers would not fit beside its 64 KB of weights and output staging)
+    static constexpr bool kCanStage = KIND == C_ENC_IC || KIND == C_DEC2 || KIND == C_DEC1 || KIND == C_OUT12;
+    // staged input of one tile: conv3x3_9ch rows y-1..y+1 of all channels, x from x0 - 8 (the
+    // TMA start is 16-byte aligned) over 144 pixels; dec: one row of the deeper map (64 pixels
+    // from x0 / 2) and of the skip map (128 pixels); pointwise: one row of 128 pixels
+    static constexpr int kStgUp = kType == 1 ? kUp * 64 * 2 : 0;
+    static constexpr int kStgBytes = !STG ? 0 : kType == 0 ? kIn * 3 * 144 * 2 : kType == 1 ? kStgUp + kSkip * 128 * 2
+                                                                                              : kIn * 128 * 2;
+    static constexpr int kStgBuf = (kStgBytes + 1023) / 1024 * 1024;
+    static constexpr int kWRes = kResident ? (kWBytes + 1023) / 1024 * 1024 : 0;
+    // epilogue groups of four warps: two take alternate tiles (one TMEM accumulator buffer each)
+    // in the staged form (its gather needs few registers: 576 threads fit without spills)
+    static constexpr int kEpiGroups = kAccBufs == 2 && STG ? 2 : 1;
+    static constexpr int kThreads = 32 * (10 + 4 * kEpiGroups);
+    // output staging (two epilogue groups): a tile of [kN channels][128 pixels] per group, written
+    // by one TMA store.  (With one group the TMA hand-off lengthens the per-tile chain: direct
+    // stores measured faster there, and the plain-load gather keeps the L1 this would take.)
+    static constexpr int kOutBuf = kEpiGroups == 2 ? (kN * 256 + 1023) / 1024 * 1024 : 0;
+    static constexpr int kReserve = 2 * kOutBuf + (int)sizeof(Bars) + 1024;
+    static constexpr int kStages = !kResident || STG || 8 * 16384 + kWRes + kReserve > 232448 ? 4 : 8;  // A ring
     static constexpr int kStageBytes = kResident ? 16384 : 32768;  // A (+ B when streamed)
     static constexpr int kWOff = kStages * kStageBytes;         // resident weights
-    static constexpr int kBarOff = kWOff + (kResident ? (kWBytes + 1023) / 1024 * 1024 : 0);
+    static constexpr int kStgOff = kWOff + kWRes;               // the input staging buffers
+    static constexpr int kStgFit = !STG ? 0 : (232448 - kReserve - kStgOff) / kStgBuf;
+    static constexpr int kStgN = kStgFit > kMaxStg ? kMaxStg : kStgFit;
+    static constexpr int kOutOff = kStgOff + kStgN * kStgBuf;
+    static constexpr int kBarOff = kOutOff + 2 * kOutBuf;
 };
 
-constexpr int kThreads = 32 * 14;
-constexpr int kMaxStages = 8;
 constexpr int kABytes = 128 * 128;  // one A K-block: 128 rows x 64 fp16, SW128
 
 struct CodecArgs {
@@ -94,19 +146,13 @@ struct CodecArgs {
     int relu;            // conv3x3_9ch / pw: the push constant (1 = ReLU)
     const __half* blob;  // the weights arena: matrix at element wo, biases at bo (any alignment)
     int wo, bo;
+    int tma_out;         // 1: output tiles staged in shared memory and written by TMA (tm_out)
     uint32_t* err;
 };
 
-struct Bars {
-    uint64_t a_full[kMaxStages], b_full[kMaxStages], empty[kMaxStages];
-    uint64_t acc_full[2], acc_empty[2], drain;
-    uint32_t tmem_base;
-    int abort;
-    float bias[128];
-};
-template <int KIND>
+template <int KIND, bool STG>
 constexpr int codec_smem() {  // + alignment slack of the dynamic base
-    return CodecCfg<KIND>::kBarOff + (int)sizeof(Bars) + 1024;
+    return CodecCfg<KIND, STG>::kBarOff + (int)sizeof(Bars) + 1024;
 }
 
 PRISM_DEV uint16_t h_bits(float f) { return __half_as_ushort(__float2half_rn(f)); }
@@ -114,10 +160,13 @@ PRISM_DEV float bits_h(uint16_t b) { return __half2float(__ushort_as_half(b)); }
 // `if (v < 0) v = 0` on an fp16 value (negative zero stays, as in the shaders)
 PRISM_DEV uint16_t relu_bits(uint16_t b) { return bits_h(b) < 0.0f ? (uint16_t)0 : b; }
 
-template <int KIND>
-__global__ void __launch_bounds__(kThreads, 1)
-    codec_tc_kernel(const CodecArgs a, const __grid_constant__ CUtensorMap tm_w) {
-    using C = CodecCfg<KIND>;
+template <int KIND, bool STG>
+__global__ void __launch_bounds__(CodecCfg<KIND, STG>::kThreads, 1)
+    codec_tc_kernel(const CodecArgs a, const __grid_constant__ CUtensorMap tm_w,
+                    const __grid_constant__ CUtensorMap tm_in, const __grid_constant__ CUtensorMap tm_skip,
+                    const __grid_constant__ CUtensorMap tm_out) {
+    using C = CodecCfg<KIND, STG>;
+    static_assert(!STG || (C::kCanStage && C::kResident && C::kG == 1 && C::kStgN >= 2), "staged form");
     constexpr int kStages = C::kStages, kStageBytes = C::kStageBytes;
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -125,7 +174,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     volatile int* abort = &bars->abort;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int out_px = a.out_w * a.out_h;
-    const int n_tiles = (out_px + 127) >> 7;
+    // staged: out_h rows of tpr tiles (128 pixels of one row each); else 128 consecutive pixels
+    const int tpr = (a.out_w + 127) >> 7;
+    const int n_tiles = STG ? a.out_h * tpr : (out_px + 127) >> 7;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -138,6 +189,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&bars->acc_empty[b], 4);
         }
         mbar_init(&bars->drain, 1);
+        for (int b = 0; b < C::kStgN; ++b) {
+            mbar_init(&bars->stg_full[b], 1);
+            mbar_init(&bars->stg_empty[b], 8);  // the eight gather warps
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&bars->out_full[b], 4);  // the four epilogue warps have written the tile
+            mbar_init(&bars->out_free[b], 1);  // its previous TMA store has read the buffer
+        }
         bars->abort = 0;
         fence_barrier_init();
     }
@@ -194,6 +253,31 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (warp == 0) {
         // ============================ producer ============================
+        if (STG && lane == 0) {  // each tile's input rows, kStgN tiles ahead of the gather
+            prefetch_tmap(&tm_in);
+            if (C::kType == 1) prefetch_tmap(&tm_skip);
+            int b = 0;
+            uint32_t bph = 0;
+            for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+                if (!mbar_wait(&bars->stg_empty[b], bph ^ 1, abort)) break;
+                const int oy = tile / tpr, x0 = (tile - oy * tpr) * 128;
+                uint64_t* bar = &bars->stg_full[b];
+                const uint32_t dst = smem_u32(smem + C::kStgOff + b * C::kStgBuf);
+                mbar_expect_tx(bar, C::kStgBytes);
+                if (C::kType == 0) {
+                    tma_load_3d(dst, &tm_in, bar, x0 - 8, oy - 1, 0);
+                } else if (C::kType == 1) {
+                    tma_load_3d(dst, &tm_in, bar, x0 >> 1, min(oy >> 1, a.in_h - 1), 0);
+                    tma_load_3d(dst + C::kStgUp, &tm_skip, bar, x0, oy, 0);
+                } else {
+                    tma_load_3d(dst, &tm_in, bar, x0, oy, 0);
+                }
+                if (++b == C::kStgN) {
+                    b = 0;
+                    bph ^= 1;
+                }
+            }
+        }
         if (lane == 0 && !C::kResident) {  // the streamed weight K-blocks beside the A K-blocks
             prefetch_tmap(&tm_w);
             int s = 0;
@@ -250,6 +334,79 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mma_commit_w(&bars->drain);
         mbar_wait_w(&bars->drain, 0, abort);
+    } else if (STG && warp < 10) {
+        // ============================ gather (staged input) ============================
+        // warp 2 + 4h + q fills rows 32q.. with K columns [32h, 32h + 32) of every K-block, read
+        // from the tile's staging buffer (lanes = consecutive pixels: conflict-free 16-bit reads)
+        const int gw = warp - 2, quad = gw & 3, half = gw >> 2;
+        const int row = quad * 32 + lane;
+        int s = 0, b = 0;
+        uint32_t ph = 0, bph = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
+            const int oy = tile / tpr, x0 = (tile - oy * tpr) * 128;
+            if (!mbar_wait(&bars->stg_full[b], bph, abort)) break;
+            const unsigned short* sg = reinterpret_cast<const unsigned short*>(smem + C::kStgOff + b * C::kStgBuf);
+#pragma unroll 1
+            for (int kb = 0; kb < C::kKB; ++kb) {
+                const int k0 = kb * 64 + half * 32;
+                uint32_t w[16];
+                if constexpr (C::kType == 0) {
+                    // taps k0 / 16 and k0 / 16 + 1 (16 channel slots each, channels 0..8 real)
+#pragma unroll
+                    for (int tt = 0; tt < 2; ++tt) {
+                        const int t = k0 / C::kCgP + tt;
+                        const int base = (t / 3) * 144 + row + t % 3 + 7;  // x - (x0 - 8) = row + dx - 1 + 8
+#pragma unroll
+                        for (int c = 0; c < 16; c += 2) {
+                            const uint32_t v0 = t < 9 && c < C::kIn ? sg[c * 432 + base] : 0u;
+                            const uint32_t v1 = t < 9 && c + 1 < C::kIn ? sg[(c + 1) * 432 + base] : 0u;
+                            w[tt * 8 + c / 2] = v0 | (v1 << 16);
+                        }
+                    }
+                } else {
+                    const unsigned short* src;
+                    int pitch;
+                    if (C::kType == 1 && k0 < C::kUp) {  // the deeper map, nearest, clamped
+                        src = sg + k0 * 64 + (min((x0 + row) >> 1, a.in_w - 1) - (x0 >> 1));
+                        pitch = 64;
+                    } else {  // the skip map, or the pointwise input
+                        src = sg + C::kStgUp / 2 + (k0 - (C::kType == 1 ? C::kUp : 0)) * 128 + row;
+                        pitch = 128;
+                    }
+                    if (k0 < C::kKG) {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j)
+                            w[j] = (uint32_t)src[2 * j * pitch] | ((uint32_t)src[(2 * j + 1) * pitch] << 16);
+                    } else {  // K padding
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) w[j] = 0u;
+                    }
+                }
+                if (!mbar_wait(&bars->empty[s], ph ^ 1, abort)) {
+                    ok = false;
+                    break;
+                }
+                unsigned char* dst = stage_a(s);
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+                    *reinterpret_cast<uint4*>(dst + sw128_off(row, half * 4 + c)) =
+                        make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+                fence_async_shared();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bars->a_full[s]);
+                if (++s == kStages) {
+                    s = 0;
+                    ph ^= 1;
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->stg_empty[b]);  // this warp is done with the buffer
+            if (++b == C::kStgN) {
+                b = 0;
+                bph ^= 1;
+            }
+        }
     } else if (warp < 10) {
         // ============================ gather ============================
         // The values are fp16 already and go to the A tile unchanged, so each lane issues its 32
@@ -345,18 +502,46 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else {
         // ============================ epilogue ============================
+        // With tma_out, each tile's output goes to a shared-memory tile [channel][128 pixels] (a
+        // thread per pixel: conflict-free 16-bit stores) that one TMA store writes to the CHW map,
+        // clipped at the map's edge; two such tiles alternate.  Otherwise 16-bit global stores.
+        const bool tma_out = C::kOutBuf > 0 && a.tma_out;  // (staging exists only with two groups)
         const int quad = warp & 3;
         const int row = quad * 32 + lane;
         const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
+        const int eg = (warp - 10) >> 2;            // epilogue group: tiles it = eg, eg + kEpiGroups, ..
+        const int store_warp = 10 + 4 * eg;          // its lane 0 issues the group's TMA stores
+        const bool issuer = warp == store_warp && lane == 0;
         constexpr int kChunk = C::kNP >= 32 && C::kG == 1 ? 32 : 16;  // columns per TMEM load and group
-        uint32_t it = 0;
-        for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
+        uint32_t it = eg;
+        for (int tile = blockIdx.x + eg * gridDim.x; tile < n_tiles; tile += C::kEpiGroups * gridDim.x, it += C::kEpiGroups) {
             const int buf = C::kAccBufs == 2 ? (int)(it & 1) : 0;
             const uint32_t use = C::kAccBufs == 2 ? (it >> 1) : it;
-            if (!mbar_wait(&bars->acc_full[buf], use & 1, abort)) break;
+            const int ob_i = it & 1;
+            const uint32_t ob_use = it >> 1;
+            unsigned short* ob = reinterpret_cast<unsigned short*>(smem + C::kOutOff + ob_i * C::kOutBuf);
+            if (tma_out && ob_use > 0) {
+                if (issuer) {  // the store of two tiles ago has read this buffer
+                    if (C::kEpiGroups == 2) tma_store_wait_read<0>();  // (the group's only buffer)
+                    else tma_store_wait_read<1>();
+                    mbar_arrive(&bars->out_free[ob_i]);
+                }
+                if (!mbar_wait_w(&bars->out_free[ob_i], (ob_use - 1) & 1, abort)) break;
+            }
+            if (!mbar_wait_w(&bars->acc_full[buf], use & 1, abort)) break;
             tc_fence_after();
-            const int p = tile * 128 + row;
-            const bool valid = p < out_px;
+            int p, sx, sy;  // pixel index; the tile's TMA store coordinates
+            bool valid;
+            if constexpr (STG) {
+                const int oy = tile / tpr, x0 = (tile - oy * tpr) * 128;
+                p = oy * a.out_w + x0 + row;
+                valid = x0 + row < a.out_w;
+                sx = x0, sy = oy;
+            } else {
+                p = tile * 128 + row;
+                valid = p < out_px;
+                sx = tile * 128, sy = 0;
+            }
 #pragma unroll 1
             for (int cc = 0; cc < C::kNP; cc += kChunk) {
                 uint32_t v[C::kG][32];
@@ -367,6 +552,35 @@ __global__ void __launch_bounds__(kThreads, 1)
                     else tmem_ld16(t, *reinterpret_cast<uint32_t(*)[16]>(&v[g][0]));
                 }
                 tmem_ld_wait();
+                if constexpr (KIND != C_ENC2 && KIND != C_ENC3) {
+                    // two channels per step: h(acc + bias) as one f32x2 add and one f16x2
+                    // conversion (each element rounded as alone), then the ReLU (`if (v < 0) v = 0`:
+                    // -0 and NaN stay) as a half2 mask
+                    const bool relu = KIND == C_ENC_IC || KIND == C_OUT12 ? a.relu == 1 : true;
+#pragma unroll
+                    for (int j = 0; j < kChunk; j += 2) {
+                        const int c = cc + j;
+                        if (c >= C::kN) break;  // (kN is even)
+                        const float2 b = *reinterpret_cast<const float2*>(&bars->bias[c]);
+                        float s0, s1;
+                        f2_unpack(f2_add(f2_pack(__uint_as_float(v[0][j]), __uint_as_float(v[0][j + 1])),
+                                         f2_pack(b.x, b.y)),
+                                  s0, s1);
+                        uint32_t h = pack_h2(s0, s1);
+                        if (relu) {
+                            const __half2 hv = *reinterpret_cast<const __half2*>(&h);
+                            h &= ~__hlt2_mask(hv, __float2half2_rn(0.0f));
+                        }
+                        if (tma_out) {
+                            ob[c * 128 + row] = (unsigned short)(h & 0xffffu);
+                            ob[(c + 1) * 128 + row] = (unsigned short)(h >> 16);
+                        } else if (valid) {
+                            a.out[(size_t)c * out_px + p] = __ushort_as_half((unsigned short)(h & 0xffffu));
+                            a.out[(size_t)(c + 1) * out_px + p] = __ushort_as_half((unsigned short)(h >> 16));
+                        }
+                    }
+                    continue;
+                }
 #pragma unroll
                 for (int j = 0; j < kChunk; ++j) {
                     const int c = cc + j;
@@ -390,18 +604,32 @@ __global__ void __launch_bounds__(kThreads, 1)
                             acc = h_bits(__fsub_rn(__fadd_rn(bits_h(acc), pg), b));
                         }
                         o = relu_bits(acc);
-                    } else if constexpr (KIND == C_ENC_IC || KIND == C_OUT12) {
-                        o = a.relu == 1 ? relu_bits(p0) : p0;
                     } else {
-                        o = relu_bits(p0);
+                        o = p0;  // (the other kinds take the paired path above)
                     }
-                    if (valid) a.out[(size_t)c * out_px + p] = __ushort_as_half(o);
+                    if (tma_out)
+                        ob[c * 128 + row] = o;
+                    else if (valid)
+                        a.out[(size_t)c * out_px + p] = __ushort_as_half(o);
                 }
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&bars->acc_empty[buf]);
+            if (tma_out) {
+                fence_async_shared();  // the tile's stores, for the TMA engine
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bars->out_full[ob_i]);
+                if (warp == store_warp) {  // the issuing warp waits for all four (warp-uniform result)
+                    if (!mbar_wait_w(&bars->out_full[ob_i], ob_use & 1, abort)) break;
+                    if (issuer) {
+                        tma_store_3d(&tm_out, smem_u32(ob), sx, sy, 0);
+                        tma_store_commit();
+                    }
+                }
+            }
         }
+        if (tma_out && issuer) tma_store_wait0();  // the output is written before the CTA exits
     }
 
     tc_fence_before();
@@ -545,12 +773,52 @@ int run_codec(prism_ctx* ctx, const int32_t* q, const __half* weights, size_t we
     a.wo = wo;
     a.bo = bo;
     a.err = ctx->err;
-    const int n_tiles = (int)((out_px + 127) / 128);
-    constexpr int smem = codec_smem<KIND>();
-    static_assert(smem <= 232448, "shared memory budget");
-    cudaError_t e = cudaFuncSetAttribute(codec_tc_kernel<KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e == cudaSuccess) {
-        e = launch_pdl(codec_tc_kernel<KIND>, dim3(std::min(ctx->sm_count, n_tiles)), dim3(kThreads), smem, s, a, tm);
+    // TMA maps (3-D {x, y, channel}, no swizzle) need 16-byte aligned bases and row pitches: the
+    // staged form's input maps, and the output map (else the epilogue stores directly)
+    auto fn = encode_tiled();
+    auto map3 = [&](CUtensorMap* m, const __half* base, int64_t w, int64_t h, int c, int bw, int bh) {
+        if (!fn || ((uintptr_t)base & 15) || (w * 2) % 16) return false;
+        cuuint64_t dims[3] = {(cuuint64_t)w, (cuuint64_t)h, (cuuint64_t)c};
+        cuuint64_t strides[2] = {(cuuint64_t)w * 2, (cuuint64_t)(w * h * 2)};
+        cuuint32_t box[3] = {(cuuint32_t)bw, (cuuint32_t)bh, (cuuint32_t)c};
+        cuuint32_t estr[3] = {1, 1, 1};
+        return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<__half*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    };
+    CUtensorMap tin{}, tskip{}, tout{};
+    bool staged = false;
+    if constexpr (C::kCanStage) {
+        if (C::kType == 0)
+            staged = map3(&tin, a.in, in_w, in_h, C::kIn, 144, 3);
+        else if (C::kType == 1)
+            staged = map3(&tin, a.in, in_w, in_h, C::kUp, 64, 1) && map3(&tskip, a.skip, out_w, out_h, C::kSkip, 128, 1);
+        else
+            staged = map3(&tin, a.in, in_w, in_h, C::kIn, 128, 1);
+    }
+    // output tiles: 128 pixels of one row (staged) or 128 consecutive pixels of the map
+    a.tma_out = staged && CodecCfg<KIND, C::kCanStage>::kEpiGroups == 2 &&
+                        map3(&tout, a.out, out_w, out_h, C::kN, 128, 1)
+                    ? 1
+                    : 0;
+    cudaError_t e;
+    if (staged) {
+        constexpr bool kStg = C::kCanStage;  // (always true here; keeps the template well-formed)
+        const int n_tiles = out_h * ((out_w + 127) / 128);
+        constexpr int smem = codec_smem<KIND, kStg>();
+        static_assert(smem <= 232448, "shared memory budget");
+        e = cudaFuncSetAttribute(codec_tc_kernel<KIND, kStg>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e == cudaSuccess)
+            e = launch_pdl(codec_tc_kernel<KIND, kStg>, dim3(std::min(ctx->sm_count, n_tiles)),
+                           dim3(CodecCfg<KIND, kStg>::kThreads), smem, s, a, tm, tin, tskip, tout);
+    } else {
+        const int n_tiles = (int)((out_px + 127) / 128);
+        constexpr int smem = codec_smem<KIND, false>();
+        static_assert(smem <= 232448, "shared memory budget");
+        e = cudaFuncSetAttribute(codec_tc_kernel<KIND, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e == cudaSuccess)
+            e = launch_pdl(codec_tc_kernel<KIND, false>, dim3(std::min(ctx->sm_count, n_tiles)),
+                           dim3(CodecCfg<KIND, false>::kThreads), smem, s, a, tm, tin, tskip, tout);
     }
     if (e != cudaSuccess) return set_error(PRISM_E_CUDA, "prism_codec_pass: %s", cudaGetErrorString(e));
     return PRISM_OK;

@@ -42,19 +42,22 @@ def test_codec_pass_matches_reference_golden(prism_ctx, name):
     assert_close(output_of(c), gold, name)
 
 
-def _chain(w0, h0, seed):
+def _chain(w0, h0, seed, feat_pad=1):
     """Weights, feature arena and dispatch list of one frame's encoder / decoder path at a
-    render size of w0 x h0, with weights and maps at odd (unaligned) element offsets."""
+    render size of w0 x h0, with weights at odd element offsets and the maps at odd offsets
+    (feat_pad=1: every pass gathers with plain loads) or 16-byte aligned ones (feat_pad=0: the
+    passes whose map rows are 16-byte multiples stage their input rows by TMA)."""
     from prism_inference_b200 import codec
-    fc = codec.frame_chain(w0, h0, weight_pad=3, feat_pad=1)
+    fc = codec.frame_chain(w0, h0, weight_pad=3, feat_pad=feat_pad)
     blob, feat = codec.synthetic(fc, seed)
     return blob, feat, fc.passes, fc.pixelshuffle, fc.feat_off, fc.feat_size, fc.rgb_elems
 
 
-def test_codec_passes_at_reference_frame_size(prism_ctx, oracle):
+@pytest.mark.parametrize("feat_pad", [1, 0], ids=["plain-gather", "tma-staged"])
+def test_codec_passes_at_reference_frame_size(prism_ctx, oracle, feat_pad):
     """Each pass at the reference's sizes (960x540 render, 120x68 bottleneck), on the GPU's own
     inputs for that pass (the oracle is given the same arena), so each pass is checked alone."""
-    blob, feat, passes, ps, fo, sizes, n_rgb = _chain(960, 540, 3)
+    blob, feat, passes, ps, fo, sizes, n_rgb = _chain(960, 540, 3, feat_pad)
     w, f = _dev(blob), _dev(feat)
     for shader, push, out in passes:
         cur = _host(f)
@@ -72,12 +75,15 @@ def test_codec_passes_at_reference_frame_size(prism_ctx, oracle):
     assert_close(_host(rgb), ref, "pixelshuffle_sigmoid")
 
 
-@pytest.mark.parametrize("w0,h0,seed", [(40, 22, 6), (17, 9, 5), (2, 1, 7), (130, 70, 8)])
-def test_codec_chain_matches_oracle(prism_ctx, oracle, w0, h0, seed):
+@pytest.mark.parametrize("w0,h0,seed,feat_pad", [(40, 22, 6, 1), (17, 9, 5, 1), (2, 1, 7, 1), (130, 70, 8, 1),
+                                                 (192, 100, 9, 0), (64, 3, 10, 0), (136, 72, 11, 0)])
+def test_codec_chain_matches_oracle(prism_ctx, oracle, w0, h0, seed, feat_pad):
     """The whole chain run independently on the GPU and by the oracle, odd and degenerate frame
-    sizes included (partial 128-pixel tiles, maps of one pixel): the final RGB agrees."""
+    sizes included (partial 128-pixel tiles, maps of one pixel): the final RGB agrees.  The
+    aligned cases run the TMA-staged passes on rows with a partial last tile (192 = 128 + 64),
+    maps narrower than a tile and one row high, and a mix (136 wide: 68-pixel rows fall back)."""
     import torch
-    blob, feat, passes, ps, fo, sizes, n_rgb = _chain(w0, h0, seed)
+    blob, feat, passes, ps, fo, sizes, n_rgb = _chain(w0, h0, seed, feat_pad)
     w, f = _dev(blob), _dev(feat)
     rgb = torch.zeros(n_rgb, dtype=torch.float16, device="cuda")
     for shader, push, _ in passes:
