@@ -113,7 +113,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     using Cfg = AttnCfg<D>;
     constexpr int kKB = Cfg::kKB, kHeads = Cfg::kHeads, kStage = Cfg::kStage;
     extern __shared__ unsigned char smem_raw[];
-    unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    unsigned char* smem = smem_align1k(smem_raw);
     unsigned char* sX = smem + Cfg::kOffX;
     unsigned char* sQ = smem + Cfg::kOffQ;
     unsigned char* sK = smem + Cfg::kOffK;

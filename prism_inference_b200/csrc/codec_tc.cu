@@ -169,7 +169,7 @@ __global__ void __launch_bounds__(CodecCfg<KIND, STG>::kThreads, 1)
     static_assert(!STG || (C::kCanStage && C::kResident && C::kG == 1 && C::kStgN >= 2), "staged form");
     constexpr int kStages = C::kStages, kStageBytes = C::kStageBytes;
     extern __shared__ unsigned char smem_raw[];
-    unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    unsigned char* smem = smem_align1k(smem_raw);
     Bars* bars = reinterpret_cast<Bars*>(smem + C::kBarOff);
     volatile int* abort = &bars->abort;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;

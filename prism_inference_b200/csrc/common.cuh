@@ -27,6 +27,13 @@ constexpr uint64_t kWaitLimitNs = 2000000000ull;
 PRISM_DEV uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
+// The dynamic shared-memory base rounded up to 1024 bytes by pointer arithmetic on the
+// __shared__ array itself: the compiler then knows every pointer derived from it is in the
+// shared window and emits shared-memory loads and stores (a base rebuilt from an integer is a
+// generic address, and generic accesses go through the slower L1 path).
+PRISM_DEV unsigned char* smem_align1k(unsigned char* raw) {
+    return raw + ((1024u - (smem_u32(raw) & 1023u)) & 1023u);
+}
 PRISM_DEV uint64_t globaltimer() {
     uint64_t t;
     asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));

@@ -276,6 +276,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     expert_tc_kernel(const FfnArgs a, const __grid_constant__ CUtensorMap tm_w1,
                      const __grid_constant__ CUtensorMap tm_w2) {
     extern __shared__ unsigned char smem_raw[];
+    // (a generic base, rebuilt from an integer: measured 5 % faster for this kernel than the
+    // shared-window base of smem_align1k, 0.171 against 0.180 ms per 64-frame launch, while the
+    // attention and codec kernels gain from the shared window)
     unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     unsigned char* sA = smem + kOffA;
     unsigned char* sO = smem + kOffO;

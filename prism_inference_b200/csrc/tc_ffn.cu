@@ -75,7 +75,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     using Cfg = FfnCfg<MODE, KIN, HID, NOUT>;
     extern __shared__ unsigned char smem_raw[];
     // 1024-byte alignment for the swizzled operand tiles
-    unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    unsigned char* smem = smem_align1k(smem_raw);
     unsigned char* sA = smem;
     unsigned char* sH = sA + Cfg::kA;
     unsigned char* sW = sH + Cfg::kH;
