@@ -589,12 +589,14 @@ def run_codec(args):
     pushes = [p[1] for p in fc.passes] + [fc.pixelshuffle]
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(len(names) + 1)]
 
-    def frame(timed=False):
+    def frame(timed=False, fb=None, rb=None):
         stream = torch.cuda.current_stream()
+        fb = f if fb is None else fb
+        rb = rgb if rb is None else rb
         for i, (sh, pc) in enumerate(zip(names, pushes)):
             if timed:
                 ev[i].record(stream)
-            ctx.codec_pass(sh, pc, w, f, rgb if sh == "pixelshuffle_sigmoid" else None, stream)
+            ctx.codec_pass(sh, pc, w, fb, rb if sh == "pixelshuffle_sigmoid" else None, stream)
         if timed:
             ev[-1].record(stream)
 
@@ -636,21 +638,59 @@ def run_codec(args):
     e1.record(stream)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.steps
-    # end to end: the frame from page-locked host memory and the RGB back, every step
+    # end to end, as a serving loop runs it: every step uploads its frame from page-locked host
+    # memory into one of two device frame slots, replays the chain there and downloads its RGB,
+    # with the upload of the next frame and the download of the previous one on their own
+    # streams (the copies cross PCIe in both directions while the chain runs)
     o, n = fc.feat_off["in"], fc.feat_size["in"]
     xin = torch.from_numpy(feat[o:o + n].view(np.int16)).view(torch.float16).pin_memory()
-    rgb_h = torch.empty(fc.rgb_elems, dtype=torch.float16).pin_memory()
+    rgb_h = [torch.empty(fc.rgb_elems, dtype=torch.float16).pin_memory() for _ in range(2)]
+    slots = [(f, rgb), (f.clone(), torch.zeros_like(rgb))]
+    graphs = [g]
+    with torch.cuda.stream(side):
+        frame(fb=slots[1][0], rb=slots[1][1])
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    g1 = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g1):
+        frame(fb=slots[1][0], rb=slots[1][1])
+    graphs.append(g1)
+    up, comp, down = torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream()
+    uploaded = [torch.cuda.Event() for _ in range(2)]
+    computed = [torch.cuda.Event() for _ in range(2)]
+    downloaded = [torch.cuda.Event() for _ in range(2)]
+    steps_e2e = max(args.steps, 20)
     torch.cuda.synchronize()
     e0.record(stream)
-    for _ in range(args.steps):
-        f[o:o + n].copy_(xin, non_blocking=True)
-        g.replay()
-        rgb_h.copy_(rgb, non_blocking=True)
+    for st_ in (up, comp, down):
+        st_.wait_stream(stream)
+    for i in range(steps_e2e):
+        sl = i % 2
+        fb, rb = slots[sl]
+        with torch.cuda.stream(up):
+            if i >= 2:
+                up.wait_event(computed[sl])  # the chain of two steps ago has read this slot's input
+            fb[o:o + n].copy_(xin, non_blocking=True)
+            uploaded[sl].record(up)
+        with torch.cuda.stream(comp):
+            comp.wait_event(uploaded[sl])
+            if i >= 2:
+                comp.wait_event(downloaded[sl])  # this slot's RGB of two steps ago is home
+            graphs[sl].replay()
+            computed[sl].record(comp)
+        with torch.cuda.stream(down):
+            down.wait_event(computed[sl])
+            rgb_h[sl].copy_(rb, non_blocking=True)
+            downloaded[sl].record(down)
+    for st_ in (up, comp, down):
+        stream.wait_stream(st_)
     e1.record(stream)
     torch.cuda.synchronize()
-    ms_e2e = e0.elapsed_time(e1) / args.steps
+    ms_e2e = e0.elapsed_time(e1) / steps_e2e
+    if not torch.equal(rgb_h[(steps_e2e - 1) % 2].view(torch.int16), rgb.cpu().view(torch.int16)):
+        raise RuntimeError("codec e2e: the downloaded RGB differs from the device-resident chain's")
     clk = clocks.stop(mark)
-    del g
+    del g, g1, graphs
     ctx.status()
     if ws > 1:
         t = torch.tensor([ms, ms_e2e], dtype=torch.float64, device="cuda")
@@ -676,8 +716,9 @@ def run_codec(args):
                            "frames_per_gpu": 1, "passes_eager": rows, "algorithmic_bytes_per_frame": total_bytes,
                            "l2": "maps of one frame total 140 MB; a pass reads the previous pass's output"},
                 "e2e": {"value": ws * 1e3 / ms_e2e, "unit": "frames/s", "h2d_bytes_per_step": int(xin.numel() * 2),
-                        "d2h_bytes_per_step": int(rgb_h.numel() * 2), "ms_per_step": ms_e2e,
-                        "api": "prism_codec_pass per pass (graph replay); frame in / RGB out through page-locked host memory"},
+                        "d2h_bytes_per_step": int(rgb_h[0].numel() * 2), "ms_per_step": ms_e2e, "steps": steps_e2e,
+                        "api": "prism_codec_pass per pass (graph replay); frame in / RGB out through page-locked host memory",
+                        "overlap": "upload, chain and download of neighbouring steps on three streams, two device frame slots"},
                 # a pass kernel each, a weight repack before each pass whose matrix streams (over
                 # 64 KB: the two split convolutions), the pixel shuffle
                 "gpu_launches": len(fc.passes) + sum(p[0].startswith("strided_conv_split") for p in fc.passes) + 1,
