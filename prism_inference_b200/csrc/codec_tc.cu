@@ -31,9 +31,9 @@
 //           buffer each) and stage their output tiles in shared memory for one TMA store each
 //           (clipped at the map's edge).  The per-tile epilogue chain (TMEM load, bias, fp16,
 //           ReLU, stores) is what bounds these passes; the second group and the bulk stores
-//           halve its share.
+//           halve its share.  dec3 (plain form) takes the two epilogue groups as well.
 //
-// Warp roles (448 threads; 576 in the staged form):
+// Warp roles (448 threads; 576 with two epilogue groups):
 //   warp 0      producer: staged input rows by TMA; streamed weight K-blocks {64 K, N rows}
 //               (128B swizzle, no multicast)
 //   warp 1      TMEM owner + tcgen05.mma issuer
@@ -118,15 +118,19 @@ struct CodecCfg {
     static constexpr int kStgBuf = (kStgBytes + 1023) / 1024 * 1024;
     static constexpr int kWRes = kResident ? (kWBytes + 1023) / 1024 * 1024 : 0;
     // epilogue groups of four warps: two take alternate tiles (one TMEM accumulator buffer each)
-    // in the staged form (its gather needs few registers: 576 threads fit without spills)
-    static constexpr int kEpiGroups = kAccBufs == 2 && STG ? 2 : 1;
+    // in the staged form and for dec3 (576 threads cap a thread at 96 registers: the plain-load
+    // gathers of the strided convolutions then spill and ran 20-25 % slower with two groups)
+    static constexpr int kEpiGroups = kAccBufs == 2 && (STG || KIND == C_DEC3) ? 2 : 1;
     static constexpr int kThreads = 32 * (10 + 4 * kEpiGroups);
     // output staging (two epilogue groups): a tile of [kN channels][128 pixels] per group, written
     // by one TMA store.  (With one group the TMA hand-off lengthens the per-tile chain: direct
     // stores measured faster there, and the plain-load gather keeps the L1 this would take.)
     static constexpr int kOutBuf = kEpiGroups == 2 ? (kN * 256 + 1023) / 1024 * 1024 : 0;
     static constexpr int kReserve = 2 * kOutBuf + (int)sizeof(Bars) + 1024;
-    static constexpr int kStages = !kResident || STG || 8 * 16384 + kWRes + kReserve > 232448 ? 4 : 8;  // A ring
+    // A ring: 8 stages where they fit (the per-stage round trip gather -> MMA -> release bounds a
+    // shallow ring), beside at least two staging buffers in the staged form
+    static constexpr int kFixed = kWRes + kReserve + (STG ? 2 * kStgBuf : 0);
+    static constexpr int kStages = !kResident ? 4 : 8 * 16384 + kFixed <= 232448 ? 8 : 6 * 16384 + kFixed <= 232448 ? 6 : 4;
     static constexpr int kStageBytes = kResident ? 16384 : 32768;  // A (+ B when streamed)
     static constexpr int kWOff = kStages * kStageBytes;         // resident weights
     static constexpr int kStgOff = kWOff + kWRes;               // the input staging buffers
@@ -797,10 +801,10 @@ int run_codec(prism_ctx* ctx, const int32_t* q, const __half* weights, size_t we
             staged = map3(&tin, a.in, in_w, in_h, C::kIn, 128, 1);
     }
     // output tiles: 128 pixels of one row (staged) or 128 consecutive pixels of the map
-    a.tma_out = staged && CodecCfg<KIND, C::kCanStage>::kEpiGroups == 2 &&
-                        map3(&tout, a.out, out_w, out_h, C::kN, 128, 1)
-                    ? 1
-                    : 0;
+    if (staged)
+        a.tma_out = CodecCfg<KIND, C::kCanStage>::kEpiGroups == 2 && map3(&tout, a.out, out_w, out_h, C::kN, 128, 1);
+    else
+        a.tma_out = CodecCfg<KIND, false>::kEpiGroups == 2 && map3(&tout, a.out, out_px, 1, C::kN, 128, 1);
     cudaError_t e;
     if (staged) {
         constexpr bool kStg = C::kCanStage;  // (always true here; keeps the template well-formed)
