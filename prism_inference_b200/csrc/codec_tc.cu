@@ -27,7 +27,8 @@
 //           16-byte multiples) tiles of 128 pixels of one output row; the producer brings each
 //           tile's input rows into shared memory by TMA (3-D boxes {x, y, channel}; the zero fill
 //           outside the map is the padding), up to 8 tiles ahead; the gather warps build the A
-//           tile from there; two epilogue groups take alternate tiles (one TMEM accumulator
+//           tile from there (dec / pointwise: 64-pixel 128B-swizzled rows, transposed 8 x 8 at a
+//           time by ldmatrix.trans + stmatrix); two epilogue groups take alternate tiles (one TMEM accumulator
 //           buffer each) and stage their output tiles in shared memory for one TMA store each
 //           (clipped at the map's edge).  The per-tile epilogue chain (TMEM load, bias, fp16,
 //           ReLU, stores) is what bounds these passes; the second group and the bulk stores
@@ -270,11 +271,13 @@ __global__ void __launch_bounds__(CodecCfg<KIND, STG>::kThreads, 1)
                 mbar_expect_tx(bar, C::kStgBytes);
                 if (C::kType == 0) {
                     tma_load_3d(dst, &tm_in, bar, x0 - 8, oy - 1, 0);
-                } else if (C::kType == 1) {
+                } else if (C::kType == 1) {  // 64-pixel SW128 boxes: the deeper row, two skip halves
                     tma_load_3d(dst, &tm_in, bar, x0 >> 1, min(oy >> 1, a.in_h - 1), 0);
                     tma_load_3d(dst + C::kStgUp, &tm_skip, bar, x0, oy, 0);
+                    tma_load_3d(dst + C::kStgUp + C::kSkip * 128, &tm_skip, bar, x0 + 64, oy, 0);
                 } else {
                     tma_load_3d(dst, &tm_in, bar, x0, oy, 0);
+                    tma_load_3d(dst + C::kIn * 128, &tm_in, bar, x0 + 64, oy, 0);
                 }
                 if (++b == C::kStgN) {
                     b = 0;
@@ -369,22 +372,35 @@ __global__ void __launch_bounds__(CodecCfg<KIND, STG>::kThreads, 1)
                         }
                     }
                 } else {
-                    const unsigned short* src;
-                    int pitch;
-                    if (C::kType == 1 && k0 < C::kUp) {  // the deeper map, nearest, clamped
-                        src = sg + k0 * 64 + (min((x0 + row) >> 1, a.in_w - 1) - (x0 >> 1));
-                        pitch = 64;
-                    } else {  // the skip map, or the pointwise input
-                        src = sg + C::kStgUp / 2 + (k0 - (C::kType == 1 ? C::kUp : 0)) * 128 + row;
-                        pitch = 128;
-                    }
-                    if (k0 < C::kKG) {
-#pragma unroll
-                        for (int j = 0; j < 16; ++j)
-                            w[j] = (uint32_t)src[2 * j * pitch] | ((uint32_t)src[(2 * j + 1) * pitch] << 16);
-                    } else {  // K padding
+                    // dec / pointwise: 8 x 8 blocks (8 pixels x 8 channels) transposed from the
+                    // staged [channel][64 pixels] SW128 rows by ldmatrix.trans (lane 8i + k: row k of
+                    // block i = channel c0 + 8i + k; its eight channel rows sit in eight different
+                    // bank groups); they go to the A rows by stmatrix after the stage is free
+                    const uint32_t sgb = smem_u32(sg);
+                    const int bi = lane >> 3, bk = lane & 7;
+                    if (k0 >= C::kKG) {  // K padding
 #pragma unroll
                         for (int j = 0; j < 16; ++j) w[j] = 0u;
+                    } else if (C::kType == 1 && k0 < C::kUp) {
+                        // the deeper map, nearest: output pixel r reads up pixel r / 2 of the row
+                        // (x0 is even; rows past out_w are never stored, so no clamp is needed where
+                        // out_w <= 2 in_w, which the host requires of this form)
+                        const int c = k0 + 8 * bi + bk;
+#pragma unroll
+                        for (int ub = 0; ub < 2; ++ub) {
+                            const int uc = 2 * quad + ub;  // 8-pixel chunk of the deeper row
+                            ldsm_x4_trans(sgb + c * 128 + ((uc ^ (c & 7)) << 4), w[4 * ub], w[4 * ub + 1],
+                                          w[4 * ub + 2], w[4 * ub + 3]);
+                        }
+                    } else {
+                        constexpr int kC = C::kType == 1 ? C::kSkip : C::kIn;
+                        const int c = k0 - (C::kType == 1 ? C::kUp : 0) + 8 * bi + bk;
+#pragma unroll
+                        for (int pb = 0; pb < 4; ++pb) {
+                            const int r0 = 32 * quad + 8 * pb, pc = (r0 & 63) >> 3;
+                            ldsm_x4_trans(sgb + C::kStgUp + (r0 >> 6) * (kC * 128) + c * 128 + ((pc ^ (c & 7)) << 4),
+                                          w[4 * pb], w[4 * pb + 1], w[4 * pb + 2], w[4 * pb + 3]);
+                        }
                     }
                 }
                 if (!mbar_wait(&bars->empty[s], ph ^ 1, abort)) {
@@ -392,10 +408,31 @@ __global__ void __launch_bounds__(CodecCfg<KIND, STG>::kThreads, 1)
                     break;
                 }
                 unsigned char* dst = stage_a(s);
+                if constexpr (C::kType == 0) {
 #pragma unroll
-                for (int c = 0; c < 4; ++c)
-                    *reinterpret_cast<uint4*>(dst + sw128_off(row, half * 4 + c)) =
-                        make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+                    for (int c = 0; c < 4; ++c)
+                        *reinterpret_cast<uint4*>(dst + sw128_off(row, half * 4 + c)) =
+                            make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+                } else {
+                    // block i of each stmatrix -> A chunk 4 half + i of eight consecutive rows
+                    const uint32_t ab = smem_u32(dst);
+                    const int bi = lane >> 3, bk = lane & 7;
+                    if (C::kType == 1 && k0 < C::kUp && k0 < C::kKG) {
+#pragma unroll
+                        for (int ub = 0; ub < 2; ++ub)
+#pragma unroll
+                            for (int odd = 0; odd < 2; ++odd) {  // each up pixel feeds two output rows
+                                const int r = 32 * quad + 16 * ub + 2 * bk + odd;
+                                stsm_x4(ab + sw128_off(r, 4 * half + bi), w[4 * ub], w[4 * ub + 1], w[4 * ub + 2],
+                                        w[4 * ub + 3]);
+                            }
+                    } else {
+#pragma unroll
+                        for (int pb = 0; pb < 4; ++pb)
+                            stsm_x4(ab + sw128_off(32 * quad + 8 * pb + bk, 4 * half + bi), w[4 * pb], w[4 * pb + 1],
+                                    w[4 * pb + 2], w[4 * pb + 3]);
+                    }
+                }
                 fence_async_shared();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&bars->a_full[s]);
@@ -780,25 +817,28 @@ int run_codec(prism_ctx* ctx, const int32_t* q, const __half* weights, size_t we
     // TMA maps (3-D {x, y, channel}, no swizzle) need 16-byte aligned bases and row pitches: the
     // staged form's input maps, and the output map (else the epilogue stores directly)
     auto fn = encode_tiled();
-    auto map3 = [&](CUtensorMap* m, const __half* base, int64_t w, int64_t h, int c, int bw, int bh) {
+    auto map3 = [&](CUtensorMap* m, const __half* base, int64_t w, int64_t h, int c, int bw, int bh,
+                    CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_NONE) {
         if (!fn || ((uintptr_t)base & 15) || (w * 2) % 16) return false;
         cuuint64_t dims[3] = {(cuuint64_t)w, (cuuint64_t)h, (cuuint64_t)c};
         cuuint64_t strides[2] = {(cuuint64_t)w * 2, (cuuint64_t)(w * h * 2)};
         cuuint32_t box[3] = {(cuuint32_t)bw, (cuuint32_t)bh, (cuuint32_t)c};
         cuuint32_t estr[3] = {1, 1, 1};
         return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<__half*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
     };
+    constexpr CUtensorMapSwizzle kSw128 = CU_TENSOR_MAP_SWIZZLE_128B;
     CUtensorMap tin{}, tskip{}, tout{};
     bool staged = false;
     if constexpr (C::kCanStage) {
         if (C::kType == 0)
             staged = map3(&tin, a.in, in_w, in_h, C::kIn, 144, 3);
-        else if (C::kType == 1)
-            staged = map3(&tin, a.in, in_w, in_h, C::kUp, 64, 1) && map3(&tskip, a.skip, out_w, out_h, C::kSkip, 128, 1);
+        else if (C::kType == 1)  // (the staged gather reads up pixel x / 2 unclamped: out_w <= 2 in_w)
+            staged = out_w <= 2 * in_w && map3(&tin, a.in, in_w, in_h, C::kUp, 64, 1, kSw128) &&
+                     map3(&tskip, a.skip, out_w, out_h, C::kSkip, 64, 1, kSw128);
         else
-            staged = map3(&tin, a.in, in_w, in_h, C::kIn, 128, 1);
+            staged = map3(&tin, a.in, in_w, in_h, C::kIn, 64, 1, kSw128);
     }
     // output tiles: 128 pixels of one row (staged) or 128 consecutive pixels of the map
     if (staged)

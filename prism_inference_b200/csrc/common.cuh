@@ -381,6 +381,21 @@ PRISM_DEV uint64_t sdesc(uint32_t saddr, int layout) {
 PRISM_DEV uint32_t sw128_off(uint32_t row, uint32_t chunk) {
     return row * 128u + ((chunk ^ (row & 7u)) << 4);
 }
+// Four 8x8 fp16 tiles from shared memory, transposed: lanes 8i..8i+7 address the eight 16-byte
+// rows of tile i; lane t receives elements (2(t%4), t/4) and (2(t%4)+1, t/4) of each tile.
+PRISM_DEV void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr)
+                 : "memory");
+}
+// Four 8x8 fp16 tiles to shared memory: lanes 8i..8i+7 address the eight 16-byte rows of tile i;
+// lane t supplies elements (t/4, 2(t%4)) and (t/4, 2(t%4)+1) of each tile.
+PRISM_DEV void stsm_x4(uint32_t addr, uint32_t r0, uint32_t r1, uint32_t r2, uint32_t r3) {
+    asm volatile("stmatrix.sync.aligned.m8n8.x4.shared.b16 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(r0), "r"(r1),
+                 "r"(r2), "r"(r3)
+                 : "memory");
+}
 PRISM_DEV uint32_t sw64_off(uint32_t row, uint32_t chunk) {
     return row * 64u + ((chunk ^ ((row >> 1) & 3u)) << 4);
 }
