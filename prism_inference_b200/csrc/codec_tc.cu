@@ -26,7 +26,7 @@
 //   staged  (conv3x3_9ch, dec2, dec1, pointwise, when the maps' bases and row pitches are
 //           16-byte multiples) tiles of 128 pixels of one output row; the producer brings each
 //           tile's input rows into shared memory by TMA (3-D boxes {x, y, channel}; the zero fill
-//           outside the map is the padding), up to 8 tiles ahead; the gather warps build the A
+//           outside the map is the padding), 2 to 8 tiles ahead; the gather warps build the A
 //           tile from there (dec / pointwise: 64-pixel 128B-swizzled rows, transposed 8 x 8 at a
 //           time by ldmatrix.trans + stmatrix); two epilogue groups take alternate tiles (one TMEM accumulator
 //           buffer each) and stage their output tiles in shared memory for one TMA store each
@@ -42,9 +42,10 @@
 //               K-block, 16-byte stores into the swizzled A tile
 //   warps 10-13 epilogue: TMEM -> the shader's rounding / group rule -> CHW output (direct
 //   (+14-17)    stores: each warp instruction writes 32 consecutive pixels of one channel)
-// The A K-blocks pass through a ring of 8 stages (4 in the staged form and with streamed
-// weights, whose B K-blocks share the stage).  Every wait is bounded (common.cuh); on timeout
-// the CTA sets the context's error word and winds down.
+// The A K-blocks pass through a ring of 8 stages where shared memory allows (6 for dec2 and dec3,
+// beside their weights and staging tiles; 4 with streamed weights, whose B K-blocks share the
+// stage).  Every wait is bounded (common.cuh); on timeout the CTA sets the context's error word and
+// winds down.
 #include <cudaTypedefs.h>
 
 #include <mutex>
