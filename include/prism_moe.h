@@ -207,7 +207,11 @@ int prism_dense_block(prism_ctx* ctx, const prism_dense_params* p,
  * neither does this call.  The contractions run on the tensor cores with the shaders' rounding
  * points; the first call of a kind on a context allocates that kind's weight scratch (a repacked,
  * aligned copy made on the stream before each pass, so calls of one context go on one stream).
- * A bounded device wait that gives up is reported by prism_ctx_status. */
+ * Maps may sit at any element offset; conv3x3_coopvec_9ch, dec2/dec1_fused and pw_conv_coopvec_32to12
+ * run a faster form (input rows staged by TMA, output tiles written by TMA) when every map of the
+ * call starts 16-byte aligned and its row width is a multiple of 8 pixels (with out_w <= 2 in_w for
+ * the decoders), e.g. the 960x540 frame path of prism_inference_b200/codec.py; both forms give the
+ * same results.  A bounded device wait that gives up is reported by prism_ctx_status. */
 enum prism_codec_kind {
     PRISM_CODEC_ENC_IC = 0, PRISM_CODEC_ENC1 = 1, PRISM_CODEC_ENC2 = 2, PRISM_CODEC_ENC3 = 3,
     PRISM_CODEC_DEC3 = 4, PRISM_CODEC_DEC2 = 5, PRISM_CODEC_DEC1 = 6, PRISM_CODEC_OUT12 = 7,
