@@ -62,6 +62,9 @@ def parse():
     p.add_argument("--codec", action="store_true",
                    help="the encoder / decoder passes around the stack at the reference's 960x540 render size "
                         "(prism_codec_pass) instead of the stack")
+    p.add_argument("--dropin", action="store_true",
+                   help="one MoE block through the per-pass drop-ins (the reference's per-dispatch loop) "
+                        "against prism_moe_block on the same arenas")
     return p.parse_args()
 
 
@@ -732,8 +735,100 @@ def run_codec(args):
         dist.destroy_process_group()
 
 
+def run_dropin(args):
+    """One MoE block of the headline configuration (dim 256, 64 experts) on one 120x68 frame, as a
+    host keeping the reference's per-dispatch loop runs it (prism_moe_bench.cpp:416-437: attention,
+    the router, one expert dispatch per expert, through prism_attn_window / prism_router /
+    prism_expert on the reference's arenas), against prism_moe_block on the same arenas (the tcgen05
+    path).  Both as replayed CUDA graphs (device time, no host launch cost); the outputs are
+    compared.  1 GPU; not part of the driver's contract."""
+    import torch
+    from prism_inference_b200 import Prism, Stack, layout, synth
+    from prism_inference_b200.abi import AttnParams, ExpertParams, RouterParams
+    ctx = Prism(0)
+    L = layout.build_stack(256, 1, n_experts=64)
+    T, D, E = L.tokens, 256, 64
+    b = L.blocks[0]
+    blob = synth.make_blob(L)
+    x = synth.make_frames(L, 1)[0]
+    w = torch.from_numpy(blob.view(np.int16)).cuda().view(torch.float16)
+    feat = torch.zeros(3 * T * D, dtype=torch.float16, device="cuda")
+    feat[:T * D] = torch.from_numpy(x.reshape(-1).view(np.int16)).cuda().view(torch.float16)
+    aux = torch.zeros(T + E, dtype=torch.int32, device="cuda")
+    pa = AttnParams(T, D, 8, 32, L.spatial_w, L.spatial_h, 8, b.qkv_w, b.qkv_b, b.out_w, b.out_b, 0, T * D)
+    pr = RouterParams(T, D, E, b.router_w, b.router_b, T * D, 0, T)
+    pe = [ExpertParams(T, D, e, b.expert_w1 + e * b.expert_stride, b.expert_b1 + e * b.expert_stride,
+                       b.expert_w2 + e * b.expert_stride, b.expert_b2 + e * b.expert_stride, T * D, 2 * T * D, 0)
+          for e in range(E)]
+    blk = Stack(ctx, L, blob, 1)
+    fast_out = torch.zeros(T * D, dtype=torch.float16, device="cuda")
+    fast_aux = torch.zeros(T + E, dtype=torch.int32, device="cuda")
+
+    def dropin():
+        ctx.attn_window(pa, w, feat)
+        ctx.router(pr, w, feat, aux)
+        for p_ in pe:
+            ctx.expert(p_, w, feat, aux)
+
+    def dropin_static():  # the experts as one allocation-free call (prism_expert_all_static)
+        ctx.attn_window(pa, w, feat)
+        ctx.router(pr, w, feat, aux)
+        ctx.expert_all_static(pe[0], E, b.expert_stride, w, feat, aux)
+
+    def fast():
+        blk.moe_block(feat[:T * D].view(1, T, D), fast_out.view(1, T, D), fast_aux[:T], fast_aux[T:])
+
+    def timed(fn):
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                fn()
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        for _ in range(max(args.warmup, 3)):
+            g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        del g
+        return e0.elapsed_time(e1) / args.steps
+
+    ms_static = timed(dropin_static)
+    ms_dropin = timed(dropin)
+    ms_fast = timed(fast)
+    ctx.status()
+    blk.status()
+    a = feat[2 * T * D:].float()
+    f = fast_out.float()
+    diff = (a - f).abs().max().item()
+    rel = ((a - f).norm() / f.norm()).item()
+    same_route = float((aux[:T] == fast_aux[:T]).float().mean().item())
+    print(json.dumps({"metric": "one MoE block (dim 256, 64 experts) on one 120x68 frame: per-pass drop-ins vs "
+                                "prism_moe_block", "unit": "ms",
+                      "dropin_ms": ms_dropin, "dropin_launches": 2 + E, "dropin_static_experts_ms": ms_static,
+                      "moe_block_ms": ms_fast,
+                      "speedup": ms_dropin / ms_fast, "max_abs_diff": diff, "rel_l2_diff": rel,
+                      "routing_agreement": same_route, "steps": args.steps, "data": "synthetic"}))
+    blk.close()
+    ctx.close()
+
+
 def main():
     args = parse()
+    if args.dropin:
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "--dropin measures this library only"}))
+            return
+        run_dropin(args)
+        return
     if args.codec:
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "unavailable": "--codec measures this library only"}))
