@@ -6,8 +6,10 @@
 // coopVecMatMulAddNV is an fp32 dot product summed in k order with separately
 // rounded multiplies and adds, plus the bias, rounded once to fp16.  They read the
 // blob at any 2-byte alignment (the reference layout puts experts on 8-byte
-// boundaries).  The batched fast path (stack.cu, tc_kernels.cu) uses tcgen05
-// tensor-core tiles instead.
+// boundaries).  The batched fast path (stack.cu with attn_tc.cu, expert_tc.cu, tc_ffn.cu) uses
+// tcgen05 tensor-core tiles instead.
+#include <algorithm>
+
 #include "common.cuh"
 #include "cta_mv.cuh"
 #include "pass_kernels.cuh"
@@ -126,40 +128,66 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
     }
 }
 
-// ---- expert FFN with skip: moe_expert_skip.comp.glsl:25-54.  One CTA per 32
-// tokens; only tokens routed to expert_id are computed and written.
+// ---- expert FFN with skip: moe_expert_skip.comp.glsl:25-54 (one dispatch per expert; tokens of
+// other experts return early, :30).  Every CTA scans the assignments and ranks this expert's
+// tokens in token order (warp ballots, a running count per 256-token chunk); CTA b computes tiles
+// b, b + gridDim.x, ... of kExpertTile of them.  A dispatch thus reads the expert's weights once per
+// kExpertTile of its tokens, not once per window of the arena, and spreads an expert's ~T/E tokens
+// over T/E/kExpertTile SMs; the arithmetic of every token is that of the shader (cta_mv rows are
+// independent), so the outputs do not depend on the tiling.
+constexpr int kExpertTile = 8;
 template <int D>
-__global__ void __launch_bounds__(256) expert_kernel(ExpertArgs a) {
+__global__ void __launch_bounds__(256) expert_kernel(ExpertArgs a, int tiles_per_cta) {
+    constexpr int TT = kExpertTile;
     extern __shared__ __align__(16) unsigned char smem[];
-    float* Xs = reinterpret_cast<float*>(smem);  // [32][D]
-    float* Hs = Xs + 32 * D;                     // [32][D]
-    float* Rs = Hs + 32 * D;                     // [32][D]
-    __shared__ int tok[32];
-    __shared__ int ntok;
-    const int t0 = blockIdx.x * 32;
-    if (threadIdx.x == 0) {
-        int n = 0;
-        for (int t = t0; t < min(t0 + 32, a.n_tokens); ++t)
-            if (a.assign[t] == a.expert_id) tok[n++] = t;  // :30
-        ntok = n;
+    float* Xs = reinterpret_cast<float*>(smem);            // [TT][D]
+    float* Hs = Xs + TT * D;                               // [TT][D]
+    float* Rs = Hs + TT * D;                               // [TT][D]
+    int* list = reinterpret_cast<int*>(Rs + TT * D);       // [tiles_per_cta][TT]: this CTA's tokens
+    __shared__ int wcount[8];
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    const int G = gridDim.x;
+    int n = 0;  // the expert's tokens before the current chunk (the same in every thread)
+    for (int t0 = 0; t0 < a.n_tokens; t0 += 256) {
+        const int t = t0 + tid;
+        const bool mine = t < a.n_tokens && a.assign[t] == a.expert_id;  // :30
+        const unsigned bal = __ballot_sync(0xffffffffu, mine);
+        if (lane == 0) wcount[w] = __popc(bal);
+        __syncthreads();
+        int before = n, in_chunk = 0;
+#pragma unroll
+        for (int v = 0; v < 8; ++v) {
+            before += v < w ? wcount[v] : 0;
+            in_chunk += wcount[v];
+        }
+        if (mine) {
+            const int r = before + __popc(bal & ((1u << lane) - 1u));
+            const int tile = r / TT;
+            if (tile % G == (int)blockIdx.x && tile / G < tiles_per_cta) list[(tile / G) * TT + r % TT] = t;
+        }
+        n += in_chunk;
+        __syncthreads();  // wcount is rewritten by the next chunk; list is complete after the loop
     }
-    __syncthreads();
-    const int nt = ntok;
-    if (nt == 0) return;
-    for (int i = threadIdx.x; i < 32 * D; i += blockDim.x) {
-        const int t = i / D;
-        Xs[i] = t < nt ? __half2float(a.x[(size_t)tok[t] * D + (i % D)]) : 0.0f;
-    }
-    __syncthreads();
-    cta_mv<32>(a.weights + a.w1, D, a.weights + a.b1, D, D, Xs, D, Hs, D);
-    __syncthreads();
-    for (int i = threadIdx.x; i < 32 * D; i += blockDim.x) Hs[i] = rh(gelu_exact(Hs[i]));
-    __syncthreads();
-    cta_mv<32>(a.weights + a.w2, D, a.weights + a.b2, D, D, Hs, D, Rs, D);
-    __syncthreads();
-    for (int i = threadIdx.x; i < nt * D; i += blockDim.x) {
-        const int t = i / D, c = i % D;
-        a.y[(size_t)tok[t] * D + c] = __float2half_rn(__fadd_rn(Rs[i], Xs[i]));  // :52
+    for (int k = 0; (int)blockIdx.x + k * G < (n + TT - 1) / TT && k < tiles_per_cta; ++k) {
+        const int tile = blockIdx.x + k * G;
+        const int nt = min(TT, n - tile * TT);
+        const int* tok = list + k * TT;
+        for (int i = tid; i < TT * D; i += blockDim.x) {
+            const int t = i / D;
+            Xs[i] = t < nt ? __half2float(a.x[(size_t)tok[t] * D + (i % D)]) : 0.0f;
+        }
+        __syncthreads();
+        cta_mv<TT>(a.weights + a.w1, D, a.weights + a.b1, D, D, Xs, D, Hs, D);
+        __syncthreads();
+        for (int i = tid; i < TT * D; i += blockDim.x) Hs[i] = rh(gelu_exact(Hs[i]));
+        __syncthreads();
+        cta_mv<TT>(a.weights + a.w2, D, a.weights + a.b2, D, D, Hs, D, Rs, D);
+        __syncthreads();
+        for (int i = tid; i < nt * D; i += blockDim.x) {
+            const int t = i / D, c = i % D;
+            a.y[(size_t)tok[t] * D + c] = __float2half_rn(__fadd_rn(Rs[i], Xs[i]));  // :52
+        }
+        __syncthreads();  // Xs / Rs are rewritten by the next tile
     }
 }
 
@@ -264,17 +292,21 @@ cudaError_t launch_router(const RouterArgs& a, int dim, cudaStream_t s) {
 }
 
 cudaError_t launch_expert(const ExpertArgs& a, int dim, cudaStream_t s) {
-    const int grid = (a.n_tokens + 31) / 32;
-    const size_t sm = (size_t)3 * 32 * dim * 4;
-    if (grid == 0) return cudaSuccess;
+    // tiles if every token went to this expert; one CTA per SM-ish, more when a CTA's token list
+    // (tiles_per_cta x kExpertTile ints beside the three [kExpertTile][dim] fp32 tiles) would not fit
+    const int tiles = (a.n_tokens + kExpertTile - 1) / kExpertTile;
+    if (tiles == 0) return cudaSuccess;
+    const int grid = std::max(std::min(tiles, 148), (tiles + 4095) / 4096);
+    const int tiles_per_cta = (tiles + grid - 1) / grid;
+    const size_t sm = (size_t)3 * kExpertTile * dim * 4 + (size_t)tiles_per_cta * kExpertTile * 4;
     if (dim == 256) {
         cudaError_t e = set_smem(expert_kernel<256>, sm);
         if (e != cudaSuccess) return e;
-        expert_kernel<256><<<grid, 256, sm, s>>>(a);
+        expert_kernel<256><<<grid, 256, sm, s>>>(a, tiles_per_cta);
     } else {
         cudaError_t e = set_smem(expert_kernel<128>, sm);
         if (e != cudaSuccess) return e;
-        expert_kernel<128><<<grid, 256, sm, s>>>(a);
+        expert_kernel<128><<<grid, 256, sm, s>>>(a, tiles_per_cta);
     }
     return cudaGetLastError();
 }
