@@ -133,8 +133,9 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
 // tokens in token order (warp ballots, a running count per 256-token chunk); CTA b computes tiles
 // b, b + gridDim.x, ... of kExpertTile of them.  A dispatch thus reads the expert's weights once per
 // kExpertTile of its tokens, not once per window of the arena, and spreads an expert's ~T/E tokens
-// over T/E/kExpertTile SMs (a dispatch is a latency: 4-token tiles measured faster than 8); the arithmetic of every token is that of the shader (cta_mv rows are
-// independent), so the outputs do not depend on the tiling.
+// over T/E/kExpertTile SMs (a dispatch is a latency: 4-token tiles measured faster than 8); the
+// arithmetic of every token is that of the shader (cta_mv rows are independent), so the outputs do
+// not depend on the tiling.
 constexpr int kExpertTile = 4;
 template <int D>
 __global__ void __launch_bounds__(256) expert_kernel(ExpertArgs a, int tiles_per_cta) {
