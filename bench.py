@@ -26,6 +26,12 @@ against the sustained cuBLAS bf16 figure of MEASURED_PEAKS.json.
 its GLSL shader sources compiled as C++ (oracle/_ref, see oracle/glsl_ref), dispatched
 in the order of prism_moe_bench.cpp:408-444 with all host threads.  The reference
 Vulkan path cannot run on this box (no Vulkan driver, Win32 host code).
+
+Other measurements (not the driver's line):
+    python bench.py --codec    the nine encoder / decoder passes at 960x540 (prism_codec_pass),
+                               frames/s, e2e through page-locked host memory
+    python bench.py --dropin   one MoE block through the per-pass drop-ins (the reference's
+                               per-dispatch loop) against prism_moe_block on the same arenas
 """
 from __future__ import annotations
 
