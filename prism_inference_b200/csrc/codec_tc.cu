@@ -112,8 +112,9 @@ struct CodecCfg {
     // (dec3's staging buffers would not fit beside its 64 KB of weights and output staging)
     static constexpr bool kCanStage = KIND == C_ENC_IC || KIND == C_DEC2 || KIND == C_DEC1 || KIND == C_OUT12;
     // staged input of one tile: conv3x3_9ch rows y-1..y+1 of all channels, x from x0 - 8 (the
-    // TMA start is 16-byte aligned) over 144 pixels; dec: one row of the deeper map (64 pixels
-    // from x0 / 2) and of the skip map (128 pixels); pointwise: one row of 128 pixels
+    // TMA start is 16-byte aligned) over 144 pixels, no swizzle; dec: one row of the deeper map
+    // (64 pixels from x0 / 2) and of the skip map (two 64-pixel boxes); pointwise: one row (two
+    // 64-pixel boxes); the dec / pointwise boxes are 128B-swizzled [channel][64 pixels] tiles
     static constexpr int kStgUp = kType == 1 ? kUp * 64 * 2 : 0;
     static constexpr int kStgBytes = !STG ? 0 : kType == 0 ? kIn * 3 * 144 * 2 : kType == 1 ? kStgUp + kSkip * 128 * 2
                                                                                               : kIn * 128 * 2;
