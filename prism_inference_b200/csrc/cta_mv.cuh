@@ -23,6 +23,9 @@ __device__ void cta_mv(const __half* __restrict__ W, int ldw, const __half* __re
         for (int t = 0; t < TT; ++t) acc[t] = 0.0f;
         const __half* wr = W + (size_t)r * ldw;
         if (vec8) {
+            // (four loads in flight: each thread streams its own row, so a lone load per iteration
+            // waits the whole L2 latency)
+#pragma unroll 4
             for (int k = 0; k < K; k += 8) {
                 const uint4 w8 = __ldg(reinterpret_cast<const uint4*>(wr + k));
                 const float wv[8] = {lo_h2f(w8.x), hi_h2f(w8.x), lo_h2f(w8.y), hi_h2f(w8.y),
@@ -34,6 +37,7 @@ __device__ void cta_mv(const __half* __restrict__ W, int ldw, const __half* __re
                         acc[t] = __fadd_rn(acc[t], __fmul_rn(wv[j], (float)Xs[t * ldx + k + j]));
             }
         } else if (vec) {
+#pragma unroll 4
             for (int k = 0; k < K; k += 4) {
                 const uint2 w4 = __ldg(reinterpret_cast<const uint2*>(wr + k));
                 const float wv[4] = {lo_h2f(w4.x), hi_h2f(w4.x), lo_h2f(w4.y), hi_h2f(w4.y)};
