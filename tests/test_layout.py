@@ -115,3 +115,23 @@ def test_export_custom_names_and_missing_tensors(tmp_path):
     del ck["blocks.0.moe.router.bias"]
     with pytest.raises(KeyError, match="router.bias"):
         export.export(L, ck, str(tmp_path / "b.weights"), names={"blk0.out": "encoder.layer0.mha.out_proj"})
+
+
+def test_reference_frame_layout_allows_the_staged_codec_passes():
+    """The 960x540 frame path laid out with an aligned arena (as bench.py --codec does) meets what
+    prism_codec_pass needs for its TMA-staged form (conv3x3_9ch, dec2, dec1, pointwise): every map
+    starts 16-byte aligned and every level's row is a multiple of 8 pixels (16 bytes of fp16), and
+    each decoder's output is at most twice its deeper map's width."""
+    from prism_inference_b200 import codec
+    fc = codec.frame_chain(960, 540)
+    for name, off in fc.feat_off.items():
+        assert (off * 2) % 16 == 0, f"map {name} at element {off} is not 16-byte aligned"
+    for w, h in fc.levels:
+        assert (w * 2) % 16 == 0, f"row of {w} pixels is not a multiple of 16 bytes"
+    for shader, push, _ in fc.passes:
+        if shader.startswith("dec"):
+            out_w, in_w = push[0], push[2]
+            assert out_w <= 2 * in_w, shader
+    # an odd arena offset (the other tests' unaligned layout) takes the plain form instead
+    odd = codec.frame_chain(960, 540, feat_pad=1)
+    assert any((off * 2) % 16 for off in odd.feat_off.values())
